@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""bench.py — QRAF's quantized matvec on B200 (BASELINE.json metric: "Q8/Q4 matvec HBM GB/s").
+
+Default workload: BASELINE.json configs[1], the Q4_0 4096x4096 batch-1 matvec.
+Weight W ~ N(0, 0.02) from std::mt19937(42) (the reference's seeding idiom),
+quantized on the GPU by the byte-exact Q4_0 quantizer; activation x ~ N(0, 1)
+from std::mt19937(43).
+
+A STEP is one pass over a pool of R distinct copies of the quantized weight
+(R = ceil(4 x L2 / weight bytes)), one matvec launch per copy: every launch
+reads its weight cold from HBM (inputs larger than L2, so no flush is needed).
+The step is captured once as a CUDA graph and replayed.  value = algorithmic
+bytes (N*K/32*block_bytes + 4K + 4N per matvec) of every launch of every rank
+/ max-over-ranks device time of the K timed steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>]] [--mode fast|exact]
+
+With --gpus N > 1 (launched by torch.distributed.run) every rank runs the same
+workload on its own weights (independent matvec objects, no data-path
+collective): "scaling": "weak".  --impl reference times the reference's own
+CPU code (oracle/_ref: dispatch_matvec_q's per-row dot, fanned out over all host
+threads) on the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+Q8, Q4 = 10, 20
+BLOCK_BYTES = {Q8: 36, Q4: 18}
+METRIC = "Q8/Q4 matvec HBM GB/s"
+
+
+def parse_workload(name: str):
+    """'q4_4096x4096' -> (dtype, N, K, M); an optional '_m<M>' suffix sets the batch."""
+    parts = name.split("_")
+    dt = {"q4": Q4, "q8": Q8}[parts[0]]
+    n, k = (int(v) for v in parts[1].split("x"))
+    m = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("m") else 1
+    return dt, n, k, m
+
+
+def alg_bytes(dt, n, k, m):
+    return n * (k // 32) * BLOCK_BYTES[dt] + 4 * m * k + 4 * m * n
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback (6.65 TB/s, profiling recipe)"
+
+
+def profiled_traffic(dt):
+    """DRAM bytes per launch from the committed ncu summary of the same kernel, if present."""
+    name = "matvec_stream_q4_4096x4096.md" if dt == Q4 else "matvec_stream_q8_4096x4096.md"
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ── clocks during the timed region (NVML, what nvidia-smi reads) ───────────
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle", 0x10: "sync_boost"}
+
+    def __init__(self, torch_device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons = [], set()
+        self.ok = False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            import torch
+
+            props = torch.cuda.get_device_properties(torch_device_index)
+            h = None
+            uuid = getattr(props, "uuid", None)
+            if uuid is not None:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(uuid)).encode())
+                except Exception:
+                    h = None
+            if h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[torch_device_index]) if vis and vis.split(",")[0].isdigit() else torch_device_index
+                h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.nvml, self.h = pynvml, h
+            self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report that instead of clocks
+            self.err = str(e)
+
+    def _reasons_now(self):
+        fn = getattr(self.nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            self.nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(fn(self.h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                bits = self._reasons_now()
+                for b, name in self.REASONS.items():
+                    if bits & b and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable: " + self.err}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.sm_max,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ── the reference's CPU path ──────────────────────────────────────────────
+def cpu_reference(dt, n, k, m, q_host, x_host, threads, budget_s, max_ops=None):
+    """Time the reference's own dispatch_matvec_q code (oracle/_ref) on host cores."""
+    import oracle
+
+    if oracle.reference_available():
+        ref, kind = oracle.Reference(), "reference"
+
+        def op():
+            for j in range(m):
+                ref.matvec(dt, q_host, n, k, x_host[j], 32, threads=threads)
+    else:   # the C restatement, rows fanned out over threads (ctypes releases the GIL)
+        from concurrent.futures import ThreadPoolExecutor
+
+        orc, kind = oracle.Oracle(), "port"
+        rb = q_host.size // n
+        pool = ThreadPoolExecutor(max(1, threads))
+        bounds = [(n * t // threads, n * (t + 1) // threads) for t in range(threads)]
+
+        def op():
+            for j in range(m):
+                list(pool.map(lambda b: orc.matvec(dt, q_host[b[0] * rb:b[1] * rb], b[1] - b[0], k, x_host[j]),
+                              bounds))
+    op()   # warm
+    t0 = time.perf_counter()
+    ops = 0
+    while True:
+        op()
+        ops += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_ops is not None and ops >= max_ops):
+            break
+    return ops, el, kind
+
+
+def run_reference_arm(args, dt, n, k, m):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import qraf_b200 as qb
+
+    w = qb.fill_normal(42, 0.0, 0.02, n * k).reshape(n, k)
+    import oracle
+
+    q_host = (oracle.Reference() if oracle.reference_available() else oracle.Oracle()).quantize(dt, w.ravel(), 32)
+    x_host = qb.fill_normal(43, 0.0, 1.0, m * k).reshape(m, k)
+    threads = os.cpu_count() or 1
+    # Each step is one full matvec of the workload; warm-up is bounded to keep the run short.
+    for _ in range(min(args.warmup, 3)):
+        cpu_reference(dt, n, k, m, q_host, x_host, threads, 0.0, max_ops=1)
+    ops, el, kind = cpu_reference(dt, n, k, m, q_host, x_host, threads, budget_s=1e9, max_ops=args.steps)
+    gbs = ops * alg_bytes(dt, n, k, m) / el / 1e9
+    sample = (f"{ops} full {n}x{k} {'Q4_0' if dt == Q4 else 'Q8_0'} matvecs (M={m}) through the reference's "
+              f"dot_{'q4' if dt == Q4 else 'q8'}_0_f32, rows split over {threads} threads "
+              f"(the reference's own row fan-out, backend.cpp:145-151)")
+    line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": ops, "warmup": args.warmup, "ms_per_step": el / ops * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "N": n, "K": k, "M": m},
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ── our arm ───────────────────────────────────────────────────────────────
+def run_ours(args, dt, n, k, m):
+    import torch
+
+    import qraf_b200 as qb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    qb.init(local)
+    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+
+    # Seeded weight, quantized on the GPU (byte-exact with the reference quantizer).
+    wf = torch.from_numpy(qb.fill_normal(42, 0.0, 0.02, n * k)).to(dev).reshape(n, k)
+    q = qb.quantize_rows(dt, wf, 32).reshape(-1)
+    del wf
+    wbytes = q.numel()
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    free, _ = torch.cuda.mem_get_info(dev)
+    R = max(2, math.ceil(4 * l2 / wbytes))
+    R = max(2, min(R, int(0.5 * free // wbytes)))
+    pool = torch.empty((R, wbytes), dtype=torch.uint8, device=dev)
+    pool[:] = q
+    weights = [qb.Weight.from_device(pool[r], dt, n, k) for r in range(R)]
+    x = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * k)).to(dev).reshape(m, k)
+    y = torch.empty((R, m, n), dtype=torch.float32, device=dev)
+
+    payload_ok = None
+    dg = os.path.join(ROOT, "tests", "golden", "config_digests.json")
+    if os.path.exists(dg) and (n, k) == (4096, 4096):
+        import hashlib
+
+        key = "cfg2_q4_4096x4096" if dt == Q4 else "cfg1_q8_4096x4096"
+        want = json.load(open(dg))[key]["sha_q"]
+        payload_ok = hashlib.sha256(q.cpu().numpy().tobytes()).hexdigest() == want
+
+    # One step = one launch per weight copy, with per-launch timing events, as a CUDA graph.
+    s = torch.cuda.Stream(dev)
+    ev_s = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(R)]
+    ev_e = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(R)]
+    with torch.cuda.stream(s):
+        for r in range(R):
+            qb.matvec_q(weights[r], x, y[r], mode=mode)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for r in range(R):
+            ev_s[r].record()
+            qb.matvec_q(weights[r], x, y[r], mode=mode)
+            ev_e[r].record()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    with torch.cuda.stream(s):
+        t0.record()
+        for _ in range(args.steps):
+            g.replay()
+        t1.record()
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    if dist:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    kern_ms = statistics.mean(ev_s[r].elapsed_time(ev_e[r]) for r in range(R))
+    if dist:
+        t = torch.tensor([elapsed_ms, kern_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    per_launch = alg_bytes(dt, n, k, m)
+    value = world * args.steps * R * per_launch / (elapsed_ms / 1e3) / 1e9
+    peak, peak_src = measured_peaks()
+    achieved = per_launch / (kern_ms / 1e3) / 1e9
+    status = qb.device_status()
+
+    # e2e: the reference-facing host entry (host x in, host y out, synchronous), same pool.
+    q_host = q.cpu().numpy()
+    host_copies = [q_host.copy() for _ in range(R)]
+    x_host = x.cpu().numpy()
+    y_host = np.empty((m, n), dtype=np.float32)
+    for r in range(R):   # first call per copy uploads it into the device weight cache
+        qb.dispatch_matvec_q(host_copies[r], wbytes, dt, 32, n, k, x_host, y_host, m=m, mode=mode)
+    e2e_steps = max(3, min(args.steps, 100))
+    if dist:
+        dist.barrier()
+    te = time.perf_counter()
+    for _ in range(e2e_steps):
+        for r in range(R):
+            qb.dispatch_matvec_q(host_copies[r], wbytes, dt, 32, n, k, x_host, y_host, m=m, mode=mode)
+    e2e_s = time.perf_counter() - te
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t[0])
+    e2e = {"value": world * e2e_steps * R * per_launch / e2e_s / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": R * m * k * 4, "d2h_bytes_per_step": R * m * n * 4, "steps": e2e_steps,
+           "path": "qraf_cuda_matvec_q_host (drop-in body of qraf::dispatch_matvec_q): pinned staging, H2D x, "
+                   "kernel, D2H y, stream sync per call; weights cached on the device after their first call"}
+    qb.host_cache_clear()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        ops, el, kind = cpu_reference(dt, n, k, m, q_host, x_host.reshape(m, k), 1, budget_s=args.cpu_seconds)
+        cpu = {"value": ops * per_launch / el / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+               "sample": f"{ops} full {n}x{k} matvecs (M={m}) through dispatch_matvec_q's scalar Linux path "
+                         f"(single-threaded, as the reference runs it), {el:.1f} s of {os.cpu_count()} host threads' "
+                         f"worth of cores used: 1"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "N": n, "K": k, "M": m, "block": 32,
+                       "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode,
+                       "parallelism": f"independent weights per rank x{world}" if world > 1 else "single GPU",
+                       "pool_copies": R, "pool_bytes": R * wbytes, "l2_bytes": l2,
+                       "l2_policy": "inputs larger than L2: rotating pool of weight copies >= 4x L2",
+                       "step": f"{R} matvec launches, one per L2-cold weight copy (CUDA graph replay)",
+                       "weights": "N(0,0.02) std::mt19937(42), quantized on GPU (byte-exact Q*_0)",
+                       "payload_sha_matches_reference": payload_ok, "arith": "fp32 accumulate"},
+            "e2e": e2e,
+            "gpu_launches": args.steps * R,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profiled_traffic(dt), "peak_source": peak_src,
+                         "kernel": "qmv_stream_kernel", "kernel_us": kern_ms * 1e3,
+                         "alg_bytes_per_launch": per_launch},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="q4_4096x4096")
+    ap.add_argument("--mode", choices=["fast", "exact"], default="fast")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    dt, n, k, m = parse_workload(args.workload)
+    if args.impl == "reference":
+        run_reference_arm(args, dt, n, k, m)
+    else:
+        run_ours(args, dt, n, k, m)
+
+
+if __name__ == "__main__":
+    main()

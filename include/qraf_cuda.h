@@ -1,0 +1,147 @@
+/*
+ * qraf_cuda.h — C ABI of the B200 quantized matvec library (libqraf_cuda.so).
+ *
+ * The library replaces the body of one seam of QRAF (simonpierreboucher02/qraf):
+ * the block-quantized Q8_0 / Q4_0 weight x fp32 activation matvec behind
+ * `qraf::dispatch_matvec_q` (src/nn/backend.cpp:131-199, declared at
+ * include/nn/backend.h:31-34) and its per-row primitives `dot_q8_0_f32` /
+ * `dot_q4_0_f32` (src/tensor/quantize.cpp:187-239, include/tensor/quantize.h:60-61).
+ * The on-device weight layout is the reference's native block layout, byte for
+ * byte (include/tensor/quantize.h:11-31):
+ *
+ *   Q8_0 block: [f32 scale][block_size x int8]                 4 + bs bytes
+ *   Q4_0 block: [f16 scale][block_size/2 x u8, element 2i in
+ *               the low nibble, 2i+1 in the high, +8 bias]      2 + bs/2 bytes
+ *   weight:     rows x ceil(cols / bs) blocks, rows back to back.
+ *
+ * Conventions: every function returns a status (QRAF_OK = 0).  Pointers named
+ * `*_dev` are device memory of the current device; `*_host` are host memory.
+ * `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ * stream).  Device entry points are asynchronous on `stream`; host entry points
+ * are synchronous.  On error, qraf_cuda_last_error() returns a message for the
+ * calling thread.
+ */
+#ifndef QRAF_CUDA_H
+#define QRAF_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status codes ───────────────────────────────────────────────────────── */
+#define QRAF_OK              0
+#define QRAF_ERR_INVALID     1   /* an argument is out of range or inconsistent */
+#define QRAF_ERR_UNSUPPORTED 2   /* unknown dtype, or a mode this shape has no kernel for */
+#define QRAF_ERR_CUDA        3   /* a CUDA runtime call failed */
+#define QRAF_ERR_TIMEOUT     4   /* a bounded device-side wait expired (see qraf_cuda_device_status) */
+#define QRAF_ERR_COMM        5   /* a collective / peer-exchange step failed */
+#define QRAF_ERR_NOMEM       6   /* device or pinned-host allocation failed */
+
+/* ── weight dtypes: the reference's DType values (include/core/types.h:27-39) */
+#define QRAF_DTYPE_Q8_0 10u
+#define QRAF_DTYPE_Q4_0 20u
+
+/* ── arithmetic modes ───────────────────────────────────────────────────── */
+#define QRAF_MODE_EXACT 0  /* bit-identical to the reference's Linux scalar path */
+#define QRAF_MODE_FAST  1  /* fused multiply-add, reordered sums; allclose(rtol 1e-5, atol 1e-6) */
+#define QRAF_MODE_TC    2  /* tensor-core tile for M >= 16; same tolerance as FAST */
+#define QRAF_MODE_AUTO  3  /* FAST below M = 16, TC from M = 16 */
+
+/* A quantized weight on one device: a plain descriptor, no hidden state. */
+typedef struct qraf_weight {
+    const void* data;     /* device pointer to rows * row_bytes bytes */
+    uint64_t bytes;       /* rows * row_bytes */
+    uint64_t row_bytes;   /* ceil(cols / block_size) * block bytes */
+    uint32_t dtype;       /* QRAF_DTYPE_Q8_0 or QRAF_DTYPE_Q4_0 */
+    uint32_t block_size;  /* elements per block (QuantScheme::block_size, format.h:91) */
+    uint32_t rows;        /* N = out_dim */
+    uint32_t cols;        /* K = in_dim */
+    int32_t device;       /* CUDA device that holds `data` */
+    uint32_t owned;       /* 1 when the library allocated `data` (qraf_cuda_weight_upload) */
+} qraf_weight_t;
+
+/* ── library ────────────────────────────────────────────────────────────── */
+const char* qraf_cuda_version(void);
+/* Select `device` for the calling thread and prepare the kernels on it. */
+int qraf_cuda_init(int device);
+/* Free the host-pointer weight cache and staging buffers of every device. */
+int qraf_cuda_shutdown(void);
+/* Copy the calling thread's last error message into buf (always NUL-terminated). */
+int qraf_cuda_last_error(char* buf, size_t len);
+/* Synchronise the current device and return QRAF_ERR_TIMEOUT if a kernel
+ * reported an expired wait since the last clear; `clear` resets the word. */
+int qraf_cuda_device_status(int clear);
+
+/* Bytes of one row: ceil(cols / block_size) blocks (backend.cpp:138-139,167-168).
+ * 0 for an unknown dtype or block_size 0. */
+uint64_t qraf_row_bytes(uint32_t dtype, uint32_t block_size, uint32_t cols);
+
+/* ── weights ────────────────────────────────────────────────────────────── */
+/* Describe native blocks already on the device (nothing is copied). */
+int qraf_cuda_weight_wrap(const void* data_dev, uint64_t bytes, uint32_t dtype, uint32_t block_size,
+                          uint32_t rows, uint32_t cols, qraf_weight_t* out);
+/* Copy native blocks from host memory to a new device allocation. */
+int qraf_cuda_weight_upload(const void* data_host, uint64_t bytes, uint32_t dtype, uint32_t block_size,
+                            uint32_t rows, uint32_t cols, qraf_weight_t* out);
+/* Free a weight made by qraf_cuda_weight_upload (no-op for wrapped weights). */
+int qraf_cuda_weight_free(qraf_weight_t* w);
+/* Rows [rank*rows/world, (rank+1)*rows/world) of `full` as a view (no copy).
+ * Row sharding keeps each row's bytes intact, so every shard is a valid weight. */
+int qraf_cuda_weight_shard(const qraf_weight_t* full, uint32_t world, uint32_t rank, qraf_weight_t* out);
+
+/* ── the hot path ───────────────────────────────────────────────────────── */
+/* Y[m][n] = dispatch_matvec_q(W, X[m])[n] for m < M (backend.cpp:131-199 per
+ * vector; the reference's batching is M independent batch-1 forwards,
+ * include/runtime/batch_scheduler.h:187-228).  x_dev is [M][cols] fp32,
+ * y_dev is [M][rows] fp32. */
+int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int mode,
+                       void* stream);
+
+/* One quantized row dotted with x (dot_q8_0_f32 / dot_q4_0_f32,
+ * quantize.cpp:187-239); *out_dev receives the fp32 result. */
+int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint64_t count, uint32_t block_size,
+                    float* out_dev, int mode, void* stream);
+
+/* Per-block partial products p[n][b] = fl(block_sum * scale) exactly as the
+ * reference forms them before `total += ...` (quantize.cpp:201-205, 226-234).
+ * partials_dev is [rows][ceil(cols / block_size)].  For bit-exact checking. */
+int qraf_cuda_block_partials(const qraf_weight_t* w, const float* x_dev, float* partials_dev, void* stream);
+
+/* ── quantizer (byte-exact with the reference) ──────────────────────────── */
+/* quantize_q8_0 / quantize_q4_0 over `count` contiguous values
+ * (quantize.cpp:105-183); out_dev receives qraf_row_bytes(dtype, bs, count) bytes. */
+int qraf_cuda_quantize(uint32_t dtype, const float* x_dev, uint64_t count, uint32_t block_size, void* out_dev,
+                       void* stream);
+/* The same applied to each of `rows` rows of `cols` values (the layout a
+ * weight has when each output row is quantized on its own). */
+int qraf_cuda_quantize_rows(uint32_t dtype, const float* x_dev, uint32_t rows, uint32_t cols, uint32_t block_size,
+                            void* out_dev, void* stream);
+/* dequantize_tensor for Q8_0 / Q4_0 (quantize.cpp:55-101). */
+int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint32_t block_size, float* out_dev,
+                         void* stream);
+
+/* ── host-pointer entry: the drop-in body of qraf::dispatch_matvec_q ────── */
+/* Same arguments as the reference's dispatch_matvec_q (backend.h:31-34) plus M
+ * and mode.  The first call with a given (w_host, w_size, dtype, bs, rows,
+ * cols) uploads the weight to the current device and caches it (weights are
+ * immutable model data, mmap'd read-only by the reference, loader.cpp:80);
+ * each call copies x in, runs the kernel and copies y out before returning.
+ * Thread-safe; calls on one device are serialised. */
+int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype, uint32_t block_size,
+                            uint32_t out_dim, uint32_t in_dim, const float* x_host, float* y_host, uint32_t M,
+                            int mode);
+/* Drop every cached device copy made by qraf_cuda_matvec_q_host. */
+int qraf_cuda_host_cache_clear(void);
+
+/* ── host utility ───────────────────────────────────────────────────────── */
+/* Seeded synthetic data with the reference's idiom: std::mt19937(seed) and
+ * std::normal_distribution<float>(mean, stddev) (tools/dummy_model.cpp:12-16). */
+void qraf_fill_normal(uint32_t seed, float mean, float stddev, float* out_host, uint64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QRAF_CUDA_H */

@@ -1,0 +1,224 @@
+"""ctypes bindings for the parity checkers (TEST INFRASTRUCTURE ONLY).
+
+Two libraries live here, both CPU-only:
+
+* ``libqraf_oracle.so`` — the C restatement of the reference's quantized
+  matvec path (``qraf_oracle.c``), built by ``make -C oracle``.
+* ``_ref/libqraf_ref.so`` — the reference's own sources compiled in place by
+  ``make -C oracle ref`` (only where the reference tree exists; the built file
+  travels with the repository snapshot).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` import this package.  The product (``qraf_b200``) never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "libqraf_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libqraf_ref.so")
+REF_TREE = os.environ.get("QRAF_REFERENCE_TREE", "/root/reference")
+
+Q8_0 = 10
+Q4_0 = 20
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+
+
+def build(with_ref: bool | None = None) -> None:
+    """Compile the restatement, and the reference library when its tree exists."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    if with_ref is None:
+        with_ref = os.path.isdir(os.path.join(REF_TREE, "src"))
+    if with_ref:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
+
+
+def block_bytes(dtype: int, bs: int) -> int:
+    return 4 + bs if dtype == Q8_0 else 2 + bs // 2
+
+
+def row_bytes(dtype: int, bs: int, k: int) -> int:
+    return (k + bs - 1) // bs * block_bytes(dtype, bs)
+
+
+class Oracle:
+    """The C restatement (qraf_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build(with_ref=False)
+        lib = C.CDLL(path)
+        lib.qo_fp16_to_fp32.restype = C.c_float
+        lib.qo_fp16_to_fp32.argtypes = [C.c_uint16]
+        lib.qo_fp32_to_fp16.restype = C.c_uint16
+        lib.qo_fp32_to_fp16.argtypes = [C.c_float]
+        for q in ("qo_quantize_q8_0", "qo_quantize_q4_0"):
+            getattr(lib, q).restype = C.c_size_t
+            getattr(lib, q).argtypes = [_f32p, C.c_size_t, C.c_int, _u8p]
+        for d in ("qo_dot_q8_0_f32", "qo_dot_q4_0_f32"):
+            getattr(lib, d).restype = C.c_float
+            getattr(lib, d).argtypes = [_u8p, _f32p, C.c_size_t, C.c_int]
+        for d in ("qo_dequantize_block_q8_0", "qo_dequantize_block_q4_0"):
+            getattr(lib, d).restype = None
+            getattr(lib, d).argtypes = [_u8p, _f32p, C.c_int]
+        lib.qo_matvec_q.restype = None
+        lib.qo_matvec_q.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f32p]
+        lib.qo_matmul_q.restype = None
+        lib.qo_matmul_q.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
+                                    _f32p, _f32p]
+        lib.qo_block_partials.restype = None
+        lib.qo_block_partials.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f32p]
+        lib.qo_matvec_q_f64.restype = None
+        lib.qo_matvec_q_f64.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f64p]
+        self.lib = lib
+
+    def fp32_to_fp16(self, f: float) -> int:
+        return int(self.lib.qo_fp32_to_fp16(f))
+
+    def fp16_to_fp32(self, h: int) -> float:
+        return float(self.lib.qo_fp16_to_fp32(h))
+
+    def quantize(self, dtype: int, data: np.ndarray, bs: int = 32) -> np.ndarray:
+        data = np.ascontiguousarray(data, dtype=np.float32).ravel()
+        out = np.zeros(row_bytes(dtype, bs, data.size), dtype=np.uint8)
+        fn = self.lib.qo_quantize_q8_0 if dtype == Q8_0 else self.lib.qo_quantize_q4_0
+        n = fn(data, data.size, bs, out)
+        assert n == out.size
+        return out
+
+    def quantize_rows(self, dtype: int, w: np.ndarray, bs: int = 32) -> np.ndarray:
+        """Per-row quantization of a [N][K] weight (the layout the matvec reads)."""
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        n, k = w.shape
+        rb = row_bytes(dtype, bs, k)
+        out = np.zeros((n, rb), dtype=np.uint8)
+        for r in range(n):
+            out[r] = self.quantize(dtype, w[r], bs)
+        return out
+
+    def dot(self, dtype: int, q: np.ndarray, x: np.ndarray, count: int, bs: int = 32) -> float:
+        fn = self.lib.qo_dot_q8_0_f32 if dtype == Q8_0 else self.lib.qo_dot_q4_0_f32
+        return float(fn(np.ascontiguousarray(q, dtype=np.uint8).ravel(),
+                        np.ascontiguousarray(x, dtype=np.float32).ravel(), count, bs))
+
+    def dequantize_block(self, dtype: int, q: np.ndarray, bs: int) -> np.ndarray:
+        out = np.zeros(bs, dtype=np.float32)
+        fn = self.lib.qo_dequantize_block_q8_0 if dtype == Q8_0 else self.lib.qo_dequantize_block_q4_0
+        fn(np.ascontiguousarray(q, dtype=np.uint8).ravel(), out, bs)
+        return out
+
+    def matvec(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32) -> np.ndarray:
+        y = np.zeros(n, dtype=np.float32)
+        self.lib.qo_matvec_q(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k,
+                             np.ascontiguousarray(x, dtype=np.float32).ravel(), y)
+        return y
+
+    def matmul(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        m = x.size // k
+        y = np.zeros((m, n), dtype=np.float32)
+        self.lib.qo_matmul_q(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k, m,
+                             x.ravel(), y.ravel())
+        return y
+
+    def block_partials(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32):
+        nb = (k + bs - 1) // bs
+        p = np.zeros((n, nb), dtype=np.float32)
+        self.lib.qo_block_partials(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k,
+                                   np.ascontiguousarray(x, dtype=np.float32).ravel(), p.ravel())
+        return p
+
+    def matvec_f64(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32):
+        y = np.zeros(n, dtype=np.float64)
+        self.lib.qo_matvec_q_f64(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k,
+                                 np.ascontiguousarray(x, dtype=np.float32).ravel(), y)
+        return y
+
+
+class Reference:
+    """The reference's own compiled code (oracle/_ref/libqraf_ref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref` where the reference tree exists")
+        lib = C.CDLL(path)
+        lib.qref_quantize.restype = C.c_size_t
+        lib.qref_quantize.argtypes = [C.c_uint32, _f32p, C.c_size_t, C.c_int, _u8p]
+        lib.qref_dot.restype = C.c_float
+        lib.qref_dot.argtypes = [C.c_uint32, _u8p, _f32p, C.c_size_t, C.c_int]
+        lib.qref_dequantize_block.restype = None
+        lib.qref_dequantize_block.argtypes = [C.c_uint32, _u8p, _f32p, C.c_int]
+        lib.qref_dispatch_matvec_q.restype = None
+        lib.qref_dispatch_matvec_q.argtypes = [_u8p, C.c_uint64, C.c_uint32, C.c_int, C.c_uint32,
+                                               C.c_uint32, _f32p, _f32p]
+        lib.qref_ops_matvec_quantized.restype = None
+        lib.qref_ops_matvec_quantized.argtypes = lib.qref_dispatch_matvec_q.argtypes
+        lib.qref_matvec_q_threaded.restype = None
+        lib.qref_matvec_q_threaded.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32,
+                                               _f32p, _f32p, C.c_int]
+        lib.qref_fp32_to_fp16.restype = C.c_uint16
+        lib.qref_fp32_to_fp16.argtypes = [C.c_float]
+        lib.qref_fp16_to_fp32.restype = C.c_float
+        lib.qref_fp16_to_fp32.argtypes = [C.c_uint16]
+        lib.qref_fill_normal.restype = None
+        lib.qref_fill_normal.argtypes = [C.c_uint32, C.c_float, C.c_float, _f32p, C.c_size_t]
+        self.lib = lib
+
+    def fill_normal(self, seed: int, mean: float, std: float, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        self.lib.qref_fill_normal(seed, mean, std, out, n)
+        return out
+
+    def quantize(self, dtype: int, data: np.ndarray, bs: int = 32) -> np.ndarray:
+        data = np.ascontiguousarray(data, dtype=np.float32).ravel()
+        out = np.zeros(row_bytes(dtype, bs, data.size), dtype=np.uint8)
+        n = self.lib.qref_quantize(dtype, data, data.size, bs, out)
+        assert n == out.size
+        return out
+
+    def quantize_rows(self, dtype: int, w: np.ndarray, bs: int = 32) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        n, k = w.shape
+        out = np.zeros((n, row_bytes(dtype, bs, k)), dtype=np.uint8)
+        for r in range(n):
+            out[r] = self.quantize(dtype, w[r], bs)
+        return out
+
+    def dot(self, dtype: int, q: np.ndarray, x: np.ndarray, count: int, bs: int = 32) -> float:
+        return float(self.lib.qref_dot(dtype, np.ascontiguousarray(q, dtype=np.uint8).ravel(),
+                                       np.ascontiguousarray(x, dtype=np.float32).ravel(), count, bs))
+
+    def dequantize_block(self, dtype: int, q: np.ndarray, bs: int) -> np.ndarray:
+        out = np.zeros(bs, dtype=np.float32)
+        self.lib.qref_dequantize_block(dtype, np.ascontiguousarray(q, dtype=np.uint8).ravel(), out, bs)
+        return out
+
+    def matvec(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32,
+               threads: int = 1) -> np.ndarray:
+        y = np.zeros(n, dtype=np.float32)
+        wb = np.ascontiguousarray(w, dtype=np.uint8).ravel()
+        xb = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        if threads > 1:
+            self.lib.qref_matvec_q_threaded(wb, dtype, bs, n, k, xb, y, threads)
+        else:
+            self.lib.qref_dispatch_matvec_q(wb, wb.size, dtype, bs, n, k, xb, y)
+        return y
+
+    def ops_matvec(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32):
+        y = np.zeros(n, dtype=np.float32)
+        wb = np.ascontiguousarray(w, dtype=np.uint8).ravel()
+        self.lib.qref_ops_matvec_quantized(wb, wb.size, dtype, bs, n, k,
+                                           np.ascontiguousarray(x, dtype=np.float32).ravel(), y)
+        return y
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_SO)

@@ -1,0 +1,117 @@
+// ref_shim.cpp — C entry points onto the reference's OWN compiled sources.
+//
+// TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
+// the unmodified reference sources (src/tensor/{quantize,dtype,tensor}.cpp,
+// src/nn/{backend,ops,threading}.cpp, src/core/{logging,error}.cpp, read in
+// place from the reference tree) into oracle/_ref/libqraf_ref.so.  It is used
+// to pin the C restatement (qraf_oracle.c), to generate the golden fixtures in
+// tests/golden/, and as the timed CPU baseline.  No reference source is copied.
+#include "core/types.h"
+#include "nn/backend.h"
+#include "nn/ops.h"
+#include "qraf/format.h"
+#include "tensor/quantize.h"
+
+#include <cstring>
+#include <random>
+#include <thread>
+#include <vector>
+
+using namespace qraf;
+
+namespace qraf {
+f32 fp16_to_fp32(f16 h);
+f16 fp32_to_fp16(f32 f);
+}
+
+static QuantScheme make_scheme(int block_size) {
+    QuantScheme qs;
+    std::memset(&qs, 0, sizeof(qs));
+    qs.block_size = static_cast<u32>(block_size);
+    qs.flags = 1;
+    return qs;
+}
+
+extern "C" {
+
+// quantize_q8_0 / quantize_q4_0 (src/tensor/quantize.cpp:105-183).  Copies the
+// returned byte vector into `out` (caller sizes it) and returns its length.
+size_t qref_quantize(uint32_t dtype, const float* data, size_t count, int block_size, uint8_t* out) {
+    std::vector<u8> v;
+    if (dtype == static_cast<uint32_t>(DType::Q8_0)) v = quantize_q8_0(data, count, block_size);
+    else if (dtype == static_cast<uint32_t>(DType::Q4_0)) v = quantize_q4_0(data, count, block_size);
+    else return 0;
+    if (out) std::memcpy(out, v.data(), v.size());
+    return v.size();
+}
+
+// dot_q8_0_f32 / dot_q4_0_f32 (src/tensor/quantize.cpp:187-239).
+float qref_dot(uint32_t dtype, const void* q, const float* x, size_t count, int block_size) {
+    if (dtype == static_cast<uint32_t>(DType::Q8_0)) return dot_q8_0_f32(q, x, count, block_size);
+    if (dtype == static_cast<uint32_t>(DType::Q4_0)) return dot_q4_0_f32(q, x, count, block_size);
+    return 0.0f;
+}
+
+// dequantize_block_q8_0 / _q4_0 (src/tensor/quantize.cpp:17-51).
+void qref_dequantize_block(uint32_t dtype, const void* block, float* out, int block_size) {
+    if (dtype == static_cast<uint32_t>(DType::Q8_0)) dequantize_block_q8_0(block, out, block_size);
+    else if (dtype == static_cast<uint32_t>(DType::Q4_0)) dequantize_block_q4_0(block, out, block_size);
+}
+
+// dispatch_matvec_q (src/nn/backend.cpp:131-199).  block_size <= 0 passes a
+// null QuantScheme (the reference then uses 32).
+void qref_dispatch_matvec_q(const void* w, uint64_t w_size, uint32_t dtype, int block_size,
+                            uint32_t N, uint32_t K, const float* x, float* y) {
+    QuantScheme qs = make_scheme(block_size);
+    dispatch_matvec_q(w, w_size, static_cast<DType>(dtype), block_size > 0 ? &qs : nullptr,
+                      N, K, x, y);
+}
+
+// ops::matvec_quantized (src/nn/ops.cpp:72-103).
+void qref_ops_matvec_quantized(const void* w, uint64_t w_size, uint32_t dtype, int block_size,
+                               uint32_t N, uint32_t K, const float* x, float* y) {
+    QuantScheme qs = make_scheme(block_size);
+    ops::matvec_quantized(w, w_size, static_cast<DType>(dtype), block_size > 0 ? &qs : nullptr,
+                          N, K, x, y);
+}
+
+// The same per-row dot fanned out over `threads` host threads, rows split in
+// contiguous ranges.  This mirrors the row fan-out the reference uses on its
+// threaded build (parallel_for over output rows, src/nn/backend.cpp:145-151);
+// each row is still the reference's own scalar dot, so results are identical.
+void qref_matvec_q_threaded(const void* w, uint32_t dtype, int block_size, uint32_t N, uint32_t K,
+                            const float* x, float* y, int threads) {
+    if (threads <= 1) {
+        qref_dispatch_matvec_q(w, 0, dtype, block_size, N, K, x, y);
+        return;
+    }
+    const int bs = block_size > 0 ? block_size : 32;
+    const size_t nb = (static_cast<size_t>(K) + bs - 1) / bs;
+    const size_t rb = nb * (dtype == static_cast<uint32_t>(DType::Q8_0) ? (4u + bs) : (2u + bs / 2));
+    const u8* base = static_cast<const u8*>(w);
+    std::vector<std::thread> pool;
+    for (int t = 0; t < threads; t++) {
+        uint32_t r0 = static_cast<uint32_t>(static_cast<uint64_t>(N) * t / threads);
+        uint32_t r1 = static_cast<uint32_t>(static_cast<uint64_t>(N) * (t + 1) / threads);
+        pool.emplace_back([=]() {
+            for (uint32_t r = r0; r < r1; r++)
+                y[r] = qref_dot(dtype, base + static_cast<size_t>(r) * rb, x, K, bs);
+        });
+    }
+    for (auto& th : pool) th.join();
+}
+
+// fp32_to_fp16 / fp16_to_fp32 (src/tensor/dtype.cpp:9-59).
+uint16_t qref_fp32_to_fp16(float f) { return fp32_to_fp16(f); }
+float qref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
+
+// Seeded synthetic data with the reference's idiom (std::mt19937 +
+// std::normal_distribution<float>, tools/dummy_model.cpp:12-16,
+// benchmarks/bench_main.cpp:43-44).
+void qref_fill_normal(uint32_t seed, float mean, float stddev, float* out, size_t n) {
+    std::mt19937 rng(seed);
+    std::normal_distribution<float> dist(mean, stddev);
+    for (size_t i = 0; i < n; i++) out[i] = dist(rng);
+}
+
+}  // extern "C"

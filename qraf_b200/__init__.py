@@ -1,0 +1,305 @@
+"""qraf_b200 — B200-native block-quantized (Q8_0 / Q4_0) matvec for QRAF.
+
+Host-side Python mirror of the reference's operator API for this one path
+(simonpierreboucher02/qraf: ``qraf::dispatch_matvec_q`` in src/nn/backend.cpp:131-199,
+``dot_q8_0_f32`` / ``dot_q4_0_f32`` and ``quantize_q8_0`` / ``quantize_q4_0`` in
+src/tensor/quantize.cpp), calling the sm_100a kernels of ``libqraf_cuda.so``
+through its C ABI (include/qraf_cuda.h).  PyTorch is used only to hold device
+memory and streams.
+
+There is no CPU fallback: every compute entry point runs on the GPU, and
+the first call into it raises ImportError if the CUDA library has not been
+built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build as _build
+
+Q8_0 = 10
+Q4_0 = 20
+
+MODE_EXACT = 0
+MODE_FAST = 1
+MODE_TC = 2
+MODE_AUTO = 3
+
+OK = 0
+ERR_INVALID = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_COMM = 5
+ERR_NOMEM = 6
+
+LIB_PATH = _build.LIB
+
+
+class QrafError(RuntimeError):
+    """A non-zero status from the C ABI (the reference raises QrafError too, include/core/error.h)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"qraf_cuda error {code}: {msg}")
+        self.code = code
+
+
+class qraf_weight_t(C.Structure):
+    _fields_ = [
+        ("data", C.c_void_p),
+        ("bytes", C.c_uint64),
+        ("row_bytes", C.c_uint64),
+        ("dtype", C.c_uint32),
+        ("block_size", C.c_uint32),
+        ("rows", C.c_uint32),
+        ("cols", C.c_uint32),
+        ("device", C.c_int32),
+        ("owned", C.c_uint32),
+    ]
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python -m qraf_b200.build` (nvcc, sm_100a) first")
+    lib = C.CDLL(LIB_PATH)
+    W = C.POINTER(qraf_weight_t)
+    vp, u32, u64, i32, f32p = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int, C.POINTER(C.c_float)
+    sig = {
+        "qraf_cuda_version": (C.c_char_p, []),
+        "qraf_cuda_init": (i32, [i32]),
+        "qraf_cuda_shutdown": (i32, []),
+        "qraf_cuda_last_error": (i32, [C.c_char_p, C.c_size_t]),
+        "qraf_cuda_device_status": (i32, [i32]),
+        "qraf_row_bytes": (u64, [u32, u32, u32]),
+        "qraf_cuda_weight_wrap": (i32, [vp, u64, u32, u32, u32, u32, W]),
+        "qraf_cuda_weight_upload": (i32, [vp, u64, u32, u32, u32, u32, W]),
+        "qraf_cuda_weight_free": (i32, [W]),
+        "qraf_cuda_weight_shard": (i32, [W, u32, u32, W]),
+        "qraf_cuda_matvec_q": (i32, [W, vp, vp, u32, i32, vp]),
+        "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
+        "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
+        "qraf_cuda_quantize": (i32, [u32, vp, u64, u32, vp, vp]),
+        "qraf_cuda_quantize_rows": (i32, [u32, vp, u32, u32, u32, vp, vp]),
+        "qraf_cuda_dequantize": (i32, [u32, vp, u64, u32, vp, vp]),
+        "qraf_cuda_matvec_q_host": (i32, [vp, u64, u32, u32, u32, u32, vp, vp, u32, i32]),
+        "qraf_cuda_host_cache_clear": (i32, []),
+        "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_LIB = None
+
+
+def _get_lib() -> C.CDLL:
+    """The loaded libqraf_cuda.so; raises ImportError when it has not been built."""
+    global _LIB
+    if _LIB is None:
+        _LIB = _load()
+    return _LIB
+
+
+def __getattr__(name):
+    if name == "lib":
+        return _get_lib()
+    raise AttributeError(name)
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(512)
+    _get_lib().qraf_cuda_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise QrafError(rc, last_error())
+
+
+def row_bytes(dtype: int, cols: int, block_size: int = 32) -> int:
+    return int(_get_lib().qraf_row_bytes(dtype, block_size, cols))
+
+
+def fill_normal(seed: int, mean: float, std: float, n: int) -> np.ndarray:
+    """std::mt19937(seed) + std::normal_distribution<float>(mean, std), the reference's seeding idiom."""
+    out = np.empty(n, dtype=np.float32)
+    _get_lib().qraf_fill_normal(seed, mean, std, out.ctypes.data_as(C.POINTER(C.c_float)), n)
+    return out
+
+
+# ── device side (torch tensors as device memory) ─────────────────────────
+def _torch():
+    import torch
+
+    return torch
+
+
+def _stream(stream) -> C.c_void_p:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def init(device: int = 0) -> None:
+    check(_get_lib().qraf_cuda_init(device))
+
+
+def device_status(clear: bool = True) -> int:
+    return int(_get_lib().qraf_cuda_device_status(1 if clear else 0))
+
+
+class Weight:
+    """A quantized [rows][cols] weight in the reference's native block layout on one device."""
+
+    def __init__(self, desc: qraf_weight_t, keepalive=None):
+        self.desc = desc
+        self._keep = keepalive
+
+    @classmethod
+    def from_device(cls, data, dtype: int, rows: int, cols: int, block_size: int = 32) -> "Weight":
+        """Wrap a CUDA uint8 tensor holding rows * row_bytes native bytes (no copy)."""
+        d = qraf_weight_t()
+        check(_get_lib().qraf_cuda_weight_wrap(C.c_void_p(data.data_ptr()), data.numel() * data.element_size(), dtype,
+                                        block_size, rows, cols, C.byref(d)))
+        return cls(d, keepalive=data)
+
+    @classmethod
+    def upload(cls, host: np.ndarray, dtype: int, rows: int, cols: int, block_size: int = 32) -> "Weight":
+        host = np.ascontiguousarray(host, dtype=np.uint8)
+        d = qraf_weight_t()
+        check(_get_lib().qraf_cuda_weight_upload(host.ctypes.data_as(C.c_void_p), host.nbytes, dtype, block_size, rows,
+                                          cols, C.byref(d)))
+        return cls(d)
+
+    def shard(self, world: int, rank: int) -> "Weight":
+        d = qraf_weight_t()
+        check(_get_lib().qraf_cuda_weight_shard(C.byref(self.desc), world, rank, C.byref(d)))
+        return Weight(d, keepalive=self)
+
+    @property
+    def rows(self) -> int:
+        return self.desc.rows
+
+    @property
+    def cols(self) -> int:
+        return self.desc.cols
+
+    @property
+    def dtype(self) -> int:
+        return self.desc.dtype
+
+    @property
+    def nbytes(self) -> int:
+        return self.desc.bytes
+
+    def free(self) -> None:
+        if self.desc.owned:
+            check(_get_lib().qraf_cuda_weight_free(C.byref(self.desc)))
+
+    def __del__(self):
+        try:
+            if self.desc.owned and self.desc.data:
+                _get_lib().qraf_cuda_weight_free(C.byref(self.desc))
+        except Exception:
+            pass
+
+
+def matvec_q(w: Weight, x, y=None, mode: int = MODE_AUTO, stream=None):
+    """Y[m] = dispatch_matvec_q(W, X[m]) on the GPU.  x: CUDA fp32 [M, cols] or [cols]."""
+    torch = _torch()
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.dtype != torch.float32 or not x2.is_cuda or not x2.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA float32 tensor")
+    m = x2.shape[0]
+    if x2.shape[1] != w.cols:
+        raise ValueError(f"x has {x2.shape[1]} columns, the weight has {w.cols}")
+    if y is None:
+        y = torch.empty((m, w.rows), dtype=torch.float32, device=x.device)
+    check(_get_lib().qraf_cuda_matvec_q(C.byref(w.desc), C.c_void_p(x2.data_ptr()), C.c_void_p(y.data_ptr()), m, mode,
+                                 _stream(stream)))
+    return y.reshape(w.rows) if squeeze else y
+
+
+def dot_q(dtype: int, q, x, count: int, block_size: int = 32, mode: int = MODE_EXACT, stream=None):
+    """dot_q8_0_f32 / dot_q4_0_f32 on device buffers; returns a 1-element CUDA tensor."""
+    torch = _torch()
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    check(_get_lib().qraf_cuda_dot_q(dtype, C.c_void_p(q.data_ptr()), C.c_void_p(x.data_ptr()), count, block_size,
+                              C.c_void_p(out.data_ptr()), mode, _stream(stream)))
+    return out
+
+
+def dot_q8_0_f32(q, x, count: int, block_size: int = 32, mode: int = MODE_EXACT):
+    return dot_q(Q8_0, q, x, count, block_size, mode)
+
+
+def dot_q4_0_f32(q, x, count: int, block_size: int = 32, mode: int = MODE_EXACT):
+    return dot_q(Q4_0, q, x, count, block_size, mode)
+
+
+def block_partials(w: Weight, x, stream=None):
+    torch = _torch()
+    nb = (w.cols + w.desc.block_size - 1) // w.desc.block_size
+    out = torch.empty((w.rows, nb), dtype=torch.float32, device=x.device)
+    check(_get_lib().qraf_cuda_block_partials(C.byref(w.desc), C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),
+                                       _stream(stream)))
+    return out
+
+
+def quantize(dtype: int, x, block_size: int = 32, stream=None):
+    """quantize_q8_0 / quantize_q4_0 of a contiguous CUDA fp32 tensor (all elements as one sequence)."""
+    torch = _torch()
+    n = x.numel()
+    out = torch.empty(row_bytes(dtype, n, block_size), dtype=torch.uint8, device=x.device)
+    check(_get_lib().qraf_cuda_quantize(dtype, C.c_void_p(x.data_ptr()), n, block_size, C.c_void_p(out.data_ptr()),
+                                 _stream(stream)))
+    return out
+
+
+def quantize_q8_0(x, block_size: int = 32):
+    return quantize(Q8_0, x, block_size)
+
+
+def quantize_q4_0(x, block_size: int = 32):
+    return quantize(Q4_0, x, block_size)
+
+
+def quantize_rows(dtype: int, x2d, block_size: int = 32, stream=None):
+    """Quantize each row of a [rows, cols] CUDA fp32 tensor; returns uint8 [rows, row_bytes]."""
+    torch = _torch()
+    rows, cols = x2d.shape
+    out = torch.empty((rows, row_bytes(dtype, cols, block_size)), dtype=torch.uint8, device=x2d.device)
+    check(_get_lib().qraf_cuda_quantize_rows(dtype, C.c_void_p(x2d.data_ptr()), rows, cols, block_size,
+                                      C.c_void_p(out.data_ptr()), _stream(stream)))
+    return out
+
+
+def dequantize(dtype: int, q, count: int, block_size: int = 32, stream=None):
+    torch = _torch()
+    out = torch.empty(count, dtype=torch.float32, device=q.device)
+    check(_get_lib().qraf_cuda_dequantize(dtype, C.c_void_p(q.data_ptr()), count, block_size, C.c_void_p(out.data_ptr()),
+                                   _stream(stream)))
+    return out
+
+
+# ── host side: the reference-facing entry ────────────────────────────────
+def dispatch_matvec_q(w_data: np.ndarray, w_size: int, w_dtype: int, block_size: int, out_dim: int, in_dim: int,
+                      x: np.ndarray, y: np.ndarray, m: int = 1, mode: int = MODE_EXACT) -> None:
+    """qraf::dispatch_matvec_q with host buffers (backend.cpp:131-199); y is overwritten."""
+    if not (w_data.flags.c_contiguous and x.flags.c_contiguous and y.flags.c_contiguous):
+        raise ValueError("host buffers must be C-contiguous")
+    check(_get_lib().qraf_cuda_matvec_q_host(w_data.ctypes.data_as(C.c_void_p), w_size, w_dtype, block_size, out_dim,
+                                      in_dim, x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p), m, mode))
+
+
+def host_cache_clear() -> None:
+    check(_get_lib().qraf_cuda_host_cache_clear())

@@ -1,0 +1,612 @@
+// capi.cu — the C ABI of libqraf_cuda.so (declared in include/qraf_cuda.h):
+// argument checking, kernel selection and launch planning, the host-pointer
+// drop-in entry with its device weight cache, and small host utilities.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <random>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "common.cuh"
+#include "matvec_generic.cuh"
+#include "matvec_stream.cuh"
+#include "quantize.cuh"
+
+using namespace qraf_dev;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+#define QRAF_CUDA_TRY(expr)                                                                        \
+    do {                                                                                           \
+        cudaError_t e_ = (expr);                                                                   \
+        if (e_ != cudaSuccess) return fail(QRAF_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+    } while (0)
+
+bool known_dtype(uint32_t dt) { return dt == QRAF_DTYPE_Q8_0 || dt == QRAF_DTYPE_Q4_0; }
+
+uint64_t block_bytes_of(uint32_t dt, uint32_t bs) {
+    if (dt == QRAF_DTYPE_Q8_0) return 4ull + bs;
+    if (dt == QRAF_DTYPE_Q4_0) return 2ull + bs / 2u;
+    return 0;
+}
+
+// ── per-device state ──────────────────────────────────────────────────────
+struct DeviceInfo {
+    bool ready = false;
+    int sm_count = 0;
+    int smem_optin = 0;
+};
+
+std::mutex g_dev_mutex;
+DeviceInfo g_dev[64];
+
+constexpr int kSmemReserve = 1024;
+
+template <typename K>
+cudaError_t allow_smem(K kernel, int bytes) {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+int ensure_device(int* dev_out, DeviceInfo** info_out) {
+    int dev = 0;
+    QRAF_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QRAF_ERR_INVALID, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.ready) {
+        cudaDeviceProp prop;
+        QRAF_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major < 10)
+            return fail(QRAF_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                        prop.major, prop.minor);
+        d.sm_count = prop.multiProcessorCount;
+        d.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+        const int lim = d.smem_optin;
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ8, true, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ8, false, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ8, false, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ8, false, 4>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, true, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 4>, lim));
+        d.ready = true;
+    }
+    if (dev_out) *dev_out = dev;
+    if (info_out) *info_out = &d;
+    return QRAF_OK;
+}
+
+// ── streaming-kernel plan ────────────────────────────────────────────────
+struct StreamPlan {
+    StreamParams p;
+    int grid = 0, threads = 0, MT = 1;
+    size_t smem = 0;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool plan_stream(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool exact, int MT,
+                 const DeviceInfo& dev, StreamPlan* out) {
+    if (w.block_size != 32 || (w.cols % 32) != 0 || (w.row_bytes % 16) != 0) return false;
+    if (!aligned16(w.data) || !aligned16(x) || (w.cols % 4) != 0) return false;
+    const uint32_t nblk = w.cols / 32;
+    const uint32_t nwk = (nblk + 31) / 32;
+    const uint32_t cw_max = (MT == 1) ? 16u : (MT == 2 ? 12u : 8u);
+    if (nwk > cw_max) return false;
+    const uint32_t P = cw_max / nwk;
+    const uint32_t CW = nwk * P;
+    const uint32_t unit = (MT == 1) ? 2u * P : P;
+    const uint64_t rb = w.row_bytes;
+    uint32_t R = unit;
+    while (R * rb < 16384 && (R + unit) * rb <= 40960) R += unit;
+    while (R > 1 && R * rb > 49152) --R;
+    const uint32_t G = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), w.rows);
+    const uint32_t rows_base = w.rows / G, rows_extra = w.rows % G;
+    const uint32_t max_rows = rows_base + (rows_extra ? 1u : 0u);
+    R = std::min(R, max_rows);
+    const uint32_t slot_stride = static_cast<uint32_t>((R * rb + 127) / 128 * 128);
+    uint32_t pb_row, pb_bytes;
+    if (exact) {
+        pb_row = nblk + 4;
+        pb_bytes = R * pb_row * 4u;
+    } else if (MT == 1) {
+        pb_row = nwk;
+        pb_bytes = R * nwk * 4u;
+    } else {
+        pb_row = nwk;
+        pb_bytes = R * M * nwk * 4u;
+    }
+    const uint32_t pb_stride = (pb_bytes + 127) / 128 * 128;
+    const uint32_t per_slot = slot_stride + pb_stride + 20u;
+    const int budget = dev.smem_optin - kSmemReserve;
+    const uint32_t stages_needed = (max_rows + R - 1) / R;
+    uint32_t nst = std::min<uint32_t>(8u, stages_needed);
+    while (nst > 1 && static_cast<int>(nst * per_slot + 64) > budget) --nst;
+    if (static_cast<int>(nst * per_slot + 64) > budget) return false;
+
+    StreamParams& p = out->p;
+    p.w = static_cast<const uint8_t*>(w.data);
+    p.x = x;
+    p.y = y;
+    p.row_bytes = rb;
+    p.N = w.rows;
+    p.K = w.cols;
+    p.M = M;
+    p.nblk = nblk;
+    p.nwk = nwk;
+    p.P = P;
+    p.CW = CW;
+    p.R = R;
+    p.nst = nst;
+    p.slot_stride = slot_stride;
+    p.pb_stride = pb_stride;
+    p.pb_row = pb_row;
+    p.rows_base = rows_base;
+    p.rows_extra = rows_extra;
+    out->grid = static_cast<int>(G);
+    out->threads = static_cast<int>((CW + 1) * 32);
+    out->MT = MT;
+    out->smem = static_cast<size_t>(nst) * (slot_stride + pb_stride) + nst * 20u + 64u;
+    return true;
+}
+
+template <uint32_t DT>
+cudaError_t launch_stream(const StreamPlan& pl, bool exact, cudaStream_t st) {
+    if (exact) {
+        qmv_stream_kernel<DT, true, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+    } else if (pl.MT == 1) {
+        qmv_stream_kernel<DT, false, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+    } else if (pl.MT == 2) {
+        qmv_stream_kernel<DT, false, 2><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+    } else {
+        qmv_stream_kernel<DT, false, 4><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+    }
+    return cudaGetLastError();
+}
+
+template <uint32_t DT, bool EXACT, bool PARTIALS>
+cudaError_t launch_generic(const GenericParams& gp, uint64_t tasks, cudaStream_t st) {
+    const uint64_t grid = (tasks + 7) / 8;
+    if (grid == 0) return cudaSuccess;
+    if (grid > 0x7FFFFFFFull) return cudaErrorInvalidConfiguration;
+    qmv_generic_kernel<DT, EXACT, PARTIALS><<<static_cast<unsigned>(grid), 256, 0, st>>>(gp);
+    return cudaGetLastError();
+}
+
+int check_weight(const qraf_weight_t* w) {
+    if (!w) return fail(QRAF_ERR_INVALID, "weight is NULL");
+    if (!known_dtype(w->dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", w->dtype);
+    if (w->block_size == 0) return fail(QRAF_ERR_INVALID, "block_size is 0");
+    if (w->dtype == QRAF_DTYPE_Q4_0 && w->block_size < 2)
+        return fail(QRAF_ERR_INVALID, "Q4_0 block_size must be at least 2");
+    if (w->row_bytes != qraf_row_bytes(w->dtype, w->block_size, w->cols))
+        return fail(QRAF_ERR_INVALID, "row_bytes %llu does not match dtype/block_size/cols",
+                    static_cast<unsigned long long>(w->row_bytes));
+    if (w->rows && w->cols && !w->data) return fail(QRAF_ERR_INVALID, "weight data is NULL");
+    return QRAF_OK;
+}
+
+int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode, cudaStream_t st) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
+    if (mode == QRAF_MODE_TC) return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core tile is not built in this library");
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_INVALID, "unknown mode %d", mode);
+    if (M == 0 || w->rows == 0) return QRAF_OK;
+    if (!x || !y) return fail(QRAF_ERR_INVALID, "x or y is NULL");
+    if (w->cols == 0) {
+        QRAF_CUDA_TRY(cudaMemsetAsync(y, 0, static_cast<size_t>(M) * w->rows * sizeof(float), st));
+        return QRAF_OK;
+    }
+    DeviceInfo* dev = nullptr;
+    rc = ensure_device(nullptr, &dev);
+    if (rc) return rc;
+    const bool exact = (mode == QRAF_MODE_EXACT);
+
+    // Streaming kernel where the layout allows it.
+    StreamPlan pl;
+    if (exact) {
+        if (plan_stream(*w, x, y, 1, true, 1, *dev, &pl)) {
+            for (uint32_t m = 0; m < M; ++m) {
+                pl.p.x = x + static_cast<size_t>(m) * w->cols;
+                pl.p.y = y + static_cast<size_t>(m) * w->rows;
+                const cudaError_t e = (w->dtype == QRAF_DTYPE_Q8_0) ? launch_stream<kDtypeQ8>(pl, true, st)
+                                                                     : launch_stream<kDtypeQ4>(pl, true, st);
+                if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "stream kernel launch: %s", cudaGetErrorString(e));
+            }
+            return QRAF_OK;
+        }
+    } else {
+        int MT = (M == 1) ? 1 : (M == 2 ? 2 : 4);
+        bool ok = plan_stream(*w, x, y, M, false, MT, *dev, &pl);
+        if (!ok && MT == 4) ok = plan_stream(*w, x, y, M, false, MT = 2, *dev, &pl);
+        if (!ok && MT == 2 && M == 2) ok = false;
+        if (ok) {
+            const cudaError_t e = (w->dtype == QRAF_DTYPE_Q8_0) ? launch_stream<kDtypeQ8>(pl, false, st)
+                                                                 : launch_stream<kDtypeQ4>(pl, false, st);
+            if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "stream kernel launch: %s", cudaGetErrorString(e));
+            return QRAF_OK;
+        }
+    }
+
+    // Generic kernel: any block size, ragged blocks, any alignment.
+    GenericParams gp;
+    gp.w = static_cast<const uint8_t*>(w->data);
+    gp.x = x;
+    gp.y = y;
+    gp.row_bytes = w->row_bytes;
+    gp.N = w->rows;
+    gp.K = w->cols;
+    gp.M = M;
+    gp.bs = w->block_size;
+    gp.nblk = (w->cols + w->block_size - 1) / w->block_size;
+    gp.block_bytes = static_cast<uint32_t>(block_bytes_of(w->dtype, w->block_size));
+    const uint64_t tasks = static_cast<uint64_t>(w->rows) * M;
+    cudaError_t e;
+    if (w->dtype == QRAF_DTYPE_Q8_0)
+        e = exact ? launch_generic<kDtypeQ8, true, false>(gp, tasks, st) : launch_generic<kDtypeQ8, false, false>(gp, tasks, st);
+    else
+        e = exact ? launch_generic<kDtypeQ4, true, false>(gp, tasks, st) : launch_generic<kDtypeQ4, false, false>(gp, tasks, st);
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "generic kernel launch: %s", cudaGetErrorString(e));
+    return QRAF_OK;
+}
+
+// ── host-pointer entry: weight cache + staging ───────────────────────────
+struct CacheKey {
+    const void* ptr;
+    uint64_t bytes;
+    uint32_t dtype, bs, rows, cols;
+    int device;
+    bool operator<(const CacheKey& o) const {
+        return std::tie(ptr, bytes, dtype, bs, rows, cols, device) <
+               std::tie(o.ptr, o.bytes, o.dtype, o.bs, o.rows, o.cols, o.device);
+    }
+};
+
+struct HostStaging {
+    cudaStream_t stream = nullptr;
+    float* x_pinned = nullptr;
+    float* y_pinned = nullptr;
+    float* x_dev = nullptr;
+    float* y_dev = nullptr;
+    size_t x_cap = 0, y_cap = 0;   // in floats
+};
+
+std::mutex g_host_mutex;
+std::map<CacheKey, qraf_weight_t> g_cache;
+HostStaging g_staging[64];
+
+int grow(HostStaging& s, size_t xn, size_t yn) {
+    if (!s.stream) QRAF_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    if (xn > s.x_cap) {
+        if (s.x_pinned) cudaFreeHost(s.x_pinned);
+        if (s.x_dev) cudaFree(s.x_dev);
+        s.x_pinned = nullptr;
+        s.x_dev = nullptr;
+        s.x_cap = 0;
+        if (cudaMallocHost(&s.x_pinned, xn * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&s.x_dev, xn * sizeof(float)) != cudaSuccess)
+            return fail(QRAF_ERR_NOMEM, "staging allocation of %zu floats failed", xn);
+        s.x_cap = xn;
+    }
+    if (yn > s.y_cap) {
+        if (s.y_pinned) cudaFreeHost(s.y_pinned);
+        if (s.y_dev) cudaFree(s.y_dev);
+        s.y_pinned = nullptr;
+        s.y_dev = nullptr;
+        s.y_cap = 0;
+        if (cudaMallocHost(&s.y_pinned, yn * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&s.y_dev, yn * sizeof(float)) != cudaSuccess)
+            return fail(QRAF_ERR_NOMEM, "staging allocation of %zu floats failed", yn);
+        s.y_cap = yn;
+    }
+    return QRAF_OK;
+}
+
+}  // namespace
+
+// ══ exported C ABI ════════════════════════════════════════════════════════
+extern "C" {
+
+const char* qraf_cuda_version(void) { return "qraf_b200 0.1 (sm_100a)"; }
+
+int qraf_cuda_init(int device) {
+    QRAF_CUDA_TRY(cudaSetDevice(device));
+    return ensure_device(nullptr, nullptr);
+}
+
+int qraf_cuda_last_error(char* buf, size_t len) {
+    if (!buf || len == 0) return QRAF_ERR_INVALID;
+    const size_t n = std::min(len - 1, t_last_error.size());
+    std::memcpy(buf, t_last_error.data(), n);
+    buf[n] = '\0';
+    return QRAF_OK;
+}
+
+int qraf_cuda_device_status(int clear) {
+    QRAF_CUDA_TRY(cudaDeviceSynchronize());
+    uint32_t v = 0;
+    QRAF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_status, sizeof(v)));
+    if (clear) {
+        const uint32_t z = 0;
+        QRAF_CUDA_TRY(cudaMemcpyToSymbol(g_status, &z, sizeof(z)));
+    }
+    if (v & kErrWaitTimeout) return fail(QRAF_ERR_TIMEOUT, "a device-side wait expired (status 0x%x)", v);
+    if (v & kErrBadLaunch) return fail(QRAF_ERR_INVALID, "a kernel rejected its launch shape (status 0x%x)", v);
+    return QRAF_OK;
+}
+
+uint64_t qraf_row_bytes(uint32_t dtype, uint32_t block_size, uint32_t cols) {
+    if (!known_dtype(dtype) || block_size == 0) return 0;
+    const uint64_t nb = (static_cast<uint64_t>(cols) + block_size - 1) / block_size;
+    return nb * block_bytes_of(dtype, block_size);
+}
+
+static int describe_weight(uint64_t bytes, uint32_t dtype, uint32_t block_size, uint32_t rows, uint32_t cols,
+                           qraf_weight_t* out) {
+    if (!out) return fail(QRAF_ERR_INVALID, "out is NULL");
+    std::memset(out, 0, sizeof(*out));
+    if (!known_dtype(dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", dtype);
+    if (block_size == 0) return fail(QRAF_ERR_INVALID, "block_size is 0");
+    if (dtype == QRAF_DTYPE_Q4_0 && block_size < 2) return fail(QRAF_ERR_INVALID, "Q4_0 block_size must be at least 2");
+    const uint64_t rb = qraf_row_bytes(dtype, block_size, cols);
+    const uint64_t need = rb * rows;
+    if (bytes < need)
+        return fail(QRAF_ERR_INVALID, "weight holds %llu bytes, %u rows of %llu bytes need %llu",
+                    static_cast<unsigned long long>(bytes), rows, static_cast<unsigned long long>(rb),
+                    static_cast<unsigned long long>(need));
+    int dev = 0;
+    QRAF_CUDA_TRY(cudaGetDevice(&dev));
+    out->bytes = need;
+    out->row_bytes = rb;
+    out->dtype = dtype;
+    out->block_size = block_size;
+    out->rows = rows;
+    out->cols = cols;
+    out->device = dev;
+    return QRAF_OK;
+}
+
+int qraf_cuda_weight_wrap(const void* data_dev, uint64_t bytes, uint32_t dtype, uint32_t block_size, uint32_t rows,
+                          uint32_t cols, qraf_weight_t* out) {
+    int rc = describe_weight(bytes, dtype, block_size, rows, cols, out);
+    if (rc) return rc;
+    out->data = data_dev;
+    return check_weight(out);
+}
+
+int qraf_cuda_weight_upload(const void* data_host, uint64_t bytes, uint32_t dtype, uint32_t block_size, uint32_t rows,
+                            uint32_t cols, qraf_weight_t* out) {
+    int rc = describe_weight(bytes, dtype, block_size, rows, cols, out);
+    if (rc) return rc;
+    if (!data_host && out->bytes) return fail(QRAF_ERR_INVALID, "host data is NULL");
+    void* d = nullptr;
+    if (out->bytes) {
+        if (cudaMalloc(&d, out->bytes) != cudaSuccess)
+            return fail(QRAF_ERR_NOMEM, "cudaMalloc of %llu bytes failed", static_cast<unsigned long long>(out->bytes));
+        const cudaError_t e = cudaMemcpy(d, data_host, out->bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(d);
+            return fail(QRAF_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
+        }
+    }
+    out->data = d;
+    out->owned = 1;
+    return QRAF_OK;
+}
+
+int qraf_cuda_weight_free(qraf_weight_t* w) {
+    if (!w) return fail(QRAF_ERR_INVALID, "weight is NULL");
+    if (w->owned && w->data) QRAF_CUDA_TRY(cudaFree(const_cast<void*>(w->data)));
+    std::memset(w, 0, sizeof(*w));
+    return QRAF_OK;
+}
+
+int qraf_cuda_weight_shard(const qraf_weight_t* full, uint32_t world, uint32_t rank, qraf_weight_t* out) {
+    int rc = check_weight(full);
+    if (rc) return rc;
+    if (!out || world == 0 || rank >= world) return fail(QRAF_ERR_INVALID, "bad shard %u of %u", rank, world);
+    const uint32_t r0 = static_cast<uint32_t>(static_cast<uint64_t>(full->rows) * rank / world);
+    const uint32_t r1 = static_cast<uint32_t>(static_cast<uint64_t>(full->rows) * (rank + 1) / world);
+    *out = *full;
+    out->data = static_cast<const uint8_t*>(full->data) + static_cast<uint64_t>(r0) * full->row_bytes;
+    out->rows = r1 - r0;
+    out->bytes = static_cast<uint64_t>(out->rows) * full->row_bytes;
+    out->owned = 0;
+    return QRAF_OK;
+}
+
+int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int mode, void* stream) {
+    return matvec_impl(w, x_dev, y_dev, M, mode, static_cast<cudaStream_t>(stream));
+}
+
+int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint64_t count, uint32_t block_size,
+                    float* out_dev, int mode, void* stream) {
+    if (count > 0xFFFFFFFFull) return fail(QRAF_ERR_INVALID, "count %llu exceeds 2^32-1", static_cast<unsigned long long>(count));
+    qraf_weight_t w;
+    const uint64_t rb = qraf_row_bytes(dtype, block_size, static_cast<uint32_t>(count));
+    int rc = qraf_cuda_weight_wrap(q_dev, rb, dtype, block_size, 1, static_cast<uint32_t>(count), &w);
+    if (rc) return rc;
+    return matvec_impl(&w, x_dev, out_dev, 1, mode, static_cast<cudaStream_t>(stream));
+}
+
+int qraf_cuda_block_partials(const qraf_weight_t* w, const float* x_dev, float* partials_dev, void* stream) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (w->rows == 0 || w->cols == 0) return QRAF_OK;
+    if (!x_dev || !partials_dev) return fail(QRAF_ERR_INVALID, "x or partials is NULL");
+    rc = ensure_device(nullptr, nullptr);
+    if (rc) return rc;
+    GenericParams gp;
+    gp.w = static_cast<const uint8_t*>(w->data);
+    gp.x = x_dev;
+    gp.y = partials_dev;
+    gp.row_bytes = w->row_bytes;
+    gp.N = w->rows;
+    gp.K = w->cols;
+    gp.M = 1;
+    gp.bs = w->block_size;
+    gp.nblk = (w->cols + w->block_size - 1) / w->block_size;
+    gp.block_bytes = static_cast<uint32_t>(block_bytes_of(w->dtype, w->block_size));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = (w->dtype == QRAF_DTYPE_Q8_0) ? launch_generic<kDtypeQ8, true, true>(gp, w->rows, st)
+                                                        : launch_generic<kDtypeQ4, true, true>(gp, w->rows, st);
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "partials kernel launch: %s", cudaGetErrorString(e));
+    return QRAF_OK;
+}
+
+static int quantize_launch(uint32_t dtype, const float* x, uint64_t rows, uint64_t row_elems, uint32_t bs, void* out,
+                           cudaStream_t st) {
+    if (!known_dtype(dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", dtype);
+    if (bs == 0) return fail(QRAF_ERR_INVALID, "block_size is 0");
+    if (rows == 0 || row_elems == 0) return QRAF_OK;
+    if (!x || !out) return fail(QRAF_ERR_INVALID, "x or out is NULL");
+    QuantParams qp;
+    qp.x = x;
+    qp.out = static_cast<uint8_t*>(out);
+    qp.blocks_per_row = (row_elems + bs - 1) / bs;
+    qp.nblocks_total = qp.blocks_per_row * rows;
+    qp.row_elems = row_elems;
+    qp.bs = bs;
+    qp.block_bytes = static_cast<uint32_t>(block_bytes_of(dtype, bs));
+    const uint64_t grid = (qp.nblocks_total + 255) / 256;
+    if (grid > 0x7FFFFFFFull) return fail(QRAF_ERR_INVALID, "too many blocks");
+    if (dtype == QRAF_DTYPE_Q8_0)
+        quantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp);
+    else
+        quantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp);
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+int qraf_cuda_quantize(uint32_t dtype, const float* x_dev, uint64_t count, uint32_t block_size, void* out_dev,
+                       void* stream) {
+    return quantize_launch(dtype, x_dev, 1, count, block_size, out_dev, static_cast<cudaStream_t>(stream));
+}
+
+int qraf_cuda_quantize_rows(uint32_t dtype, const float* x_dev, uint32_t rows, uint32_t cols, uint32_t block_size,
+                            void* out_dev, void* stream) {
+    return quantize_launch(dtype, x_dev, rows, cols, block_size, out_dev, static_cast<cudaStream_t>(stream));
+}
+
+int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint32_t block_size, float* out_dev,
+                         void* stream) {
+    if (!known_dtype(dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", dtype);
+    if (block_size == 0) return fail(QRAF_ERR_INVALID, "block_size is 0");
+    if (count == 0) return QRAF_OK;
+    if (!q_dev || !out_dev) return fail(QRAF_ERR_INVALID, "q or out is NULL");
+    const uint64_t nb = (count + block_size - 1) / block_size;
+    const uint64_t grid = (nb + 255) / 256;
+    const uint32_t bb = static_cast<uint32_t>(block_bytes_of(dtype, block_size));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (dtype == QRAF_DTYPE_Q8_0)
+        dequantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb);
+    else
+        dequantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb);
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype, uint32_t block_size, uint32_t out_dim,
+                            uint32_t in_dim, const float* x_host, float* y_host, uint32_t M, int mode) {
+    if (M == 0 || out_dim == 0) return QRAF_OK;
+    if (!y_host) return fail(QRAF_ERR_INVALID, "y is NULL");
+    if (!known_dtype(dtype)) {
+        // The reference zero-fills y for a dtype it has no kernel for (backend.cpp:195-198).
+        std::memset(y_host, 0, static_cast<size_t>(M) * out_dim * sizeof(float));
+        return QRAF_OK;
+    }
+    if (block_size == 0) block_size = 32;   // a null QuantScheme means 32 (backend.cpp:135)
+    if (!w_host || (!x_host && in_dim)) return fail(QRAF_ERR_INVALID, "w or x is NULL");
+    int dev = 0;
+    int rc = ensure_device(&dev, nullptr);
+    if (rc) return rc;
+    const uint64_t need = qraf_row_bytes(dtype, block_size, in_dim) * out_dim;
+    (void)w_size;   // the reference never reads it either; it reads exactly `need` bytes
+    std::lock_guard<std::mutex> lk(g_host_mutex);
+    CacheKey key{w_host, need, dtype, block_size, out_dim, in_dim, dev};
+    auto it = g_cache.find(key);
+    if (it == g_cache.end()) {
+        qraf_weight_t w;
+        rc = qraf_cuda_weight_upload(w_host, need, dtype, block_size, out_dim, in_dim, &w);
+        if (rc) return rc;
+        it = g_cache.emplace(key, w).first;
+    }
+    HostStaging& s = g_staging[dev];
+    const size_t xn = std::max<size_t>(static_cast<size_t>(M) * in_dim, 4);
+    const size_t yn = static_cast<size_t>(M) * out_dim;
+    rc = grow(s, xn, yn);
+    if (rc) return rc;
+    if (in_dim) {
+        std::memcpy(s.x_pinned, x_host, static_cast<size_t>(M) * in_dim * sizeof(float));
+        QRAF_CUDA_TRY(cudaMemcpyAsync(s.x_dev, s.x_pinned, static_cast<size_t>(M) * in_dim * sizeof(float),
+                                      cudaMemcpyHostToDevice, s.stream));
+    }
+    rc = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mode, s.stream);
+    if (rc) return rc;
+    QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    QRAF_CUDA_TRY(cudaStreamSynchronize(s.stream));
+    std::memcpy(y_host, s.y_pinned, yn * sizeof(float));
+    return QRAF_OK;
+}
+
+int qraf_cuda_host_cache_clear(void) {
+    std::lock_guard<std::mutex> lk(g_host_mutex);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (auto& kv : g_cache) {
+        cudaSetDevice(kv.first.device);
+        qraf_cuda_weight_free(&kv.second);
+    }
+    g_cache.clear();
+    cudaSetDevice(cur);
+    return QRAF_OK;
+}
+
+int qraf_cuda_shutdown(void) {
+    qraf_cuda_host_cache_clear();
+    std::lock_guard<std::mutex> lk(g_host_mutex);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (int d = 0; d < 64; ++d) {
+        HostStaging& s = g_staging[d];
+        if (!s.stream && !s.x_dev && !s.y_dev) continue;
+        cudaSetDevice(d);
+        if (s.x_pinned) cudaFreeHost(s.x_pinned);
+        if (s.y_pinned) cudaFreeHost(s.y_pinned);
+        if (s.x_dev) cudaFree(s.x_dev);
+        if (s.y_dev) cudaFree(s.y_dev);
+        if (s.stream) cudaStreamDestroy(s.stream);
+        s = HostStaging();
+    }
+    cudaSetDevice(cur);
+    return QRAF_OK;
+}
+
+void qraf_fill_normal(uint32_t seed, float mean, float stddev, float* out_host, uint64_t n) {
+    std::mt19937 rng(seed);
+    std::normal_distribution<float> dist(mean, stddev);
+    for (uint64_t i = 0; i < n; ++i) out_host[i] = dist(rng);
+}
+
+}  // extern "C"

@@ -1,0 +1,176 @@
+// common.cuh — shared device helpers for the qraf_b200 kernels (sm_100a).
+//
+// Block formats consumed everywhere (the reference's on-disk layout,
+// src/tensor/quantize.cpp:14-51, unchanged):
+//   Q8_0 block = [f32 scale][bs x int8]          (4 + bs bytes)
+//   Q4_0 block = [f16 scale][bs/2 x u8]           (2 + bs/2 bytes), byte i holds
+//                element 2i in its low nibble and 2i+1 in its high nibble,
+//                each biased by +8.
+// A weight is [N rows][ceil(K/bs) blocks], rows back to back.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include "../../include/qraf_cuda.h"
+
+namespace qraf_dev {
+
+constexpr uint32_t kDtypeQ8 = QRAF_DTYPE_Q8_0;
+constexpr uint32_t kDtypeQ4 = QRAF_DTYPE_Q4_0;
+
+// Bit-or'ed into the per-device status word by kernels that give up.
+constexpr uint32_t kErrWaitTimeout = 1u;    // an mbarrier / flag wait ran out of time
+constexpr uint32_t kErrBadLaunch   = 2u;    // a kernel found its launch arguments inconsistent
+
+// Per-device status word (each device that loads the module has its own copy).
+// The library is one translation unit (capi.cu includes every kernel header),
+// so the word is defined here.
+__device__ uint32_t g_status = 0;
+
+__device__ __forceinline__ void raise_error(uint32_t bits) { atomicOr(&g_status, bits); }
+
+// ── shared-memory addresses, mbarriers, bulk copies ──────────────────────
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for an mbarrier phase with a time limit.  Returns false (and raises
+// kErrWaitTimeout) when the phase has not completed within `limit_ns`; the
+// caller then stops its work and returns, so a lost arrival can never hang
+// the GPU.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // 1 s
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+            raise_error(kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// One-dimensional bulk copy global -> shared, completing on `bar`.
+// src, dst and bytes must all be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy for data read exactly once (streamed weights).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// ── packed fp32x2 arithmetic (sm_100a), IEEE round-to-nearest, no ftz ────
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// ── integer -> float without the conversion unit ──────────────────────────
+// A byte u placed in the low mantissa bits of 2^23 gives the float 2^23 + u
+// exactly; subtracting a constant then yields small integers exactly.
+constexpr uint32_t kMagicBits = 0x4B000000u;          // 2^23
+constexpr float kMagicQ8 = 8388736.0f;                // 2^23 + 128  (int8 stored with its sign bit flipped)
+constexpr float kMagicQ4 = 8388616.0f;                // 2^23 + 8    (nibble bias of Q4_0)
+
+// Selector for __byte_perm(v, kMagicBits, sel): byte t of v into byte 0,
+// zero bytes 1-2, 0x4B into byte 3.
+__device__ __forceinline__ constexpr uint32_t magic_sel(int t) { return 0x7440u | static_cast<uint32_t>(t); }
+
+__device__ __forceinline__ float magic_byte(uint32_t v, int t) {
+    return __int_as_float(static_cast<int>(__byte_perm(v, kMagicBits, magic_sel(t))));
+}
+
+// fp16 bits -> fp32, exact for every finite value, subnormals and infinities
+// (the reference's decoder, src/tensor/dtype.cpp:9-37, is exact too).
+__device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h16 & 0xFFFFu)));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
+    return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
+           (static_cast<uint32_t>(p[3]) << 24);
+}
+
+}  // namespace qraf_dev

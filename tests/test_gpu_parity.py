@@ -1,0 +1,223 @@
+"""GPU parity: the sm_100a kernels against the oracle's and the reference's outputs.
+
+Bar: quantized payloads bit-exact; EXACT mode output
+bit-exact; FAST mode within allclose(rtol=1e-5, atol=1e-6) of the reference's
+fp32 result.  Every call goes through the C ABI of libqraf_cuda.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import qraf_b200 as qb
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+FULL = os.environ.get("QRAF_TEST_FULL", "0") == "1"
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def to_dev(a, torch, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+# ── quantizer ────────────────────────────────────────────────────────────
+def test_quantizer_small_cases_byte_exact(cuda, small_cases):
+    import torch
+
+    n_checked = 0
+    for i, c in enumerate(small_cases):
+        if "w" not in c:
+            continue
+        w = to_dev(c["w"], torch, cuda)
+        q = qb.quantize_rows(c["dtype"], w, c["bs"]).cpu().numpy()
+        assert q.tobytes() == c["q"].tobytes(), f"case {i}"
+        n_checked += 1
+    assert n_checked >= 10
+
+
+def test_reference_unit_cases_on_gpu(cuda):
+    import torch
+
+    u = np.load(os.path.join(GOLDEN, "ref_unit_cases.npz"))
+    data = to_dev(u["data"], torch, cuda)
+    assert qb.quantize(qb.Q8_0, data, 8).cpu().numpy().tobytes() == u["q8"].tobytes()
+    assert qb.quantize(qb.Q4_0, data, 8).cpu().numpy().tobytes() == u["q4"].tobytes()
+    d8 = qb.dequantize(qb.Q8_0, to_dev(u["q8"], torch, cuda), 8, 8).cpu().numpy()
+    d4 = qb.dequantize(qb.Q4_0, to_dev(u["q4"], torch, cuda), 8, 8).cpu().numpy()
+    assert d8.tobytes() == u["q8_deq"].tobytes() and d4.tobytes() == u["q4_deq"].tobytes()
+    r = qb.dot_q8_0_f32(to_dev(u["dot_q8"], torch, cuda), to_dev(u["dot_b"], torch, cuda), 4, 4).cpu().numpy()
+    assert r.tobytes() == u["dot_result"].tobytes()
+    assert abs(float(r[0]) - 5.0) <= 0.1
+
+
+def test_quantizer_special_values(cuda, oracle_lib):
+    import torch
+
+    vals = [np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-40, 6e-5, 65504.0, 7e4, -3e-8, 1e30, -1e-30]
+    for dt in (qb.Q8_0, qb.Q4_0):
+        for v in vals:
+            w = np.full(32, v, dtype=np.float32)
+            w[3], w[9] = 0.5, -0.25
+            q = qb.quantize(dt, to_dev(w, torch, cuda)).cpu().numpy()
+            assert q.tobytes() == oracle_lib.quantize(dt, w).tobytes(), (dt, v)
+    # ragged and odd block sizes
+    rng = np.random.default_rng(3)
+    for dt in (qb.Q8_0, qb.Q4_0):
+        for bs, count in [(32, 33), (7, 50), (5, 23), (64, 1000), (3, 2), (32, 1)]:
+            x = rng.standard_normal(count).astype(np.float32)
+            q = qb.quantize(dt, to_dev(x, torch, cuda), bs).cpu().numpy()
+            assert q.tobytes() == oracle_lib.quantize(dt, x, bs).tobytes(), (dt, bs, count)
+            deq = qb.dequantize(dt, to_dev(q, torch, cuda), count, bs).cpu().numpy()
+            want = np.zeros(count, np.float32)
+            nb = (count + bs - 1) // bs
+            bb = 4 + bs if dt == qb.Q8_0 else 2 + bs // 2
+            for b in range(nb):
+                n = min(bs, count - b * bs)
+                blk = oracle_lib.dequantize_block(dt, q[b * bb:(b + 1) * bb], bs)
+                m = n if dt == qb.Q8_0 else 2 * (n // 2)
+                want[b * bs:b * bs + m] = blk[:m]
+            assert deq.tobytes() == want.tobytes(), (dt, bs, count)
+
+
+# ── matvec on the golden small cases ─────────────────────────────────────
+def test_matvec_exact_small_cases(cuda, small_cases):
+    import torch
+
+    for i, c in enumerate(small_cases):
+        w = qb.Weight.from_device(to_dev(c["q"], torch, cuda).reshape(-1), c["dtype"], c["n"], c["k"], c["bs"])
+        x = to_dev(c["x"], torch, cuda)
+        y = qb.matvec_q(w, x, mode=qb.MODE_EXACT).cpu().numpy()
+        assert y.tobytes() == c["y"].tobytes(), f"case {i} ({c['dtype']}, bs={c['bs']}, {c['n']}x{c['k']}, M={c['m']})"
+
+
+def test_matvec_fast_small_cases(cuda, small_cases):
+    import torch
+
+    for i, c in enumerate(small_cases):
+        w = qb.Weight.from_device(to_dev(c["q"], torch, cuda).reshape(-1), c["dtype"], c["n"], c["k"], c["bs"])
+        x = to_dev(c["x"], torch, cuda)
+        y = qb.matvec_q(w, x, mode=qb.MODE_FAST).cpu().numpy()
+        np.testing.assert_allclose(y, c["y"], rtol=RTOL, atol=ATOL, err_msg=f"case {i}")
+
+
+def test_block_partials_bit_exact(cuda, small_cases):
+    import torch
+
+    for i, c in enumerate(small_cases):
+        w = qb.Weight.from_device(to_dev(c["q"], torch, cuda).reshape(-1), c["dtype"], c["n"], c["k"], c["bs"])
+        p = qb.block_partials(w, to_dev(c["x"][0], torch, cuda)).cpu().numpy()
+        assert p.tobytes() == c["partials"].tobytes(), f"case {i}"
+
+
+def test_unaligned_pointers_take_the_generic_path(cuda, small_cases):
+    import torch
+
+    c = next(c for c in small_cases if c["k"] == 4096)
+    raw = torch.zeros(c["q"].size + 16, dtype=torch.uint8, device=cuda)
+    raw[4:4 + c["q"].size] = to_dev(c["q"].reshape(-1), torch, cuda)
+    w = qb.Weight.from_device(raw[4:4 + c["q"].size], c["dtype"], c["n"], c["k"], c["bs"])
+    xr = torch.zeros(c["k"] + 4, dtype=torch.float32, device=cuda)
+    xr[1:1 + c["k"]] = to_dev(c["x"][0], torch, cuda)
+    y = qb.matvec_q(w, xr[1:1 + c["k"]], mode=qb.MODE_EXACT).cpu().numpy()
+    assert y.tobytes() == c["y"][0].tobytes()
+
+
+def test_empty_shapes(cuda):
+    import torch
+
+    q = torch.zeros(64, dtype=torch.uint8, device=cuda)
+    w = qb.Weight.from_device(q, qb.Q8_0, 0, 32)
+    y = torch.full((1, 0), 5.0, device=cuda)
+    qb.matvec_q(w, torch.ones(32, device=cuda), y=y)
+    w = qb.Weight.from_device(q, qb.Q8_0, 3, 0)
+    y = torch.full((1, 3), 5.0, device=cuda)
+    qb.matvec_q(w, torch.ones(4, device=cuda)[:0].reshape(1, 0).contiguous(), y=y, mode=qb.MODE_EXACT)
+    assert torch.all(y == 0)
+
+
+def test_errors_are_reported(cuda):
+    import torch
+
+    q = torch.zeros(36 * 4, dtype=torch.uint8, device=cuda)
+    w = qb.Weight.from_device(q, qb.Q8_0, 4, 32)
+    with pytest.raises(qb.QrafError) as e:
+        qb.matvec_q(w, torch.ones(32, device=cuda), mode=7)
+    assert e.value.code == qb.ERR_INVALID
+    with pytest.raises(qb.QrafError):
+        qb.Weight.from_device(q[:100], qb.Q8_0, 4, 32)
+
+
+# ── the host-pointer drop-in entry ────────────────────────────────────────
+def test_host_entry_matches_reference(cuda, small_cases):
+    for i, c in enumerate(small_cases):
+        q = np.ascontiguousarray(c["q"]).reshape(-1)
+        for mode in (qb.MODE_EXACT, qb.MODE_FAST):
+            y = np.zeros((c["m"], c["n"]), np.float32)
+            qb.dispatch_matvec_q(q, q.size, c["dtype"], c["bs"], c["n"], c["k"], np.ascontiguousarray(c["x"]), y,
+                                 m=c["m"], mode=mode)
+            if mode == qb.MODE_EXACT:
+                assert y.tobytes() == c["y"].tobytes(), f"case {i}"
+            else:
+                np.testing.assert_allclose(y, c["y"], rtol=RTOL, atol=ATOL)
+    qb.host_cache_clear()
+
+
+# ── full-size configurations ──────────────────
+_W_CACHE = {}
+
+
+def weight_for(name, d, torch, dev):
+    """Quantize the config's seeded weight on the GPU and check its digest."""
+    if name in _W_CACHE:
+        return _W_CACHE[name]
+    _W_CACHE.clear()
+    wf = qb.fill_normal(d["seed_w"], 0.0, 0.02, d["n"] * d["k"])
+    wd = torch.from_numpy(wf).to(dev).reshape(d["n"], d["k"])
+    del wf
+    q = qb.quantize_rows(d["dtype"], wd, d["block_size"])
+    del wd
+    assert sha(q.cpu().numpy()) == d["sha_q"], f"{name}: quantized payload differs from the reference"
+    w = qb.Weight.from_device(q.reshape(-1), d["dtype"], d["n"], d["k"], d["block_size"])
+    _W_CACHE[name] = w
+    return w
+
+
+def config_names(digests):
+    small = [n for n, d in digests.items() if d["n"] * d["k"] <= 300_000_000]
+    return sorted(digests) if FULL else sorted(small)
+
+
+def pytest_generate_tests(metafunc):
+    if "config_name" in metafunc.fixturenames:
+        from conftest import load_digests
+
+        metafunc.parametrize("config_name", config_names(load_digests()))
+
+
+def test_config_exact_and_fast(cuda, digests, config_name):
+    import torch
+
+    d = digests[config_name]
+    w = weight_for(config_name, d, torch, cuda)
+    mmax = max(int(m) for m in d["y"])
+    xall = torch.from_numpy(qb.fill_normal(d["seed_x"], 0.0, 1.0, mmax * d["k"])).to(cuda).reshape(mmax, d["k"])
+    ys = np.load(os.path.join(GOLDEN, "config_y.npz"))
+    for ms, digest in d["y"].items():
+        m = int(ms)
+        y_exact = qb.matvec_q(w, xall[:m].contiguous(), mode=qb.MODE_EXACT).cpu().numpy()
+        assert sha(y_exact) == digest, f"{config_name} M={m}: EXACT output differs from the reference"
+        y_fast = qb.matvec_q(w, xall[:m].contiguous(), mode=qb.MODE_FAST).cpu().numpy()
+        np.testing.assert_allclose(y_fast, y_exact, rtol=RTOL, atol=ATOL, err_msg=f"{config_name} M={m}")
+        if m == 1 and config_name in ys.files:
+            np.testing.assert_allclose(y_fast[0], ys[config_name], rtol=RTOL, atol=ATOL)
+    assert qb.device_status() == qb.OK

@@ -1,0 +1,108 @@
+"""The CPU oracle, pinned against the reference's own outputs (no GPU needed).
+
+The oracle (oracle/qraf_oracle.c) restates src/tensor/quantize.cpp,
+src/tensor/dtype.cpp and src/nn/backend.cpp.  These tests hold it to the
+golden fixtures that tests/golden/make_golden.py produced with the reference's
+compiled sources, and, where oracle/_ref is built, to the reference directly.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import GOLDEN
+
+Q8, Q4 = oracle.Q8_0, oracle.Q4_0
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+# ── the reference's own unit tests (tests/test_quantize.cpp:7-50) ─────────
+def test_reference_unit_cases(oracle_lib):
+    u = np.load(os.path.join(GOLDEN, "ref_unit_cases.npz"))
+    q8 = oracle_lib.quantize(Q8, u["data"], 8)
+    q4 = oracle_lib.quantize(Q4, u["data"], 8)
+    assert q8.tobytes() == u["q8"].tobytes()
+    assert q4.tobytes() == u["q4"].tobytes()
+    d8 = oracle_lib.dequantize_block(Q8, q8, 8)
+    d4 = oracle_lib.dequantize_block(Q4, q4, 8)
+    assert d8.tobytes() == u["q8_deq"].tobytes()
+    assert d4.tobytes() == u["q4_deq"].tobytes()
+    # The reference's own tolerances (test_quantize.cpp:20, :35, :48).
+    assert np.all(np.abs(d8 - u["data"]) <= 0.02)
+    assert np.all(np.abs(d4 - u["data"]) <= 0.3)
+    qa = oracle_lib.quantize(Q8, u["dot_a"], 4)
+    assert qa.tobytes() == u["dot_q8"].tobytes()
+    r = oracle_lib.dot(Q8, qa, u["dot_b"], 4, 4)
+    assert np.float32(r).tobytes() == u["dot_result"].tobytes()
+    assert abs(r - 5.0) <= 0.1
+
+
+# ── seeded small cases: bytes, outputs and per-block partials bit-exact ──
+def test_small_cases_bit_exact(oracle_lib, small_cases):
+    for i, c in enumerate(small_cases):
+        dt, bs, n, k = c["dtype"], c["bs"], c["n"], c["k"]
+        if "w" in c:
+            q = oracle_lib.quantize_rows(dt, c["w"], bs)
+            assert q.tobytes() == c["q"].tobytes(), f"case {i}: quantized bytes differ"
+        y = oracle_lib.matmul(dt, c["q"], n, k, c["x"], bs)
+        assert y.tobytes() == c["y"].tobytes(), f"case {i}: y differs"
+        p = oracle_lib.block_partials(dt, c["q"], n, k, c["x"][0], bs)
+        assert p.tobytes() == c["partials"].tobytes(), f"case {i}: partials differ"
+
+
+def test_unknown_dtype_zero_fills(oracle_lib):
+    # dispatch_matvec_q zero-fills y for a dtype it has no kernel for (backend.cpp:195-198).
+    y = oracle_lib.matvec(30, np.zeros(64, np.uint8), 4, 32, np.ones(32, np.float32))
+    assert np.all(y == 0)
+
+
+def test_fp16_truncating_encoder(oracle_lib):
+    # fp32_to_fp16 truncates (dtype.cpp:52): 1 + 2^-11 + 2^-12 rounds down, not up.
+    assert oracle_lib.fp32_to_fp16(1.0 + 2.0 ** -11 + 2.0 ** -12) == 0x3C00
+    assert oracle_lib.fp32_to_fp16(float("nan")) == 0x7C00            # NaN -> inf
+    assert oracle_lib.fp32_to_fp16(1e-5) == 0x0000                    # below 2^-14 -> 0
+    assert oracle_lib.fp32_to_fp16(-65520.0) == 0xFBFF                # truncation keeps it finite
+    assert oracle_lib.fp16_to_fp32(0x0001) == 2.0 ** -24              # subnormal decode is exact
+
+
+# ── full-size configuration digests (the cheap ones run here) ────────────
+@pytest.mark.parametrize("name", ["cfg1_q8_4096x4096", "cfg2_q4_4096x4096", "cfg3_q8_kv", "cfg3_q8_qo"])
+def test_config_digests_oracle(oracle_lib, digests, name):
+    import qraf_b200
+
+    d = digests[name]
+    w = qraf_b200.fill_normal(d["seed_w"], 0.0, 0.02, d["n"] * d["k"])
+    q = oracle_lib.quantize(d["dtype"], w, d["block_size"])
+    assert sha(q) == d["sha_q"]
+    x = qraf_b200.fill_normal(d["seed_x"], 0.0, 1.0, d["k"])
+    y = oracle_lib.matvec(d["dtype"], q, d["n"], d["k"], x, d["block_size"])
+    assert sha(y[None, :]) == d["y"]["1"]
+
+
+# ── direct cross-check with the reference's compiled code, where built ────
+@pytest.mark.skipif(not oracle.reference_available(), reason="oracle/_ref not built here")
+def test_oracle_matches_reference_randomised(oracle_lib):
+    ref = oracle.Reference()
+    rng = np.random.default_rng(7)
+    for trial in range(60):
+        dt = (Q8, Q4)[trial % 2]
+        bs = int(rng.choice([1, 2, 3, 4, 7, 8, 16, 32, 33, 64]))
+        if dt == Q4 and bs < 2:
+            bs = 2
+        n, k = int(rng.integers(1, 9)), int(rng.integers(1, 300))
+        w = (rng.standard_normal((n, k)) * 10.0 ** rng.integers(-6, 4)).astype(np.float32)
+        x = rng.standard_normal(k).astype(np.float32)
+        qa, qb = oracle_lib.quantize_rows(dt, w, bs), ref.quantize_rows(dt, w, bs)
+        assert qa.tobytes() == qb.tobytes()
+        assert oracle_lib.matvec(dt, qa, n, k, x, bs).tobytes() == ref.matvec(dt, qb, n, k, x, bs).tobytes()
+    for h in range(0, 65536, 7):
+        a = np.float32(oracle_lib.fp16_to_fp32(h))
+        b = np.float32(ref.lib.qref_fp16_to_fp32(h))
+        assert a.tobytes() == b.tobytes() or (np.isnan(a) and np.isnan(b))
