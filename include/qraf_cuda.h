@@ -49,6 +49,12 @@ extern "C" {
 #define QRAF_MODE_FAST  1  /* fused multiply-add, reordered sums; allclose(rtol 1e-5, atol 1e-6) */
 #define QRAF_MODE_TC    2  /* tensor-core tile for M >= 16; same tolerance as FAST */
 #define QRAF_MODE_AUTO  3  /* FAST below M = 16, TC from M = 16 */
+/* Or-able flag: the kernel may start while the previous kernel in the stream is
+ * still running and fetch the weight before waiting for it (programmatic
+ * dependent launch).  Only valid when that previous kernel does not write the
+ * weight - true for model weights in a decode loop.  Activations are always
+ * read after the wait. */
+#define QRAF_MODE_FLAG_OVERLAP 0x100
 
 /* A quantized weight on one device: a plain descriptor, no hidden state. */
 typedef struct qraf_weight {

@@ -27,6 +27,7 @@ MODE_EXACT = 0
 MODE_FAST = 1
 MODE_TC = 2
 MODE_AUTO = 3
+MODE_FLAG_OVERLAP = 0x100
 
 OK = 0
 ERR_INVALID = 1

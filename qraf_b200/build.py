@@ -16,7 +16,10 @@ LIB = os.path.join(PKG, "libqraf_cuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+# -fmad=false: no multiply/add pair is ever contracted into an FMA.  The EXACT
+# kernels depend on separately rounded products and sums (the reference's x86
+# order); every FMA the FAST kernels want is written explicitly.
+CUDA_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               "--expt-relaxed-constexpr"]
 
 

@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "matvec_generic.cuh"
+#include "matvec_rows.cuh"
 #include "matvec_stream.cuh"
 #include "quantize.cuh"
 
@@ -87,6 +88,12 @@ int ensure_device(int* dev_out, DeviceInfo** info_out) {
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 1>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 2>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 4>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, true, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, true, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2>, lim));
         d.ready = true;
     }
     if (dev_out) *dev_out = dev;
@@ -168,6 +175,95 @@ bool plan_stream(const qraf_weight_t& w, const float* x, float* y, uint32_t M, b
     return true;
 }
 
+// ── row-owner kernel plan (M = 1 or 2 FAST; any M EXACT) ─────────────────
+struct RowPlan {
+    RowParams p;
+    int grid = 0;
+    size_t smem = 0;
+};
+
+constexpr int kPdlSmemBudget = 227 * 1024;   // one CTA per SM: use the whole shared memory
+
+bool rows_eligible(const qraf_weight_t& w, const float* x) {
+    return w.block_size == 32 && (w.cols % 32) == 0 && w.cols > 0 && (w.row_bytes % 16) == 0 && aligned16(w.data) &&
+           aligned16(x);
+}
+
+// Plan one launch over `mcount` activation vectors.  Returns false when the
+// staged activations do not fit in shared memory.
+bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount, bool exact, const DeviceInfo& dev,
+               RowPlan* out) {
+    const uint32_t nblk = w.cols / 32;
+    const uint64_t rb = w.row_bytes;
+    uint32_t G = static_cast<uint32_t>(std::max<uint64_t>(1, (10240 + rb / 2) / rb));
+    G = std::min<uint32_t>(G, kRowGMax);
+    const uint32_t grid = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), w.rows);
+    const uint32_t rows_base = w.rows / grid, rows_extra = w.rows % grid;
+    const uint32_t max_rows = rows_base + (rows_extra ? 1u : 0u);
+    G = std::min(G, max_rows);
+    const uint32_t slot_stride = static_cast<uint32_t>((G * rb + 127) / 128 * 128);
+    const uint64_t x_bytes = static_cast<uint64_t>(mcount) * nblk * 144u;
+    const uint32_t pb_row = nblk + 4;
+    const uint64_t pb_bytes = exact ? static_cast<uint64_t>(kRowWarps) * G * pb_row * 4u : 0;
+    const uint32_t stages = (max_rows + G - 1) / G;
+    const uint64_t fixed = x_bytes + pb_bytes + 64;
+    auto fit = [&](uint64_t budget) -> uint32_t {
+        if (budget <= fixed) return 0;
+        return static_cast<uint32_t>(std::min<uint64_t>({32u, stages, (budget - fixed) / (slot_stride + 12u)}));
+    };
+    const uint32_t nst = fit(std::min<uint64_t>(kPdlSmemBudget, static_cast<uint64_t>(dev.smem_optin - kSmemReserve)));
+    if (nst == 0) return false;
+    RowParams& p = out->p;
+    p.w = static_cast<const uint8_t*>(w.data);
+    p.x = x;
+    p.y = y;
+    p.row_bytes = rb;
+    p.N = w.rows;
+    p.K = w.cols;
+    p.M = mcount;
+    p.nblk = nblk;
+    p.nchunk = (nblk + 31) / 32;
+    p.G = G;
+    p.nst = nst;
+    p.slot_stride = slot_stride;
+    p.xs_stride = nblk * 36u;
+    p.pb_row = pb_row;
+    p.rows_base = rows_base;
+    p.rows_extra = rows_extra;
+    p.pdl = 0;
+    out->grid = static_cast<int>(grid);
+    out->smem = static_cast<size_t>(nst) * slot_stride + fixed + nst * 12u;
+    return true;
+}
+
+template <typename Kern>
+cudaError_t launch_ex(Kern kernel, int grid, int threads, size_t smem, cudaStream_t st, bool pdl, const RowParams& p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+cudaError_t launch_rows(uint32_t dtype, const RowPlan& pl, bool exact, int MT, bool pdl, cudaStream_t st) {
+    RowParams p = pl.p;
+    p.pdl = pdl ? 1u : 0u;
+    if (dtype == QRAF_DTYPE_Q8_0) {
+        if (exact) return launch_ex(qmv_rows_kernel<kDtypeQ8, true, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+        if (MT == 1) return launch_ex(qmv_rows_kernel<kDtypeQ8, false, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+        return launch_ex(qmv_rows_kernel<kDtypeQ8, false, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    }
+    if (exact) return launch_ex(qmv_rows_kernel<kDtypeQ4, true, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    if (MT == 1) return launch_ex(qmv_rows_kernel<kDtypeQ4, false, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    return launch_ex(qmv_rows_kernel<kDtypeQ4, false, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+}
+
 template <uint32_t DT>
 cudaError_t launch_stream(const StreamPlan& pl, bool exact, cudaStream_t st) {
     if (exact) {
@@ -204,41 +300,53 @@ int check_weight(const qraf_weight_t* w) {
     return QRAF_OK;
 }
 
-int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode, cudaStream_t st) {
+int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode_in, cudaStream_t st) {
     int rc = check_weight(w);
     if (rc) return rc;
+    const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
+    int mode = mode_in & 0xFF;
     if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
     if (mode == QRAF_MODE_TC) return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core tile is not built in this library");
-    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_INVALID, "unknown mode %d", mode);
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
     if (M == 0 || w->rows == 0) return QRAF_OK;
-    if (!x || !y) return fail(QRAF_ERR_INVALID, "x or y is NULL");
-    if (w->cols == 0) {
+    if (!y) return fail(QRAF_ERR_INVALID, "y is NULL");
+    if (w->cols == 0) {   // an empty dot is 0 (quantize.cpp:189-209 with no blocks); x is not read
         QRAF_CUDA_TRY(cudaMemsetAsync(y, 0, static_cast<size_t>(M) * w->rows * sizeof(float), st));
         return QRAF_OK;
     }
+    if (!x) return fail(QRAF_ERR_INVALID, "x is NULL");
     DeviceInfo* dev = nullptr;
     rc = ensure_device(nullptr, &dev);
     if (rc) return rc;
     const bool exact = (mode == QRAF_MODE_EXACT);
 
-    // Streaming kernel where the layout allows it.
-    StreamPlan pl;
-    if (exact) {
-        if (plan_stream(*w, x, y, 1, true, 1, *dev, &pl)) {
-            for (uint32_t m = 0; m < M; ++m) {
-                pl.p.x = x + static_cast<size_t>(m) * w->cols;
-                pl.p.y = y + static_cast<size_t>(m) * w->rows;
-                const cudaError_t e = (w->dtype == QRAF_DTYPE_Q8_0) ? launch_stream<kDtypeQ8>(pl, true, st)
-                                                                     : launch_stream<kDtypeQ4>(pl, true, st);
-                if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "stream kernel launch: %s", cudaGetErrorString(e));
+    // Row-owner streaming kernel: EXACT for any M (vectors in groups that fit in
+    // shared memory), FAST for one or two vectors.
+    if (rows_eligible(*w, x) && (exact || M <= 2)) {
+        uint32_t per = M;
+        RowPlan pl;
+        while (per > 1 && !plan_rows(*w, x, y, per, exact, *dev, &pl)) per = (per + 1) / 2;
+        if (plan_rows(*w, x, y, per, exact, *dev, &pl)) {
+            for (uint32_t m0 = 0; m0 < M; m0 += per) {
+                const uint32_t cnt = std::min(per, M - m0);
+                RowPlan one = pl;
+                one.p.x = x + static_cast<size_t>(m0) * w->cols;
+                one.p.y = y + static_cast<size_t>(m0) * w->rows;
+                one.p.M = cnt;
+                const int MT = exact ? 1 : static_cast<int>(cnt);
+                const cudaError_t e = launch_rows(w->dtype, one, exact, MT, overlap, st);
+                if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "row kernel launch: %s", cudaGetErrorString(e));
             }
             return QRAF_OK;
         }
-    } else {
+    }
+
+    // K-split streaming kernel: FAST for three or more vectors.
+    StreamPlan pl;
+    if (!exact) {
         int MT = (M == 1) ? 1 : (M == 2 ? 2 : 4);
         bool ok = plan_stream(*w, x, y, M, false, MT, *dev, &pl);
         if (!ok && MT == 4) ok = plan_stream(*w, x, y, M, false, MT = 2, *dev, &pl);
-        if (!ok && MT == 2 && M == 2) ok = false;
         if (ok) {
             const cudaError_t e = (w->dtype == QRAF_DTYPE_Q8_0) ? launch_stream<kDtypeQ8>(pl, false, st)
                                                                  : launch_stream<kDtypeQ4>(pl, false, st);

@@ -108,38 +108,13 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 }
 
 // ── packed fp32x2 arithmetic (sm_100a), IEEE round-to-nearest, no ftz ────
-__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "add.rn.f32x2 rd, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-
-__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-
-__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-        "mov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
+// CUDA's float2 intrinsics.  Used where rounding order is free (FAST mode):
+// a packed multiply followed by a packed add was measured to round like a
+// fused multiply-add on sm_100a, so EXACT code uses the scalar __fmul_rn /
+// __fadd_rn forms instead.
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // ── integer -> float without the conversion unit ──────────────────────────
 // A byte u placed in the low mantissa bits of 2^23 gives the float 2^23 + u
@@ -166,6 +141,28 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
     return v;
+}
+
+// ── block loaders (shared memory -> registers) ────────────────────────────
+// Q8: 9 words; word 0 = fp32 scale, words 1..8 = 32 int8 codes.
+__device__ __forceinline__ void load_q8_block(const uint8_t* row, uint32_t b, uint32_t (&wv)[9]) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(row + 36u * b);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wv[i] = p[i];
+}
+
+// Q4: the 18-byte block starts on a 4-byte boundary for even b and 2 bytes
+// past one for odd b.  Read the 5 aligned words covering it and funnel-shift
+// the codes into 4 words; `scale16` gets the fp16 scale bits.
+__device__ __forceinline__ void load_q4_block(const uint8_t* row, uint32_t b, uint32_t (&qw)[4], uint32_t& scale16) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(row) + ((9u * b) >> 1);
+    uint32_t w[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) w[i] = p[i];
+    const uint32_t sh = (b & 1u) ? 32u : 16u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qw[j] = __funnelshift_rc(w[j], w[j + 1], sh);
+    scale16 = __funnelshift_rc(w[0], w[1], sh - 16u) & 0xFFFFu;
 }
 
 __device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {

@@ -56,45 +56,29 @@ struct StreamTraits {
     static constexpr int kMaxThreads = (kMaxConsumerWarps + 1) * 32;
 };
 
-// ── block loaders (shared memory -> registers) ────────────────────────────
-// Q8: 9 words; word 0 = fp32 scale, words 1..8 = 32 int8 codes.
-__device__ __forceinline__ void load_q8_block(const uint8_t* row, uint32_t b, uint32_t (&wv)[9]) {
-    const uint32_t* p = reinterpret_cast<const uint32_t*>(row + 36u * b);
-#pragma unroll
-    for (int i = 0; i < 9; ++i) wv[i] = p[i];
-}
-
-// Q4: the 18-byte block starts on a 4-byte boundary for even b and 2 bytes
-// past one for odd b.  Read the 5 aligned words covering it and funnel-shift
-// the codes into 4 words; `scale16` gets the fp16 scale bits.
-__device__ __forceinline__ void load_q4_block(const uint8_t* row, uint32_t b, uint32_t (&qw)[4], uint32_t& scale16) {
-    const uint32_t* p = reinterpret_cast<const uint32_t*>(row) + ((9u * b) >> 1);
-    uint32_t w[5];
-#pragma unroll
-    for (int i = 0; i < 5; ++i) w[i] = p[i];
-    const uint32_t sh = (b & 1u) ? 32u : 16u;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) qw[j] = __funnelshift_rc(w[j], w[j + 1], sh);
-    scale16 = __funnelshift_rc(w[0], w[1], sh - 16u) & 0xFFFFu;
-}
-
 // ── per-block arithmetic, two rows at a time ──────────────────────────────
 // EXACT: fl(block_sum) chain then fl(block_sum * scale), as quantize.cpp:201-205.
+// Scalar __fmul_rn / __fadd_rn on purpose: on sm_100a with CUDA 12.9, packed
+// fp32x2 multiply-then-add sequences (inline add/mul.rn.f32x2 or the
+// __fmul2_rn / __fadd2_rn intrinsics) came out as fused multiply-adds, measured
+// against the oracle; the scalar forms are never fused.  Two rows are still
+// interleaved for instruction-level parallelism.
 __device__ __forceinline__ float2 q8_pair_exact(const uint32_t (&wa)[9], const uint32_t (&wb)[9], const float (&xr)[32]) {
-    const float2 negc = make_float2(-kMagicQ8, -kMagicQ8);
-    float2 acc = make_float2(0.0f, 0.0f);
+    float acca = 0.0f, accb = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint32_t ua = wa[1 + j] ^ 0x80808080u;
         const uint32_t ub = wb[1 + j] ^ 0x80808080u;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            const float2 q = f2_add(make_float2(magic_byte(ua, t), magic_byte(ub, t)), negc);
+            const float qa = magic_byte(ua, t) - kMagicQ8;   // exact small integer
+            const float qb = magic_byte(ub, t) - kMagicQ8;
             const float xv = xr[4 * j + t];
-            acc = f2_add(acc, f2_mul(q, make_float2(xv, xv)));
+            acca = __fadd_rn(acca, __fmul_rn(qa, xv));
+            accb = __fadd_rn(accb, __fmul_rn(qb, xv));
         }
     }
-    return f2_mul(acc, make_float2(__uint_as_float(wa[0]), __uint_as_float(wb[0])));
+    return make_float2(__fmul_rn(acca, __uint_as_float(wa[0])), __fmul_rn(accb, __uint_as_float(wb[0])));
 }
 
 __device__ __forceinline__ float2 q8_pair_fast(const uint32_t (&wa)[9], const uint32_t (&wb)[9], const float (&xr)[32]) {
@@ -119,22 +103,21 @@ __device__ __forceinline__ float2 q8_pair_fast(const uint32_t (&wa)[9], const ui
 // and 2t+1 (high nibble); word j covers elements 8j .. 8j+7 (quantize.cpp:227-233).
 __device__ __forceinline__ float2 q4_pair_exact(const uint32_t (&qa)[4], uint32_t sa, const uint32_t (&qb)[4], uint32_t sb,
                                                 const float (&xr)[32]) {
-    const float2 negc = make_float2(-kMagicQ4, -kMagicQ4);
-    float2 acc = make_float2(0.0f, 0.0f);
+    float acca = 0.0f, accb = 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t loa = qa[j] & 0x0F0F0F0Fu, hia = (qa[j] >> 4) & 0x0F0F0F0Fu;
         const uint32_t lob = qb[j] & 0x0F0F0F0Fu, hib = (qb[j] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            const float2 q0 = f2_add(make_float2(magic_byte(loa, t), magic_byte(lob, t)), negc);
-            const float2 q1 = f2_add(make_float2(magic_byte(hia, t), magic_byte(hib, t)), negc);
             const float x0 = xr[8 * j + 2 * t], x1 = xr[8 * j + 2 * t + 1];
-            acc = f2_add(acc, f2_mul(q0, make_float2(x0, x0)));
-            acc = f2_add(acc, f2_mul(q1, make_float2(x1, x1)));
+            acca = __fadd_rn(acca, __fmul_rn(magic_byte(loa, t) - kMagicQ4, x0));
+            accb = __fadd_rn(accb, __fmul_rn(magic_byte(lob, t) - kMagicQ4, x0));
+            acca = __fadd_rn(acca, __fmul_rn(magic_byte(hia, t) - kMagicQ4, x1));
+            accb = __fadd_rn(accb, __fmul_rn(magic_byte(hib, t) - kMagicQ4, x1));
         }
     }
-    return f2_mul(acc, make_float2(half_bits_to_float(sa), half_bits_to_float(sb)));
+    return make_float2(__fmul_rn(acca, half_bits_to_float(sa)), __fmul_rn(accb, half_bits_to_float(sb)));
 }
 
 __device__ __forceinline__ float2 q4_pair_fast(const uint32_t (&qa)[4], uint32_t sa, const uint32_t (&qb)[4], uint32_t sb,
