@@ -88,12 +88,16 @@ int ensure_device(int* dev_out, DeviceInfo** info_out) {
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 1>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 2>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_stream_kernel<kDtypeQ4, false, 4>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, true, 1>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 1>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 2>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, true, 1>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1>, lim));
-        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, true, 1, 0>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, true, 1, 0>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 1, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 1, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 1, 4>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ8, false, 2, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 1>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 4>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2, 2>, lim));
         d.ready = true;
     }
     if (dev_out) *dev_out = dev;
@@ -195,14 +199,17 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
                RowPlan* out) {
     const uint32_t nblk = w.cols / 32;
     const uint64_t rb = w.row_bytes;
-    uint32_t G = static_cast<uint32_t>(std::max<uint64_t>(1, (10240 + rb / 2) / rb));
-    G = std::min<uint32_t>(G, kRowGMax);
     const uint32_t grid = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), w.rows);
     const uint32_t rows_base = w.rows / grid, rows_extra = w.rows % grid;
     const uint32_t max_rows = rows_base + (rows_extra ? 1u : 0u);
-    G = std::min(G, max_rows);
+    // Rows per stage: enough stages to keep all warps busy, then as many rows as
+    // fit ~18 KB (more rows share each staged activation block).
+    uint32_t G = 1;
+    while (G < kRowGMax && (2 * G) * rb <= 18432 && 5 * ((max_rows + 2 * G - 1) / (2 * G)) >= 4 * kRowWarps) G *= 2;
+    if (!exact && mcount == 2) G = 2;
     const uint32_t slot_stride = static_cast<uint32_t>((G * rb + 127) / 128 * 128);
-    const uint64_t x_bytes = static_cast<uint64_t>(mcount) * nblk * 144u;
+    const uint32_t rec = exact ? 144u : kLimbRec;      // bytes per staged 32-element block
+    const uint64_t x_bytes = static_cast<uint64_t>(mcount) * nblk * rec;
     const uint32_t pb_row = nblk + 4;
     const uint64_t pb_bytes = exact ? static_cast<uint64_t>(kRowWarps) * G * pb_row * 4u : 0;
     const uint32_t stages = (max_rows + G - 1) / G;
@@ -226,7 +233,7 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.G = G;
     p.nst = nst;
     p.slot_stride = slot_stride;
-    p.xs_stride = nblk * 36u;
+    p.xs_stride = nblk * rec;
     p.pb_row = pb_row;
     p.rows_base = rows_base;
     p.rows_extra = rows_extra;
@@ -251,17 +258,20 @@ cudaError_t launch_ex(Kern kernel, int grid, int threads, size_t smem, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
+template <uint32_t DT>
+cudaError_t launch_rows_dt(const RowPlan& pl, const RowParams& p, bool exact, int MT, bool pdl, cudaStream_t st) {
+    if (exact) return launch_ex(qmv_rows_kernel<DT, true, 1, 0>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    if (MT == 2) return launch_ex(qmv_rows_kernel<DT, false, 2, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    if (p.G == 1) return launch_ex(qmv_rows_kernel<DT, false, 1, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    if (p.G == 2) return launch_ex(qmv_rows_kernel<DT, false, 1, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    return launch_ex(qmv_rows_kernel<DT, false, 1, 4>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+}
+
 cudaError_t launch_rows(uint32_t dtype, const RowPlan& pl, bool exact, int MT, bool pdl, cudaStream_t st) {
     RowParams p = pl.p;
     p.pdl = pdl ? 1u : 0u;
-    if (dtype == QRAF_DTYPE_Q8_0) {
-        if (exact) return launch_ex(qmv_rows_kernel<kDtypeQ8, true, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
-        if (MT == 1) return launch_ex(qmv_rows_kernel<kDtypeQ8, false, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
-        return launch_ex(qmv_rows_kernel<kDtypeQ8, false, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
-    }
-    if (exact) return launch_ex(qmv_rows_kernel<kDtypeQ4, true, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
-    if (MT == 1) return launch_ex(qmv_rows_kernel<kDtypeQ4, false, 1>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
-    return launch_ex(qmv_rows_kernel<kDtypeQ4, false, 2>, pl.grid, kRowThreads, pl.smem, st, pdl, p);
+    return dtype == QRAF_DTYPE_Q8_0 ? launch_rows_dt<kDtypeQ8>(pl, p, exact, MT, pdl, st)
+                                    : launch_rows_dt<kDtypeQ4>(pl, p, exact, MT, pdl, st);
 }
 
 template <uint32_t DT>

@@ -63,7 +63,7 @@ struct RowParams {
     uint32_t G;              // rows per stage (1..kRowGMax)
     uint32_t nst;            // slots in the ring
     uint32_t slot_stride;    // bytes per slot (multiple of 128)
-    uint32_t xs_stride;      // floats per staged activation vector = nblk * 36
+    uint32_t xs_stride;      // bytes per staged activation vector: nblk * 144 (EXACT), nblk * kLimbRec (FAST)
     uint32_t pb_row;         // EXACT: floats per row of the per-warp partial buffer
     uint32_t rows_base, rows_extra;
     uint32_t pdl;            // 1: programmatic dependent launch protocol
@@ -93,48 +93,157 @@ __device__ __forceinline__ void lds_x_block(const float* xs, uint32_t b, float4 
     for (int i = 0; i < 8; ++i) xv[i] = p[i];
 }
 
-// ── FAST block dots: returns the block's sum (before its scale) ──────────
-__device__ __forceinline__ float q8_block_fast(const uint32_t (&wv)[9], const float4 (&xv)[8]) {
-    const float2 negc = make_float2(-kMagicQ8, -kMagicQ8);
-    float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t u = wv[1 + j] ^ 0x80808080u;
-        const float2 q01 = f2_add(make_float2(magic_byte(u, 0), magic_byte(u, 1)), negc);
-        const float2 q23 = f2_add(make_float2(magic_byte(u, 2), magic_byte(u, 3)), negc);
-        a0 = f2_fma(q01, make_float2(xv[j].x, xv[j].y), a0);
-        a1 = f2_fma(q23, make_float2(xv[j].z, xv[j].w), a1);
-    }
-    const float2 s = f2_add(a0, a1);
-    return s.x + s.y;
-}
+// ── FAST: activations as integer limbs, codes used as they are ───────────
+// Per 32-element block b of an activation vector, with e_b the exponent of
+// max |x| (max |x| < 2^e_b):  X_i = rint(x_i * 2^(27 - e_b)), |X_i| < 2^27, and
+// X_i = L0*2^21 + L1*2^14 + L2*2^7 + L3 with signed digits |L_j| <= 127.
+// Then sum_i q_i x_i ~= 2^(e_b - 27) * sum_j 2^(7(3-j)) * D_j,  D_j = sum_i q_i L_ji,
+// where every D_j is an exact int32 (dp4a), so the per-block partial sums are
+// integers independent of summation order; the only roundings are X_i (a
+// relative error below 2^-27 of the block maximum) and the fp32 combination.
+// Record of one block in shared memory (kLimbRec bytes): limb plane j at
+// bytes [32j, 32j+32), c_b = 2^(e_b - 27) at 128, the plane sums S_j (int32) at
+// 144..159 (Q4 only), padding to an odd number of 16-byte units so that lanes
+// reading consecutive blocks hit distinct banks.
+// Q4 stores the elements of each group of 8 in the order 0,2,4,6,1,3,5,7 so
+// that the low and high nibbles of a code word line up with one limb word.
+constexpr uint32_t kLimbRec = 176;
 
-// Q4 FAST: x was staged as x * 16^-(e % 4).  Word j holds elements 8j..8j+7;
-// element e sits at bit 4*(e % 8) of the word, i.e. at bit 4*(e % 4) of the
-// word (e % 8 < 4) or of the word shifted right by 16 (e % 8 >= 4).
-__device__ __forceinline__ float q4_block_fast(const uint32_t (&qw)[4], const float4 (&xv)[8]) {
-    const float2 c01 = make_float2(-8388616.0f, -8388736.0f);     // -(2^23 + 8), -(2^23 + 128)
-    const float2 c23 = make_float2(-8390656.0f, -8421376.0f);     // -(2^23 + 2048), -(2^23 + 32768)
-    float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
+struct LimbBlock {
+    uint32_t L[4][8];   // limb words, plane j, 4 elements per word
+};
+
+__device__ __forceinline__ void lds_limbs(const uint8_t* rec, LimbBlock& lb) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = qw[j], hi = qw[j] >> 16;
-        const float2 q01 = f2_add(make_float2(__uint_as_float((lo & 0x000Fu) | kMagicBits),
-                                              __uint_as_float((lo & 0x00F0u) | kMagicBits)), c01);
-        const float2 q23 = f2_add(make_float2(__uint_as_float((lo & 0x0F00u) | kMagicBits),
-                                              __uint_as_float((lo & 0xF000u) | kMagicBits)), c23);
-        const float2 q45 = f2_add(make_float2(__uint_as_float((hi & 0x000Fu) | kMagicBits),
-                                              __uint_as_float((hi & 0x00F0u) | kMagicBits)), c01);
-        const float2 q67 = f2_add(make_float2(__uint_as_float((hi & 0x0F00u) | kMagicBits),
-                                              __uint_as_float((hi & 0xF000u) | kMagicBits)), c23);
-        const float4 xa = xv[2 * j], xb = xv[2 * j + 1];
-        a0 = f2_fma(q01, make_float2(xa.x, xa.y), a0);
-        a1 = f2_fma(q23, make_float2(xa.z, xa.w), a1);
-        a0 = f2_fma(q45, make_float2(xb.x, xb.y), a0);
-        a1 = f2_fma(q67, make_float2(xb.z, xb.w), a1);
+        const uint4 a = *reinterpret_cast<const uint4*>(rec + 32 * j);
+        const uint4 b = *reinterpret_cast<const uint4*>(rec + 32 * j + 16);
+        lb.L[j][0] = a.x; lb.L[j][1] = a.y; lb.L[j][2] = a.z; lb.L[j][3] = a.w;
+        lb.L[j][4] = b.x; lb.L[j][5] = b.y; lb.L[j][6] = b.z; lb.L[j][7] = b.w;
     }
-    const float2 s = f2_add(a0, a1);
-    return s.x + s.y;
+}
+
+// sum_j 2^(7(3-j)) D_j as fp32 (D0*128 + D1 and D2*128 + D3 are exact int32).
+__device__ __forceinline__ float combine_limbs(int d0, int d1, int d2, int d3) {
+    return fmaf(__int2float_rn(d0 * 128 + d1), 16384.0f, __int2float_rn(d2 * 128 + d3));
+}
+
+__device__ __forceinline__ float q8_block_limb(const uint32_t (&wv)[9], const LimbBlock& lb) {
+    int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        const int q = static_cast<int>(wv[1 + w]);
+        d0 = __dp4a(q, static_cast<int>(lb.L[0][w]), d0);
+        d1 = __dp4a(q, static_cast<int>(lb.L[1][w]), d1);
+        d2 = __dp4a(q, static_cast<int>(lb.L[2][w]), d2);
+        d3 = __dp4a(q, static_cast<int>(lb.L[3][w]), d3);
+    }
+    return combine_limbs(d0, d1, d2, d3);
+}
+
+// Q4: nibbles (0..15, the +8-biased codes) are exact as signed bytes; the bias
+// is removed with the plane sums: sum (nib - 8) L = sum nib L - 8 S.
+__device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const LimbBlock& lb, const int4 S) {
+    int d0 = -8 * S.x, d1 = -8 * S.y, d2 = -8 * S.z, d3 = -8 * S.w;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const int lo = static_cast<int>(qw[w] & 0x0F0F0F0Fu);          // elements 8w + 0, 2, 4, 6
+        const int hi = static_cast<int>((qw[w] >> 4) & 0x0F0F0F0Fu);   // elements 8w + 1, 3, 5, 7
+        d0 = __dp4a(lo, static_cast<int>(lb.L[0][2 * w]), d0);
+        d1 = __dp4a(lo, static_cast<int>(lb.L[1][2 * w]), d1);
+        d2 = __dp4a(lo, static_cast<int>(lb.L[2][2 * w]), d2);
+        d3 = __dp4a(lo, static_cast<int>(lb.L[3][2 * w]), d3);
+        d0 = __dp4a(hi, static_cast<int>(lb.L[0][2 * w + 1]), d0);
+        d1 = __dp4a(hi, static_cast<int>(lb.L[1][2 * w + 1]), d1);
+        d2 = __dp4a(hi, static_cast<int>(lb.L[2][2 * w + 1]), d2);
+        d3 = __dp4a(hi, static_cast<int>(lb.L[3][2 * w + 1]), d3);
+    }
+    return combine_limbs(d0, d1, d2, d3);
+}
+
+// Turn the staged fp32 activations into limb records, in place: on entry
+// bytes [0, 128) of every record hold the block's 32 floats.  Four threads per
+// block, eight elements each (elements 8*sub .. 8*sub+7, which for Q4 is exactly
+// one group of 8 in the 0,2,4,6,1,3,5,7 order), all of a CTA's blocks in one or
+// a few rounds; the group's maximum and plane sums need two shuffles each.
+template <uint32_t DT>
+__device__ __forceinline__ void stage_limb_records(uint8_t* xsb, uint32_t xs_stride, uint32_t M, uint32_t nblk,
+                                                   uint32_t tid, uint32_t nthreads) {
+    const uint32_t lane = tid & 31u, sub = lane & 3u;
+    const uint32_t total = M * nblk * 4u;
+    for (uint32_t base = tid - lane; base < total; base += nthreads) {
+        const uint32_t task = base + lane;
+        const bool act = task < total;
+        const uint32_t blk = act ? task >> 2 : 0u;
+        uint8_t* rec = xsb + static_cast<size_t>(blk / nblk) * xs_stride + kLimbRec * (blk % nblk);
+        float xv[8];
+        {
+            const float4 a = *reinterpret_cast<const float4*>(rec + 32u * sub);
+            const float4 b = *reinterpret_cast<const float4*>(rec + 32u * sub + 16u);
+            xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+        }
+        __syncwarp();                       // all reads of the raw floats precede the limb writes
+        float amax = 0.0f;
+        uint32_t bad = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            amax = fmaxf(amax, fabsf(xv[i]));
+            bad |= isfinite(xv[i]) ? 0u : 1u;
+        }
+        if (!act) { amax = 0.0f; bad = 0u; }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+        }
+        // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
+        // bits when both are normal floats, else by ldexpf.
+        const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
+        const bool live = amax > 0.0f && !bad;
+        int e = 0;
+        float up = 0.0f, cb = 0.0f;
+        bool slow = false;
+        if (live) {
+            if (ebits >= 29u) {
+                e = static_cast<int>(ebits) - 126;
+                up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
+                cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
+            } else {
+                frexpf(amax, &e);
+                slow = true;
+                cb = ldexpf(1.0f, e - 27);
+            }
+        }
+        uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+        int S[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
+            const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
+            const int sg = X < 0 ? -1 : 1;
+            const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
+                              sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
+            // byte position of element i inside this thread's 8 bytes of each plane
+            const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
+                S[j] += L[j];
+            }
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
+        if (act) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
+            if (sub == 0) {
+                *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
+                *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
+            }
+        }
+    }
 }
 
 // ── EXACT block dots: the reference's order, scalar, never fused ─────────
@@ -170,15 +279,18 @@ __device__ __forceinline__ float q4_block_exact(const uint32_t (&qw)[4], uint32_
 }
 
 // ── the kernel ────────────────────────────────────────────────────────────
-template <uint32_t DT, bool EXACT, int MT>
+// GT: rows per stage, fixed at compile time for FAST (1, 2 or 4; a short last
+// stage recomputes its last row instead of branching); 0 for EXACT (runtime p.G).
+template <uint32_t DT, bool EXACT, int MT, int GT>
 __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParams p) {
     static_assert(MT == 1 || MT == 2, "one or two activation vectors per pass");
+    static_assert(EXACT ? GT == 0 : (GT == 1 || GT == 2 || GT == 4), "rows per stage");
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t nst = p.nst;
     uint8_t* slots = smem;
-    float* xs = reinterpret_cast<float*>(smem + static_cast<size_t>(nst) * p.slot_stride);
-    float* pbuf = xs + static_cast<size_t>(p.M) * p.xs_stride;                          // EXACT only
+    uint8_t* xsb = smem + static_cast<size_t>(nst) * p.slot_stride;                     // staged activations
+    float* pbuf = reinterpret_cast<float*>(xsb + static_cast<size_t>(p.M) * p.xs_stride);   // EXACT only
     uint64_t* full = reinterpret_cast<uint64_t*>(
         pbuf + (EXACT ? static_cast<size_t>(kRowWarps) * p.G * p.pb_row : 0));
     volatile uint32_t* slot_stage = reinterpret_cast<volatile uint32_t*>(full + nst);
@@ -192,13 +304,11 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     const uint32_t nrows = p.rows_base + (c < p.rows_extra ? 1u : 0u);
     const uint32_t nstages = (nrows + p.G - 1) / p.G;
 
-    if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < nst; ++s) {
-            mbar_init(&full[s], 1);
-            slot_stage[s] = 0xFFFFFFFFu;
-        }
-        fence_mbar_init();
+    for (uint32_t s = threadIdx.x; s < nst; s += kRowThreads) {
+        mbar_init(&full[s], 1);
+        slot_stage[s] = 0xFFFFFFFFu;
     }
+    fence_mbar_init();
     __syncthreads();
     if (p.pdl) pdl_launch_dependents();
 
@@ -217,25 +327,31 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         for (uint32_t s = warp; s < min(nst, nstages); s += kRowWarps) issue(s);
 
     // ── stage the activations (after the previous kernel finished) ──
+    // L2-coherent loads (__ldcg): under programmatic dependent launch x may have
+    // just been written by the previous kernel, so no L1 copy of it may be trusted.
     if (p.pdl) pdl_wait();
-    {
+    if constexpr (EXACT) {
         const uint32_t n4 = p.K / 4u;
         const uint32_t total = p.M * n4;
         for (uint32_t i = threadIdx.x; i < total; i += kRowWarps * 32u) {
             const uint32_t m = i / n4, e = (i % n4) * 4u;
-            // L2-coherent load: under programmatic dependent launch x may have just been
-            // written by the previous kernel, so no L1 copy of it may be trusted.
-            float4 v = __ldcg(reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K) + (i % n4));
-            if constexpr (DT == kDtypeQ4 && !EXACT) {
-                // element e % 4 == 0,1,2,3 -> pre-scale by 16^0, 16^-1, 16^-2, 16^-3
-                v.y *= 0.0625f;
-                v.z *= 0.00390625f;
-                v.w *= 0.000244140625f;
-            }
-            *reinterpret_cast<float4*>(xs + static_cast<size_t>(m) * p.xs_stride + 36u * (e >> 5) + (e & 31u)) = v;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K) + (i % n4));
+            *reinterpret_cast<float4*>(xsb + static_cast<size_t>(m) * p.xs_stride + 144u * (e >> 5) + 4u * (e & 31u)) = v;
+        }
+    } else {
+        // pass 1: every thread's loads in flight at once (raw floats into the records)
+        const uint32_t n4 = p.K / 4u;
+        const uint32_t total = p.M * n4;
+        for (uint32_t i = threadIdx.x; i < total; i += kRowWarps * 32u) {
+            const uint32_t m = i / n4, e = (i % n4) * 4u;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K) + (i % n4));
+            *reinterpret_cast<float4*>(xsb + static_cast<size_t>(m) * p.xs_stride + kLimbRec * (e >> 5) + 4u * (e & 31u)) = v;
         }
         __syncthreads();
+        // pass 2: four threads per block turn the floats into limbs
+        stage_limb_records<DT>(xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u);
     }
+    __syncthreads();
 
     for (uint32_t s = warp; s < nstages; s += kRowWarps) {
         const uint32_t slot = s % nst;
@@ -246,43 +362,48 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         const uint8_t* sb = slots + static_cast<size_t>(slot) * p.slot_stride;
 
         if constexpr (!EXACT) {
-            float racc[kRowGMax][MT];
+            float racc[GT][MT];
+            const uint8_t* rowp[GT];
 #pragma unroll
-            for (int g = 0; g < kRowGMax; ++g)
+            for (int g = 0; g < GT; ++g) {
+                rowp[g] = sb + static_cast<size_t>(min(static_cast<uint32_t>(g), rows_s - 1u)) * p.row_bytes;
 #pragma unroll
                 for (int v = 0; v < MT; ++v) racc[g][v] = 0.0f;
+            }
             for (uint32_t ch = 0; ch < p.nchunk; ++ch) {
                 const uint32_t b = ch * 32u + lane;
                 if (b < p.nblk) {
-                    float4 xv[MT][8];
+                    LimbBlock lb[MT];
+                    float cb[MT];
+                    int4 S[MT];
 #pragma unroll
-                    for (int v = 0; v < MT; ++v) lds_x_block(xs + static_cast<size_t>(v) * p.xs_stride, b, xv[v]);
+                    for (int v = 0; v < MT; ++v) {
+                        const uint8_t* rec = xsb + static_cast<size_t>(v) * p.xs_stride + kLimbRec * b;
+                        lds_limbs(rec, lb[v]);
+                        cb[v] = *reinterpret_cast<const float*>(rec + 128);
+                        if constexpr (DT == kDtypeQ4) S[v] = *reinterpret_cast<const int4*>(rec + 144);
+                    }
                     if constexpr (DT == kDtypeQ8) {
-                        uint32_t wv[kRowGMax][9];
+                        uint32_t wv[GT][9];
 #pragma unroll
-                        for (int g = 0; g < kRowGMax; ++g)
-                            if (g < static_cast<int>(rows_s)) load_q8_block(sb + static_cast<size_t>(g) * p.row_bytes, b, wv[g]);
+                        for (int g = 0; g < GT; ++g) load_q8_block(rowp[g], b, wv[g]);
 #pragma unroll
-                        for (int g = 0; g < kRowGMax; ++g) {
-                            if (g < static_cast<int>(rows_s)) {
-                                const float sc = __uint_as_float(wv[g][0]);
+                        for (int g = 0; g < GT; ++g) {
+                            const float sc = __uint_as_float(wv[g][0]);
 #pragma unroll
-                                for (int v = 0; v < MT; ++v) racc[g][v] = fmaf(q8_block_fast(wv[g], xv[v]), sc, racc[g][v]);
-                            }
+                            for (int v = 0; v < MT; ++v)
+                                racc[g][v] = fmaf(q8_block_limb(wv[g], lb[v]), sc * cb[v], racc[g][v]);
                         }
                     } else {
-                        uint32_t qw[kRowGMax][4], s16[kRowGMax];
+                        uint32_t qw[GT][4], s16[GT];
 #pragma unroll
-                        for (int g = 0; g < kRowGMax; ++g)
-                            if (g < static_cast<int>(rows_s))
-                                load_q4_block(sb + static_cast<size_t>(g) * p.row_bytes, b, qw[g], s16[g]);
+                        for (int g = 0; g < GT; ++g) load_q4_block(rowp[g], b, qw[g], s16[g]);
 #pragma unroll
-                        for (int g = 0; g < kRowGMax; ++g) {
-                            if (g < static_cast<int>(rows_s)) {
-                                const float sc = half_bits_to_float(s16[g]);
+                        for (int g = 0; g < GT; ++g) {
+                            const float sc = half_bits_to_float(s16[g]);
 #pragma unroll
-                                for (int v = 0; v < MT; ++v) racc[g][v] = fmaf(q4_block_fast(qw[g], xv[v]), sc, racc[g][v]);
-                            }
+                            for (int v = 0; v < MT; ++v)
+                                racc[g][v] = fmaf(q4_block_limb(qw[g], lb[v], S[v]), sc * cb[v], racc[g][v]);
                         }
                     }
                 }
@@ -290,19 +411,17 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
             __syncwarp();
             if (lane == 0 && s + nst < nstages) issue(s + nst);   // the slot's bytes are no longer read
 #pragma unroll
-            for (int g = 0; g < kRowGMax; ++g) {
-                if (g < static_cast<int>(rows_s)) {
+            for (int g = 0; g < GT; ++g) {
 #pragma unroll
-                    for (int v = 0; v < MT; ++v) {
-                        const float t = warp_sum(racc[g][v]);
-                        if (lane == 0) p.y[static_cast<size_t>(v) * p.N + row0 + g] = t;
-                    }
+                for (int v = 0; v < MT; ++v) {
+                    const float t = warp_sum(racc[g][v]);
+                    if (lane == 0 && g < static_cast<int>(rows_s)) p.y[static_cast<size_t>(v) * p.N + row0 + g] = t;
                 }
             }
         } else {
             float* pb = pbuf + static_cast<size_t>(warp) * p.G * p.pb_row;
             for (uint32_t m = 0; m < p.M; ++m) {
-                const float* xm = xs + static_cast<size_t>(m) * p.xs_stride;
+                const float* xm = reinterpret_cast<const float*>(xsb + static_cast<size_t>(m) * p.xs_stride);
                 for (uint32_t ch = 0; ch < p.nchunk; ++ch) {
                     const uint32_t b = ch * 32u + lane;
                     if (b < p.nblk) {
