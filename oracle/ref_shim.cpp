@@ -7,6 +7,7 @@
 // to pin the C restatement (qraf_oracle.c), to generate the golden fixtures in
 // tests/golden/, and as the timed CPU baseline.  No reference source is copied.
 #include "core/types.h"
+#include "nn/attention.h"
 #include "nn/backend.h"
 #include "nn/ops.h"
 #include "qraf/format.h"
@@ -99,6 +100,28 @@ void qref_matvec_q_threaded(const void* w, uint32_t dtype, int block_size, uint3
         });
     }
     for (auto& th : pool) th.join();
+}
+
+// mlp_forward (src/nn/attention.cpp:159-186): SwiGLU MLP of the reference with
+// quantized gate/up/down weights, each projection through dispatch_matvec_q.
+void qref_mlp_forward(float* out, const float* x, const void* w_gate, const void* w_up, const void* w_down,
+                      uint64_t gate_bytes, uint64_t down_bytes, uint32_t dtype, int block_size, uint32_t hidden,
+                      uint32_t inter) {
+    static QuantScheme qs;
+    qs = make_scheme(block_size);
+    MLPWeights w;
+    w.w_gate_data = w_gate;
+    w.w_up_data = w_up;
+    w.w_down_data = w_down;
+    w.w_gate_size = gate_bytes;
+    w.w_up_size = gate_bytes;
+    w.w_down_size = down_bytes;
+    w.dtype = static_cast<DType>(dtype);
+    w.quant = &qs;
+    ModelConfig cfg;
+    cfg.hidden_size = hidden;
+    cfg.intermediate_size = inter;
+    mlp_forward(out, x, w, cfg);
 }
 
 // fp32_to_fp16 / fp16_to_fp32 (src/tensor/dtype.cpp:9-59).
