@@ -65,9 +65,9 @@ def measured_peaks():
     return 6650.0, "fallback (6.65 TB/s, profiling recipe)"
 
 
-def profiled_traffic(dt):
-    """DRAM bytes per launch from the committed ncu summary of the same kernel, if present."""
-    name = "matvec_stream_q4_4096x4096.md" if dt == Q4 else "matvec_stream_q8_4096x4096.md"
+def profiled_traffic(dt, n, k):
+    """DRAM bytes per launch from the committed ncu summary of the same kernel and shape, if present."""
+    name = f"matvec_rows_{'q4' if dt == Q4 else 'q8'}_{n}x{k}.md"
     path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
         return None
@@ -366,7 +366,7 @@ def run_ours(args, dt, n, k, m):
             "e2e": e2e,
             "gpu_launches": args.steps * R,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profiled_traffic(dt), "peak_source": peak_src,
+                         "frac": achieved / peak, "traffic": profiled_traffic(dt, n, k), "peak_source": peak_src,
                          "kernel": "qmv_rows_kernel" if m <= 2 else "qmv_stream_kernel",
                          "kernel_us": kern_ms * 1e3,
                          "kernel_timing": "average launch duration of back-to-back launches without overlap "
