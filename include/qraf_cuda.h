@@ -129,6 +129,38 @@ int qraf_cuda_quantize_rows(uint32_t dtype, const float* x_dev, uint32_t rows, u
 int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint32_t block_size, float* out_dev,
                          void* stream);
 
+/* ── row-sharded matvec over several GPUs (one process per GPU) ─────────── */
+/* A weight too large for one GPU's bandwidth budget is partitioned by output
+ * rows (qraf_cuda_weight_shard); each rank computes its rows and the kernel
+ * itself stores every output element into every rank's full-length y buffer
+ * over NVLink (CUDA IPC peer mappings, plain stores), then signals the peers and
+ * waits (bounded) for them: the all-gather is fused into the matvec.  The
+ * library does no networking: the caller exchanges the opaque handles (e.g.
+ * with torch.distributed or MPI).  Waits that run out set the device status
+ * (qraf_cuda_device_status returns QRAF_ERR_TIMEOUT). */
+#define QRAF_COMM_HANDLE_BYTES 256
+#define QRAF_COMM_MAX_WORLD 8
+typedef struct qraf_comm* qraf_comm_t;
+/* Allocate this rank's two output buffers of `capacity_floats` floats each
+ * (used alternately, call by call) and its flag array on the current device. */
+int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_comm_t* out);
+/* This rank's CUDA IPC handles, QRAF_COMM_HANDLE_BYTES bytes. */
+int qraf_cuda_comm_handle(qraf_comm_t comm, void* handle_out);
+/* Map every peer's buffers; `all_handles` holds world handles in rank order. */
+int qraf_cuda_comm_open(qraf_comm_t comm, const void* all_handles);
+/* Link `n` comms created by this one process (one per GPU, or several on one
+ * GPU) directly, without IPC: peer access is enabled between distinct devices.
+ * comms[i] must have rank i and world n. */
+int qraf_cuda_comm_open_local(qraf_comm_t* comms, int n);
+int qraf_cuda_comm_destroy(qraf_comm_t comm);
+/* Rows [row_offset, row_offset + shard->rows) of a weight with total_rows rows:
+ * Y[m][n] for all n lands in every rank's buffer; *y_out receives this rank's
+ * buffer for this call (valid until the call after next).  Same arguments and
+ * modes as qraf_cuda_matvec_q; needs block size 32, 16-byte-aligned rows, and M
+ * small enough for one launch (M <= 2 in FAST mode). */
+int qraf_cuda_matvec_q_sharded(qraf_comm_t comm, const qraf_weight_t* shard, uint32_t total_rows, uint32_t row_offset,
+                               const float* x_dev, uint32_t M, int mode, void* stream, float** y_out);
+
 /* ── host-pointer entry: the drop-in body of qraf::dispatch_matvec_q ────── */
 /* Same arguments as the reference's dispatch_matvec_q (backend.h:31-34) plus M
  * and mode.  The first call with a given (w_host, w_size, dtype, bs, rows,

@@ -88,6 +88,12 @@ def _load() -> C.CDLL:
         "qraf_cuda_matvec_q_host": (i32, [vp, u64, u32, u32, u32, u32, vp, vp, u32, i32]),
         "qraf_cuda_host_cache_clear": (i32, []),
         "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
+        "qraf_cuda_comm_create": (i32, [i32, i32, u64, C.POINTER(vp)]),
+        "qraf_cuda_comm_handle": (i32, [vp, vp]),
+        "qraf_cuda_comm_open": (i32, [vp, vp]),
+        "qraf_cuda_comm_open_local": (i32, [C.POINTER(vp), i32]),
+        "qraf_cuda_comm_destroy": (i32, [vp]),
+        "qraf_cuda_matvec_q_sharded": (i32, [vp, W, u32, u32, vp, u32, i32, vp, C.POINTER(vp)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -304,3 +310,85 @@ def dispatch_matvec_q(w_data: np.ndarray, w_size: int, w_dtype: int, block_size:
 
 def host_cache_clear() -> None:
     check(_get_lib().qraf_cuda_host_cache_clear())
+
+
+# ── row-sharded matvec over several GPUs ─────────────────────────────────
+COMM_HANDLE_BYTES = 256
+
+
+class Comm:
+    """One rank's buffers for the fused row-sharded matvec (qraf_cuda_comm_*)."""
+
+    def __init__(self, world: int, rank: int, capacity_floats: int):
+        h = C.c_void_p()
+        check(_get_lib().qraf_cuda_comm_create(world, rank, capacity_floats, C.byref(h)))
+        self.h, self.world, self.rank = h, world, rank
+
+    def handle(self) -> bytes:
+        buf = C.create_string_buffer(COMM_HANDLE_BYTES)
+        check(_get_lib().qraf_cuda_comm_handle(self.h, buf))
+        return buf.raw
+
+    def open(self, all_handles: list[bytes]) -> None:
+        blob = b"".join(all_handles)
+        check(_get_lib().qraf_cuda_comm_open(self.h, C.create_string_buffer(blob, len(blob))))
+
+    @staticmethod
+    def open_local(comms: list["Comm"]) -> None:
+        arr = (C.c_void_p * len(comms))(*[c.h for c in comms])
+        check(_get_lib().qraf_cuda_comm_open_local(arr, len(comms)))
+
+    def matvec_q(self, shard: Weight, total_rows: int, row_offset: int, x, mode: int = MODE_FAST, stream=None):
+        """Rows of `shard` into every rank's y; returns this rank's full y ([M, total_rows], a view)."""
+        torch = _torch()
+        x2 = x.reshape(1, -1) if x.dim() == 1 else x
+        m = x2.shape[0]
+        yp = C.c_void_p()
+        check(_get_lib().qraf_cuda_matvec_q_sharded(self.h, C.byref(shard.desc), total_rows, row_offset,
+                                                    C.c_void_p(x2.data_ptr()), m, mode, _stream(stream), C.byref(yp)))
+        return _wrap_device_floats(yp.value, m * total_rows, x.device).view(m, total_rows)
+
+    def destroy(self) -> None:
+        if self.h:
+            _get_lib().qraf_cuda_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+def _wrap_device_floats(ptr: int, n: int, device):
+    """A torch view of n fp32 values at a device address owned by the library."""
+    torch = _torch()
+
+    class _Holder:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+
+    return torch.as_tensor(_Holder(), device=device)
+
+
+def make_comm(world: int, rank: int, capacity_floats: int, all_gather_bytes) -> Comm:
+    """Create this rank's Comm and open it, exchanging handles with `all_gather_bytes`
+    (a callable taking this rank's bytes and returning every rank's, in rank order)."""
+    c = Comm(world, rank, capacity_floats)
+    handles = all_gather_bytes(c.handle())
+    if len(handles) != world or any(len(h) != COMM_HANDLE_BYTES for h in handles):
+        raise QrafError(ERR_COMM, "handle exchange returned the wrong number or size of handles")
+    c.open(handles)
+    return c
+
+
+def torch_all_gather_bytes(group=None):
+    """all_gather_bytes for make_comm over an initialised torch.distributed group."""
+    import torch.distributed as dist
+
+    def gather(b: bytes) -> list[bytes]:
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, b, group=group)
+        return out
+
+    return gather

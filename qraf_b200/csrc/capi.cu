@@ -238,6 +238,17 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.rows_base = rows_base;
     p.rows_extra = rows_extra;
     p.pdl = 0;
+    p.world = 0;
+    p.rank = 0;
+    p.epoch = 0;
+    p.y_ld = w.rows;
+    p.row_off = 0;
+    p.local_flags = nullptr;
+    p.cta_counter = nullptr;
+    for (int r = 0; r < kMaxWorld; ++r) {
+        p.peer_y[r] = nullptr;
+        p.peer_flags[r] = nullptr;
+    }
     out->grid = static_cast<int>(grid);
     out->smem = static_cast<size_t>(nst) * slot_stride + fixed + nst * 12u;
     return true;
@@ -642,6 +653,186 @@ int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint
         dequantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(
             static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb);
     QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+// ── row-sharded matvec: comm objects ──────────────────────────────────────
+struct qraf_comm {
+    int world = 0, rank = 0, device = 0;
+    uint64_t cap = 0;
+    float* y[2] = {nullptr, nullptr};           // this rank's output buffers (alternate by epoch)
+    uint32_t* flags = nullptr;                   // [world], set by the peers
+    uint32_t* counter = nullptr;                 // CTA completion counter of this rank's launches
+    float* peer_y[2][QRAF_COMM_MAX_WORLD] = {};
+    uint32_t* peer_flags[QRAF_COMM_MAX_WORLD] = {};
+    bool opened = false;
+    bool local_group = false;                    // linked by qraf_cuda_comm_open_local (no IPC mappings)
+    uint32_t epoch = 0;
+};
+
+int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_comm_t* out) {
+    if (!out || world < 1 || world > QRAF_COMM_MAX_WORLD || rank < 0 || rank >= world || capacity_floats == 0)
+        return fail(QRAF_ERR_INVALID, "bad comm arguments (world %d, rank %d)", world, rank);
+    int rc = ensure_device(nullptr, nullptr);
+    if (rc) return rc;
+    qraf_comm* c = new qraf_comm();
+    c->world = world;
+    c->rank = rank;
+    cudaGetDevice(&c->device);
+    c->cap = capacity_floats;
+    bool ok = cudaMalloc(&c->y[0], capacity_floats * sizeof(float)) == cudaSuccess &&
+              cudaMalloc(&c->y[1], capacity_floats * sizeof(float)) == cudaSuccess &&
+              cudaMalloc(&c->flags, 256) == cudaSuccess && cudaMalloc(&c->counter, 256) == cudaSuccess &&
+              cudaMemset(c->flags, 0, 256) == cudaSuccess && cudaMemset(c->counter, 0, 256) == cudaSuccess &&
+              cudaDeviceSynchronize() == cudaSuccess;
+    if (!ok) {
+        qraf_cuda_comm_destroy(c);
+        return fail(QRAF_ERR_NOMEM, "comm buffers of %llu floats could not be allocated",
+                    static_cast<unsigned long long>(capacity_floats));
+    }
+    *out = c;
+    return QRAF_OK;
+}
+
+int qraf_cuda_comm_handle(qraf_comm_t c, void* handle_out) {
+    if (!c || !handle_out) return fail(QRAF_ERR_INVALID, "comm or handle is NULL");
+    static_assert(3 * sizeof(cudaIpcMemHandle_t) <= QRAF_COMM_HANDLE_BYTES, "handle size");
+    uint8_t* h = static_cast<uint8_t*>(handle_out);
+    std::memset(h, 0, QRAF_COMM_HANDLE_BYTES);
+    cudaIpcMemHandle_t m;
+    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->y[0]));
+    std::memcpy(h, &m, sizeof(m));
+    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->y[1]));
+    std::memcpy(h + sizeof(m), &m, sizeof(m));
+    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->flags));
+    std::memcpy(h + 2 * sizeof(m), &m, sizeof(m));
+    return QRAF_OK;
+}
+
+int qraf_cuda_comm_open(qraf_comm_t c, const void* all_handles) {
+    if (!c || !all_handles) return fail(QRAF_ERR_INVALID, "comm or handles is NULL");
+    if (c->opened) return fail(QRAF_ERR_INVALID, "comm is already open");
+    const uint8_t* h = static_cast<const uint8_t*>(all_handles);
+    for (int q = 0; q < c->world; ++q) {
+        if (q == c->rank) {
+            c->peer_y[0][q] = c->y[0];
+            c->peer_y[1][q] = c->y[1];
+            c->peer_flags[q] = c->flags;
+            continue;
+        }
+        const uint8_t* hq = h + static_cast<size_t>(q) * QRAF_COMM_HANDLE_BYTES;
+        cudaIpcMemHandle_t m;
+        void* ptr = nullptr;
+        for (int i = 0; i < 3; ++i) {
+            std::memcpy(&m, hq + i * sizeof(m), sizeof(m));
+            const cudaError_t e = cudaIpcOpenMemHandle(&ptr, m, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) return fail(QRAF_ERR_COMM, "opening rank %d's buffer %d: %s", q, i, cudaGetErrorString(e));
+            if (i < 2) c->peer_y[i][q] = static_cast<float*>(ptr);
+            else c->peer_flags[q] = static_cast<uint32_t*>(ptr);
+        }
+    }
+    c->opened = true;
+    return QRAF_OK;
+}
+
+int qraf_cuda_comm_open_local(qraf_comm_t* comms, int n) {
+    if (!comms || n < 1 || n > QRAF_COMM_MAX_WORLD) return fail(QRAF_ERR_INVALID, "bad comm group of %d", n);
+    for (int i = 0; i < n; ++i)
+        if (!comms[i] || comms[i]->rank != i || comms[i]->world != n || comms[i]->opened)
+            return fail(QRAF_ERR_INVALID, "comm %d does not have rank %d of world %d, or is already open", i, i, n);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < n; ++j) {
+            if (comms[i]->device != comms[j]->device) {
+                cudaSetDevice(comms[i]->device);
+                const cudaError_t e = cudaDeviceEnablePeerAccess(comms[j]->device, 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+                    cudaSetDevice(cur);
+                    return fail(QRAF_ERR_COMM, "peer access %d -> %d: %s", comms[i]->device, comms[j]->device,
+                                cudaGetErrorString(e));
+                }
+                cudaGetLastError();
+            }
+            comms[i]->peer_y[0][j] = comms[j]->y[0];
+            comms[i]->peer_y[1][j] = comms[j]->y[1];
+            comms[i]->peer_flags[j] = comms[j]->flags;
+        }
+    }
+    cudaSetDevice(cur);
+    for (int i = 0; i < n; ++i) {
+        comms[i]->opened = true;
+        comms[i]->local_group = true;
+    }
+    return QRAF_OK;
+}
+
+int qraf_cuda_comm_destroy(qraf_comm_t c) {
+    if (!c) return QRAF_OK;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    if (c->opened && !c->local_group) {
+        for (int q = 0; q < c->world; ++q) {
+            if (q == c->rank) continue;
+            if (c->peer_y[0][q]) cudaIpcCloseMemHandle(c->peer_y[0][q]);
+            if (c->peer_y[1][q]) cudaIpcCloseMemHandle(c->peer_y[1][q]);
+            if (c->peer_flags[q]) cudaIpcCloseMemHandle(c->peer_flags[q]);
+        }
+    }
+    if (c->y[0]) cudaFree(c->y[0]);
+    if (c->y[1]) cudaFree(c->y[1]);
+    if (c->flags) cudaFree(c->flags);
+    if (c->counter) cudaFree(c->counter);
+    cudaSetDevice(cur);
+    delete c;
+    return QRAF_OK;
+}
+
+int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32_t total_rows, uint32_t row_offset,
+                               const float* x_dev, uint32_t M, int mode_in, void* stream, float** y_out) {
+    if (!c || !c->opened) return fail(QRAF_ERR_INVALID, "comm is not open");
+    int rc = check_weight(shard);
+    if (rc) return rc;
+    if (!x_dev || !y_out) return fail(QRAF_ERR_INVALID, "x or y_out is NULL");
+    if (M == 0 || shard->rows == 0 || static_cast<uint64_t>(row_offset) + shard->rows > total_rows)
+        return fail(QRAF_ERR_INVALID, "rows [%u, %u) outside %u", row_offset, row_offset + shard->rows, total_rows);
+    if (static_cast<uint64_t>(M) * total_rows > c->cap)
+        return fail(QRAF_ERR_INVALID, "M * total_rows = %llu exceeds the comm capacity %llu",
+                    static_cast<unsigned long long>(M) * total_rows, static_cast<unsigned long long>(c->cap));
+    const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
+    int mode = mode_in & 0xFF;
+    if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_UNSUPPORTED, "mode %d", mode_in);
+    const bool exact = mode == QRAF_MODE_EXACT;
+    if (!rows_eligible(*shard, x_dev) || (!exact && M > 2))
+        return fail(QRAF_ERR_UNSUPPORTED, "the sharded path needs block size 32, 16-byte-aligned rows and pointers, "
+                                          "and M <= 2 in FAST mode");
+    DeviceInfo* dev = nullptr;
+    rc = ensure_device(nullptr, &dev);
+    if (rc) return rc;
+    RowPlan pl;
+    if (!plan_rows(*shard, x_dev, nullptr, M, exact, *dev, &pl))
+        return fail(QRAF_ERR_UNSUPPORTED, "%u activation vectors do not fit one launch", M);
+    const uint32_t epoch = ++c->epoch;
+    const int buf = static_cast<int>(epoch & 1u);
+    RowParams& p = pl.p;
+    p.world = static_cast<uint32_t>(c->world);
+    p.rank = static_cast<uint32_t>(c->rank);
+    p.epoch = epoch;
+    p.y_ld = total_rows;
+    p.row_off = row_offset;
+    p.local_flags = c->flags;
+    p.cta_counter = c->counter;
+    for (int r = 0; r < c->world; ++r) {
+        p.peer_y[r] = c->peer_y[buf][r];
+        p.peer_flags[r] = c->peer_flags[r];
+    }
+    const cudaError_t e = launch_rows(shard->dtype, pl, exact, exact ? 1 : static_cast<int>(M), overlap,
+                                      static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));
+    *y_out = c->y[buf];
     return QRAF_OK;
 }
 

@@ -52,6 +52,7 @@ namespace qraf_dev {
 constexpr int kRowWarps = 16;                      // warps per CTA (4 per SM sub-partition)
 constexpr int kRowThreads = kRowWarps * 32;
 constexpr int kRowGMax = 4;                        // rows per stage, at most
+constexpr int kMaxWorld = 8;                       // GPUs in a row-sharded group, at most
 
 struct RowParams {
     const uint8_t* w;        // [N][row_bytes], 16-byte aligned, row_bytes % 16 == 0
@@ -67,10 +68,65 @@ struct RowParams {
     uint32_t pb_row;         // EXACT: floats per row of the per-warp partial buffer
     uint32_t rows_base, rows_extra;
     uint32_t pdl;            // 1: programmatic dependent launch protocol
+    // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
+    // of a y that has y_ld rows in all; every output element is stored into each
+    // rank's full-length y (peer memory mapped through CUDA IPC, written with plain
+    // stores over NVLink), then the grid's last CTA signals every rank and waits,
+    // bounded, until every rank has signalled this epoch.
+    float* peer_y[kMaxWorld];
+    uint32_t* peer_flags[kMaxWorld];   // rank r's flag array; entry `rank` is ours to set
+    uint32_t* local_flags;             // this rank's flag array, set by the peers
+    uint32_t* cta_counter;             // CTAs of this launch that have stored all their rows
+    uint32_t world, rank, epoch, y_ld, row_off;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// One output element: into y, or (row-sharded) into every rank's y.
+__device__ __forceinline__ void store_out(const RowParams& p, uint32_t v, uint32_t row, float t) {
+    if (p.world == 0) {
+        p.y[static_cast<size_t>(v) * p.N + row] = t;
+        return;
+    }
+    const size_t idx = static_cast<size_t>(v) * p.y_ld + p.row_off + row;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+        if (r < static_cast<int>(p.world)) p.peer_y[r][idx] = t;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// Row-sharded completion: called by every thread at the end of the kernel.
+// The last CTA to finish signals epoch to every rank, then waits (bounded)
+// until every rank has signalled it; after that all of y is in local memory.
+__device__ __forceinline__ void sharded_finish(const RowParams& p) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();                                  // this CTA's peer stores before its count
+    const uint32_t done = atomicAdd(p.cta_counter, 1u);
+    if (done != gridDim.x - 1u) return;
+    __threadfence_system();                                  // every CTA's stores before the signals
+    *p.cta_counter = 0u;                                     // ready for the next launch
+    for (uint32_t r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.rank, p.epoch);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t q = 0; q < p.world; ++q) {
+        while (static_cast<int32_t>(ld_acquire_sys(p.local_flags + q) - p.epoch) < 0) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                raise_error(kErrWaitTimeout);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
 
 // Wait (bounded) until the issuing lane has published stage `s` in this slot.
 __device__ __forceinline__ bool wait_stage_id(volatile uint32_t* slot_stage, uint32_t s) {
@@ -355,8 +411,8 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
 
     for (uint32_t s = warp; s < nstages; s += kRowWarps) {
         const uint32_t slot = s % nst;
-        if (!wait_stage_id(slot_stage + slot, s)) return;
-        if (!mbar_wait(&full[slot], (s / nst) & 1u)) return;
+        if (!wait_stage_id(slot_stage + slot, s)) break;      // error raised; every warp still reaches the end
+        if (!mbar_wait(&full[slot], (s / nst) & 1u)) break;
         const uint32_t rows_s = min(p.G, nrows - s * p.G);
         const uint32_t row0 = r0 + s * p.G;
         const uint8_t* sb = slots + static_cast<size_t>(slot) * p.slot_stride;
@@ -415,7 +471,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
 #pragma unroll
                 for (int v = 0; v < MT; ++v) {
                     const float t = warp_sum(racc[g][v]);
-                    if (lane == 0 && g < static_cast<int>(rows_s)) p.y[static_cast<size_t>(v) * p.N + row0 + g] = t;
+                    if (lane == 0 && g < static_cast<int>(rows_s)) store_out(p, v, row0 + g, t);
                 }
             }
         } else {
@@ -455,13 +511,14 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                         total = __fadd_rn(total, v.z);
                         total = __fadd_rn(total, v.w);
                     }
-                    p.y[static_cast<size_t>(m) * p.N + row0 + lane] = total;
+                    store_out(p, m, row0 + lane, total);
                 }
                 __syncwarp();
             }
             if (lane == 0 && s + nst < nstages) issue(s + nst);
         }
     }
+    if (p.world) sharded_finish(p);
 }
 
 }  // namespace qraf_dev
