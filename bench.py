@@ -382,6 +382,339 @@ def run_ours(args, dt, n, k, m):
         dist.barrier()
         dist.destroy_process_group()
 
+# ── decode-token workloads: BASELINE.json configs 3 and 5 ─────────────────
+# Per layer, the projections in call order: (name, N out, K in, input).  The
+# input is the output of an earlier projection of the token ("h" = the layer's
+# input, which is the previous layer's "down" output).  Attention, norms and
+# SwiGLU are not on the path: O consumes the Q projection's output and down
+# consumes gate's (same widths), so every matvec reads a real predecessor.
+TOKEN_MODELS = {
+    # Qwen2-style 3B (config 3): hidden 2048, 16 Q / 2 KV heads of 128, FFN 11008, tied LM head 151936, Q8_0.
+    "qwen3b": {"dtype": Q8, "layers": 36, "hidden": 2048, "vocab": 151936,
+               "projs": [("q", 2048, 2048, "h"), ("k", 256, 2048, "h"), ("v", 256, 2048, "h"),
+                         ("o", 2048, 2048, "q"), ("gate", 11008, 2048, "o"), ("up", 11008, 2048, "o"),
+                         ("down", 2048, 11008, "gate")]},
+    # 70B shapes (config 5), Q4_0: fused QKV 10240, gate/up 28672, down, LM head 128256.
+    "llama70b": {"dtype": Q4, "layers": 80, "hidden": 8192, "vocab": 128256,
+                 "projs": [("qkv", 10240, 8192, "h"), ("gate", 28672, 8192, "h"), ("up", 28672, 8192, "h"),
+                           ("down", 8192, 28672, "gate")]},
+}
+TOKEN_METRIC = "projection-only decode tokens/s"
+
+
+def parse_token_workload(name: str):
+    """'llama70b_token' / 'qwen3b_token_m2' -> (model, M), or None for a single-matvec workload."""
+    parts = name.split("_")
+    if len(parts) < 2 or parts[0] not in TOKEN_MODELS or parts[1] != "token":
+        return None
+    m = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("m") else 1
+    return parts[0], m
+
+
+def token_shapes(spec):
+    """Every projection of one token, in order: (name, N, K, input), the LM head last."""
+    calls = []
+    for _ in range(spec["layers"]):
+        calls.extend(spec["projs"])
+    return calls + [("lm_head", spec["vocab"], spec["hidden"], "h")]
+
+
+def token_cpu_seconds(spec, m, time_rows):
+    """Seconds for one token of M vectors on the reference's CPU path, from per-row times:
+    time_rows(n, k) -> seconds per row of that shape."""
+    per_layer = sum(time_rows(n, k) * n for _, n, k, _ in spec["projs"])
+    lm = time_rows(spec["vocab"], spec["hidden"]) * spec["vocab"]
+    return m * (spec["layers"] * per_layer + lm)
+
+
+def _sample_rows_timer(spec, threads, budget_s, quantized_rows):
+    """Per-row seconds of the reference's dot (oracle/_ref) on a bounded sample of rows of each shape.
+    quantized_rows(n, k, rows) -> host bytes of the first `rows` rows of that shape."""
+    import oracle
+
+    ref = oracle.Reference() if oracle.reference_available() else None
+    orc = None if ref else oracle.Oracle()
+    dt = spec["dtype"]
+    shapes = sorted({(n, k) for _, n, k, _ in spec["projs"]} | {(spec["vocab"], spec["hidden"])})
+    per_row, sampled = {}, []
+    x_cache = {}
+    for n, k in shapes:
+        rows = min(n, max(256, 32 * threads))
+        q = quantized_rows(n, k, rows)
+        x = x_cache.setdefault(k, qb_fill(43, k))
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            if ref:
+                ref.matvec(dt, q, rows, k, x, 32, threads=threads)
+            else:
+                orc.matvec(dt, q, rows, k, x)
+            reps += 1
+            if time.perf_counter() - t0 >= budget_s / len(shapes):
+                break
+        per_row[(n, k)] = (time.perf_counter() - t0) / (reps * rows)
+        sampled.append(f"{reps}x{rows} rows of {n}x{k}")
+    kind = "reference" if ref else "port"
+    return (lambda n, k: per_row[(n, k)]), kind, "; ".join(sampled)
+
+
+def qb_fill(seed, n):
+    import qraf_b200 as qb
+
+    return qb.fill_normal(seed, 0.0, 1.0, n)
+
+
+def run_token(args, model, m):
+    """One STEP = one decode token of M vectors through every projection of the model
+    (layers x projections + LM head), captured as one CUDA graph and replayed.
+    With N > 1 ranks every weight is split by output rows; each call's rows reach
+    every rank either through the fused kernel (peer stores over NVLink, the
+    default) or through an NCCL all-gather after the plain kernel (--allgather nccl,
+    the baseline).  value = M x steps / max-over-ranks device time (tokens/s)."""
+    import torch
+
+    import qraf_b200 as qb
+
+    spec = TOKEN_MODELS[model]
+    dt, hidden, vocab = spec["dtype"], spec["hidden"], spec["vocab"]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    qb.init(local)
+    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+    fused = world > 1 and args.allgather == "fused"
+    if world > 1 and m > 2 and mode == qb.MODE_FAST:
+        raise SystemExit("the row-sharded FAST path takes M <= 2; use --mode exact for larger M")
+
+    # Seeded weights, generated on the device in 1024-row chunks (so every rank
+    # draws the same rows whatever the world size), quantized byte-exactly, one
+    # copy per layer in distinct memory (every matvec reads its weight cold).
+    gen = torch.Generator(device=dev)
+
+    def shard_bytes(idx, n, k):
+        r0, r1 = n * rank // world, n * (rank + 1) // world
+        w = torch.empty((r1 - r0, k), device=dev)
+        for c0 in range(r0 // 1024 * 1024, r1, 1024):
+            gen.manual_seed(42 * 1_000_003 + idx * 4099 + c0 // 1024)
+            blk = torch.randn((min(1024, n - c0), k), generator=gen, device=dev) * 0.02
+            a, b = max(c0, r0), min(c0 + 1024, r1)
+            w[a - r0:b - r0] = blk[a - c0:b - c0]
+        q = qb.quantize_rows(dt, w, 32).reshape(-1)
+        del w
+        return q, r0, r1
+
+    projs = spec["projs"]
+    layer_bytes, proto = 0, []
+    for i, (name, n, k, _) in enumerate(projs):
+        q, r0, r1 = shard_bytes(i, n, k)
+        proto.append((name, n, k, q, r0, r1, layer_bytes))
+        layer_bytes += (q.numel() + 255) // 256 * 256
+    store = torch.empty((spec["layers"], layer_bytes), dtype=torch.uint8, device=dev)
+    weights, shape_bytes = [], {}
+    for l in range(spec["layers"]):
+        row = []
+        for name, n, k, q, r0, r1, off in proto:
+            view = store[l, off:off + q.numel()]
+            view.copy_(q)
+            row.append(qb.Weight.from_device(view, dt, r1 - r0, k))
+            shape_bytes.setdefault((n, k), view)
+        weights.append(row)
+    q_lm, lm0, lm1 = shard_bytes(len(projs), vocab, hidden)
+    shape_bytes[(vocab, hidden)] = q_lm
+    w_lm = qb.Weight.from_device(q_lm, dt, lm1 - lm0, hidden)
+    shard_weight_bytes = spec["layers"] * sum(p[3].numel() for p in proto) + q_lm.numel()
+    total_weight_bytes = spec["layers"] * sum(n * (k // 32) * BLOCK_BYTES[dt] for _, n, k, _ in projs) + \
+        vocab * (hidden // 32) * BLOCK_BYTES[dt]
+    del proto
+    torch.cuda.synchronize(dev)
+
+    h0 = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * hidden)).to(dev).reshape(m, hidden)
+    launch_mode = mode | (qb.MODE_FLAG_OVERLAP if args.overlap else 0)
+    comm = comm_lm = None
+    ybuf, lbuf, gbuf = {}, {}, {}
+    if fused:
+        gather = qb.torch_all_gather_bytes()
+        cap = m * max(n for _, n, _, _ in projs)
+        comm = qb.make_comm(world, rank, cap, gather)
+        comm_lm = qb.make_comm(world, rank, m * vocab, gather)   # logits: their own buffers
+    for name, n, k, _ in projs + [("lm_head", vocab, hidden, "h")]:
+        r0, r1 = n * rank // world, n * (rank + 1) // world
+        if world == 1:
+            ybuf[name] = torch.empty((m, n), device=dev)
+        elif not fused:
+            lbuf[name] = torch.empty((m, r1 - r0), device=dev)
+            gbuf[name] = torch.empty((world * m * (r1 - r0),), device=dev)
+
+    def project(name, n, k, w, x):
+        r0 = n * rank // world
+        if world == 1:
+            return qb.matvec_q(w, x, ybuf[name], mode=launch_mode)
+        if fused:
+            return (comm_lm if name == "lm_head" else comm).matvec_q(w, n, r0, x, mode=launch_mode)
+        loc = qb.matvec_q(w, x, lbuf[name], mode=launch_mode)
+        dist.all_gather_into_tensor(gbuf[name], loc)
+        rows = n // world
+        g = gbuf[name]
+        return g.view(1, n) if m == 1 else g.view(world, m, rows).permute(1, 0, 2).reshape(m, n)
+
+    def token():
+        vals = {"h": h0}
+        for l in range(spec["layers"]):
+            for (name, n, k, src), w in zip(projs, weights[l]):
+                vals[name] = project(name, n, k, w, vals[src])
+            vals["h"] = vals["down"]
+        return project("lm_head", vocab, hidden, w_lm, vals["h"])
+
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        token()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        logits = token()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    if qb.device_status() != qb.OK:
+        raise SystemExit("device status not OK after warm-up")
+
+    clocks = ClockSampler(local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    with torch.cuda.stream(s):
+        t0.record()
+        for _ in range(args.steps):
+            g.replay()
+        t1.record()
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+
+    # e2e: every step copies its input hidden state in from pinned host memory and
+    # its logits out, around the same graph.
+    h_host = torch.from_numpy(qb.fill_normal(44, 0.0, 1.0, m * hidden)).reshape(m, hidden).pin_memory()
+    lg_host = torch.empty((m, vocab), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    if dist:
+        dist.barrier()
+    te = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(s):
+            h0.copy_(h_host, non_blocking=True)
+            g.replay()
+            lg_host.copy_(logits, non_blocking=True)
+        s.synchronize()
+    e2e_s = time.perf_counter() - te
+    status = qb.device_status()
+    if dist:
+        t = torch.tensor([elapsed_ms, e2e_s, float(status != qb.OK)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_s, bad = float(t[0]), float(t[1]), float(t[2])
+        status = status if not bad else max(status, 1)
+
+    calls = len(projs) * spec["layers"] + 1
+    act_bytes = sum(4 * m * (k + n) for _, n, k, _ in token_shapes(spec))
+    per_token_s = elapsed_ms / 1e3 / args.steps
+    peak, peak_src = measured_peaks()
+    achieved = (shard_weight_bytes + act_bytes) / per_token_s / 1e9   # per GPU
+    cpu = None
+    if rank == 0 and world == 1:
+        def host_rows(n, k, rows):
+            return shape_bytes[(n, k)][:rows * (k // 32) * BLOCK_BYTES[dt]].cpu().numpy()
+
+        timer, kind, sample = _sample_rows_timer(spec, 1, args.cpu_seconds, host_rows)
+        cpu_tok_s = token_cpu_seconds(spec, m, timer)
+        cpu = {"value": m / cpu_tok_s, "unit": "tokens/s", "cores": 1, "kind": kind,
+               "sample": f"per-row time of dispatch_matvec_q's scalar path (single-threaded, as the reference runs "
+                         f"it on Linux) on {sample}, scaled to every row of one token"}
+    if rank == 0:
+        line = {
+            "metric": TOKEN_METRIC, "value": m * args.steps / (elapsed_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "model_shapes": model, "M": m, "layers": spec["layers"],
+                       "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode, "calls_per_token": calls,
+                       "weight_bytes_per_token": total_weight_bytes,
+                       "parallelism": (f"rows split over {world} GPUs, all-gather "
+                                       f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
+                       if world > 1 else "single GPU",
+                       "l2_policy": "inputs larger than L2: one distinct weight copy per layer "
+                                    f"({shard_weight_bytes / 1e9:.1f} GB per GPU per token)",
+                       "weights": "N(0,0.02) torch.Generator seeded per 1024-row chunk, quantized on GPU "
+                                  "(byte-exact Q*_0); the same bytes copied into every layer",
+                       "excluded": "attention, norms, SwiGLU, sampling (projection-only)",
+                       "step": "one token: every projection of every layer + LM head, one CUDA graph replay"},
+            "e2e": {"value": m * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": m * hidden * 4,
+                    "d2h_bytes_per_step": m * vocab * 4, "steps": e2e_steps,
+                    "path": "H2D of the token's hidden state from pinned memory, the token graph, D2H of the "
+                            "logits, stream sync, every step"},
+            "gpu_launches": args.steps * calls,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "what": "per GPU: weight shard + activation bytes of one token / time per token",
+                         "us_per_token": per_token_s * 1e6},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if dist:
+        dist.barrier()
+    for c in (comm, comm_lm):
+        if c is not None:
+            c.destroy()
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_token_reference(args, model, m):
+    """The reference's CPU path on the token workload: per-row times of its dot on a
+    bounded sample of rows of every shape, rows fanned out over all host threads."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import oracle
+
+    spec = TOKEN_MODELS[model]
+    dt = spec["dtype"]
+    threads = os.cpu_count() or 1
+    qz = oracle.Reference() if oracle.reference_available() else oracle.Oracle()
+
+    def host_rows(n, k, rows, cache={}):
+        if (n, k) not in cache:
+            w = qb_fill(42, rows * k) * np.float32(0.02)
+            cache[(n, k)] = qz.quantize(dt, w, 32)
+        return cache[(n, k)]
+
+    budget = max(2.0, min(60.0, 4.0 * args.steps))
+    timer, kind, sample = _sample_rows_timer(spec, threads, budget, host_rows)
+    tok_s = token_cpu_seconds(spec, m, timer)
+    line = {"impl": "reference", "metric": TOKEN_METRIC, "value": m / tok_s, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tok_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": args.workload, "model_shapes": model, "M": m},
+            "cpu_baseline": {"value": m / tok_s, "unit": "tokens/s", "cores": threads, "kind": kind,
+                             "sample": f"per-row time of the reference's dot, rows over {threads} threads, on "
+                                       f"{sample}; scaled to every row of one token"},
+            "e2e": {"value": m / tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -394,7 +727,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
+    ap.add_argument("--allgather", choices=["fused", "nccl"], default="fused",
+                    help="token workloads on N > 1 GPUs: all-gather fused into the kernel, or NCCL after it")
     args = ap.parse_args()
+    tok = parse_token_workload(args.workload)
+    if tok:
+        (run_token_reference if args.impl == "reference" else run_token)(args, *tok)
+        return
     dt, n, k, m = parse_workload(args.workload)
     if args.impl == "reference":
         run_reference_arm(args, dt, n, k, m)

@@ -138,26 +138,39 @@ int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint
  * library does no networking: the caller exchanges the opaque handles (e.g.
  * with torch.distributed or MPI).  Waits that run out set the device status
  * (qraf_cuda_device_status returns QRAF_ERR_TIMEOUT). */
-#define QRAF_COMM_HANDLE_BYTES 256
+#define QRAF_COMM_HANDLE_BYTES 512
+#define QRAF_COMM_BUFFERS 4
 #define QRAF_COMM_MAX_WORLD 8
 typedef struct qraf_comm* qraf_comm_t;
-/* Allocate this rank's two output buffers of `capacity_floats` floats each
- * (used alternately, call by call) and its flag array on the current device. */
+/* Allocate this rank's QRAF_COMM_BUFFERS output buffers of `capacity_floats`
+ * floats each (used in turn, call by call) and its receive array (2 x
+ * capacity_floats 8-byte words that the peers write) on the current device.
+ * A call's activations may be the output of any of the previous
+ * QRAF_COMM_BUFFERS - 1 calls. */
 int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_comm_t* out);
-/* This rank's CUDA IPC handles, QRAF_COMM_HANDLE_BYTES bytes. */
+/* This rank's CUDA IPC handle (its receive array), QRAF_COMM_HANDLE_BYTES bytes. */
 int qraf_cuda_comm_handle(qraf_comm_t comm, void* handle_out);
-/* Map every peer's buffers; `all_handles` holds world handles in rank order. */
+/* Map every peer's receive array; `all_handles` holds world handles in rank order. */
 int qraf_cuda_comm_open(qraf_comm_t comm, const void* all_handles);
 /* Link `n` comms created by this one process (one per GPU, or several on one
  * GPU) directly, without IPC: peer access is enabled between distinct devices.
  * comms[i] must have rank i and world n. */
 int qraf_cuda_comm_open_local(qraf_comm_t* comms, int n);
 int qraf_cuda_comm_destroy(qraf_comm_t comm);
-/* Rows [row_offset, row_offset + shard->rows) of a weight with total_rows rows:
- * Y[m][n] for all n lands in every rank's buffer; *y_out receives this rank's
- * buffer for this call (valid until the call after next).  Same arguments and
- * modes as qraf_cuda_matvec_q; needs block size 32, 16-byte-aligned rows, and M
- * small enough for one launch (M <= 2 in FAST mode). */
+/* Rows [row_offset, row_offset + shard->rows) of a weight with total_rows rows
+ * (the ranks' row ranges partition [0, total_rows)).  The kernel stores each of
+ * its outputs into this rank's buffer and, with the call's number, into every
+ * peer's receive array over NVLink; before it ends it copies the other ranks'
+ * rows into this rank's buffer, so Y[m][n] for all n is in *y_out (this rank's
+ * buffer for this call, valid for the next QRAF_COMM_BUFFERS - 1 calls) when
+ * the launch completes.  Same arguments and modes as qraf_cuda_matvec_q; needs
+ * block size 32, 16-byte-aligned rows, and M small enough for one launch
+ * (M <= 2 in FAST mode).  The calls of one comm go to one stream, in the same
+ * order on every rank.  Calls are numbered on the device, so a sequence of
+ * calls may be captured in a CUDA graph and replayed; capture a multiple of
+ * QRAF_COMM_BUFFERS calls per comm so that replays keep the buffer rotation
+ * (the buffers are chosen at capture).  A peer that does not deliver its rows
+ * within about a second leaves the status QRAF_ERR_TIMEOUT. */
 int qraf_cuda_matvec_q_sharded(qraf_comm_t comm, const qraf_weight_t* shard, uint32_t total_rows, uint32_t row_offset,
                                const float* x_dev, uint32_t M, int mode, void* stream, float** y_out);
 

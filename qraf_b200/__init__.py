@@ -313,7 +313,8 @@ def host_cache_clear() -> None:
 
 
 # ── row-sharded matvec over several GPUs ─────────────────────────────────
-COMM_HANDLE_BYTES = 256
+COMM_HANDLE_BYTES = 512
+COMM_BUFFERS = 4
 
 
 class Comm:

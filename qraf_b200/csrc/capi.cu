@@ -240,15 +240,14 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.pdl = 0;
     p.world = 0;
     p.rank = 0;
-    p.epoch = 0;
+    p.seq = nullptr;
     p.y_ld = w.rows;
     p.row_off = 0;
-    p.local_flags = nullptr;
+    p.y_full = nullptr;
+    p.local_ll = nullptr;
+    p.ll_cap = 0;
     p.cta_counter = nullptr;
-    for (int r = 0; r < kMaxWorld; ++r) {
-        p.peer_y[r] = nullptr;
-        p.peer_flags[r] = nullptr;
-    }
+    for (int r = 0; r < kMaxWorld; ++r) p.peer_ll[r] = nullptr;
     out->grid = static_cast<int>(grid);
     out->smem = static_cast<size_t>(nst) * slot_stride + fixed + nst * 12u;
     return true;
@@ -660,14 +659,14 @@ int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint
 struct qraf_comm {
     int world = 0, rank = 0, device = 0;
     uint64_t cap = 0;
-    float* y[2] = {nullptr, nullptr};           // this rank's output buffers (alternate by epoch)
-    uint32_t* flags = nullptr;                   // [world], set by the peers
-    uint32_t* counter = nullptr;                 // CTA completion counter of this rank's launches
-    float* peer_y[2][QRAF_COMM_MAX_WORLD] = {};
-    uint32_t* peer_flags[QRAF_COMM_MAX_WORLD] = {};
+    float* y[QRAF_COMM_BUFFERS] = {};              // this rank's output buffers (used in turn, call by call)
+    unsigned long long* ll = nullptr;               // receive array: 2 x cap words, written by the peers
+    uint32_t* counter = nullptr;                    // [0]: CTAs finished in the current launch,
+                                                    // [32]: calls completed (numbered on the device)
+    unsigned long long* peer_ll[QRAF_COMM_MAX_WORLD] = {};
     bool opened = false;
-    bool local_group = false;                    // linked by qraf_cuda_comm_open_local (no IPC mappings)
-    uint32_t epoch = 0;
+    bool local_group = false;                       // linked by qraf_cuda_comm_open_local (no IPC mappings)
+    uint32_t calls = 0;                             // calls issued from the host (picks the output buffer)
 };
 
 int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_comm_t* out) {
@@ -680,11 +679,13 @@ int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_co
     c->rank = rank;
     cudaGetDevice(&c->device);
     c->cap = capacity_floats;
-    bool ok = cudaMalloc(&c->y[0], capacity_floats * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&c->y[1], capacity_floats * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&c->flags, 256) == cudaSuccess && cudaMalloc(&c->counter, 256) == cudaSuccess &&
-              cudaMemset(c->flags, 0, 256) == cudaSuccess && cudaMemset(c->counter, 0, 256) == cudaSuccess &&
-              cudaDeviceSynchronize() == cudaSuccess;
+    bool ok = true;
+    for (int b = 0; b < QRAF_COMM_BUFFERS; ++b)
+        ok = ok && cudaMalloc(&c->y[b], capacity_floats * sizeof(float)) == cudaSuccess;
+    const size_t ll_bytes = 2 * capacity_floats * sizeof(unsigned long long);
+    ok = ok && cudaMalloc(&c->ll, ll_bytes) == cudaSuccess && cudaMalloc(&c->counter, 256) == cudaSuccess &&
+         cudaMemset(c->ll, 0, ll_bytes) == cudaSuccess && cudaMemset(c->counter, 0, 256) == cudaSuccess &&
+         cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         qraf_cuda_comm_destroy(c);
         return fail(QRAF_ERR_NOMEM, "comm buffers of %llu floats could not be allocated",
@@ -696,16 +697,12 @@ int qraf_cuda_comm_create(int world, int rank, uint64_t capacity_floats, qraf_co
 
 int qraf_cuda_comm_handle(qraf_comm_t c, void* handle_out) {
     if (!c || !handle_out) return fail(QRAF_ERR_INVALID, "comm or handle is NULL");
-    static_assert(3 * sizeof(cudaIpcMemHandle_t) <= QRAF_COMM_HANDLE_BYTES, "handle size");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= QRAF_COMM_HANDLE_BYTES, "handle size");
     uint8_t* h = static_cast<uint8_t*>(handle_out);
     std::memset(h, 0, QRAF_COMM_HANDLE_BYTES);
     cudaIpcMemHandle_t m;
-    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->y[0]));
+    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->ll));
     std::memcpy(h, &m, sizeof(m));
-    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->y[1]));
-    std::memcpy(h + sizeof(m), &m, sizeof(m));
-    QRAF_CUDA_TRY(cudaIpcGetMemHandle(&m, c->flags));
-    std::memcpy(h + 2 * sizeof(m), &m, sizeof(m));
     return QRAF_OK;
 }
 
@@ -715,21 +712,15 @@ int qraf_cuda_comm_open(qraf_comm_t c, const void* all_handles) {
     const uint8_t* h = static_cast<const uint8_t*>(all_handles);
     for (int q = 0; q < c->world; ++q) {
         if (q == c->rank) {
-            c->peer_y[0][q] = c->y[0];
-            c->peer_y[1][q] = c->y[1];
-            c->peer_flags[q] = c->flags;
+            c->peer_ll[q] = c->ll;
             continue;
         }
-        const uint8_t* hq = h + static_cast<size_t>(q) * QRAF_COMM_HANDLE_BYTES;
         cudaIpcMemHandle_t m;
+        std::memcpy(&m, h + static_cast<size_t>(q) * QRAF_COMM_HANDLE_BYTES, sizeof(m));
         void* ptr = nullptr;
-        for (int i = 0; i < 3; ++i) {
-            std::memcpy(&m, hq + i * sizeof(m), sizeof(m));
-            const cudaError_t e = cudaIpcOpenMemHandle(&ptr, m, cudaIpcMemLazyEnablePeerAccess);
-            if (e != cudaSuccess) return fail(QRAF_ERR_COMM, "opening rank %d's buffer %d: %s", q, i, cudaGetErrorString(e));
-            if (i < 2) c->peer_y[i][q] = static_cast<float*>(ptr);
-            else c->peer_flags[q] = static_cast<uint32_t*>(ptr);
-        }
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, m, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(QRAF_ERR_COMM, "opening rank %d's receive array: %s", q, cudaGetErrorString(e));
+        c->peer_ll[q] = static_cast<unsigned long long*>(ptr);
     }
     c->opened = true;
     return QRAF_OK;
@@ -754,9 +745,7 @@ int qraf_cuda_comm_open_local(qraf_comm_t* comms, int n) {
                 }
                 cudaGetLastError();
             }
-            comms[i]->peer_y[0][j] = comms[j]->y[0];
-            comms[i]->peer_y[1][j] = comms[j]->y[1];
-            comms[i]->peer_flags[j] = comms[j]->flags;
+            comms[i]->peer_ll[j] = comms[j]->ll;
         }
     }
     cudaSetDevice(cur);
@@ -774,16 +763,12 @@ int qraf_cuda_comm_destroy(qraf_comm_t c) {
     cudaSetDevice(c->device);
     cudaDeviceSynchronize();
     if (c->opened && !c->local_group) {
-        for (int q = 0; q < c->world; ++q) {
-            if (q == c->rank) continue;
-            if (c->peer_y[0][q]) cudaIpcCloseMemHandle(c->peer_y[0][q]);
-            if (c->peer_y[1][q]) cudaIpcCloseMemHandle(c->peer_y[1][q]);
-            if (c->peer_flags[q]) cudaIpcCloseMemHandle(c->peer_flags[q]);
-        }
+        for (int q = 0; q < c->world; ++q)
+            if (q != c->rank && c->peer_ll[q]) cudaIpcCloseMemHandle(c->peer_ll[q]);
     }
-    if (c->y[0]) cudaFree(c->y[0]);
-    if (c->y[1]) cudaFree(c->y[1]);
-    if (c->flags) cudaFree(c->flags);
+    for (int b = 0; b < QRAF_COMM_BUFFERS; ++b)
+        if (c->y[b]) cudaFree(c->y[b]);
+    if (c->ll) cudaFree(c->ll);
     if (c->counter) cudaFree(c->counter);
     cudaSetDevice(cur);
     delete c;
@@ -815,20 +800,18 @@ int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32
     RowPlan pl;
     if (!plan_rows(*shard, x_dev, nullptr, M, exact, *dev, &pl))
         return fail(QRAF_ERR_UNSUPPORTED, "%u activation vectors do not fit one launch", M);
-    const uint32_t epoch = ++c->epoch;
-    const int buf = static_cast<int>(epoch & 1u);
+    const int buf = static_cast<int>(++c->calls % QRAF_COMM_BUFFERS);
     RowParams& p = pl.p;
     p.world = static_cast<uint32_t>(c->world);
     p.rank = static_cast<uint32_t>(c->rank);
-    p.epoch = epoch;
+    p.seq = c->counter + 32;
     p.y_ld = total_rows;
     p.row_off = row_offset;
-    p.local_flags = c->flags;
+    p.y_full = c->y[buf];
+    p.local_ll = c->ll;
+    p.ll_cap = c->cap;
     p.cta_counter = c->counter;
-    for (int r = 0; r < c->world; ++r) {
-        p.peer_y[r] = c->peer_y[buf][r];
-        p.peer_flags[r] = c->peer_flags[r];
-    }
+    for (int r = 0; r < c->world; ++r) p.peer_ll[r] = c->peer_ll[r];
     const cudaError_t e = launch_rows(shard->dtype, pl, exact, exact ? 1 : static_cast<int>(M), overlap,
                                       static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));

@@ -69,61 +69,84 @@ struct RowParams {
     uint32_t rows_base, rows_extra;
     uint32_t pdl;            // 1: programmatic dependent launch protocol
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
-    // of a y that has y_ld rows in all; every output element is stored into each
-    // rank's full-length y (peer memory mapped through CUDA IPC, written with plain
-    // stores over NVLink), then the grid's last CTA signals every rank and waits,
-    // bounded, until every rank has signalled this epoch.
-    float* peer_y[kMaxWorld];
-    uint32_t* peer_flags[kMaxWorld];   // rank r's flag array; entry `rank` is ours to set
-    uint32_t* local_flags;             // this rank's flag array, set by the peers
-    uint32_t* cta_counter;             // CTAs of this launch that have stored all their rows
-    uint32_t world, rank, epoch, y_ld, row_off;
+    // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
+    // output element goes into this rank's y and, as one 8-byte word (call number
+    // << 32 | value bits), into every peer's receive array at the element's index:
+    // plain stores over NVLink and no fence, since an aligned 8-byte store is seen
+    // whole or not at all.  At the end every CTA copies its share of the other
+    // ranks' rows from this rank's receive array into y, polling (bounded) until
+    // each word carries this call's number.  Calls are numbered on the device
+    // (*seq), so a captured and replayed sequence of calls stays in step.
+    float* y_full;                                // this rank's y, [M][y_ld]
+    unsigned long long* peer_ll[kMaxWorld];       // rank r's receive array: two halves of ll_cap words (call parity)
+    unsigned long long* local_ll;                 // this rank's receive array
+    uint64_t ll_cap;
+    uint32_t* cta_counter;                        // CTAs of this launch that have finished
+    uint32_t* seq;                                // calls of this comm completed on this rank
+    uint32_t world, rank, y_ld, row_off;
 };
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// One output element: into y, or (row-sharded) into every rank's y.
-__device__ __forceinline__ void store_out(const RowParams& p, uint32_t v, uint32_t row, float t) {
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* a, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// One output element: into y, or (row-sharded) into this rank's y and every
+// peer's receive array.
+__device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uint32_t v, uint32_t row, float t) {
     if (p.world == 0) {
         p.y[static_cast<size_t>(v) * p.N + row] = t;
         return;
     }
     const size_t idx = static_cast<size_t>(v) * p.y_ld + p.row_off + row;
+    p.y_full[idx] = t;
+    const unsigned long long word = (static_cast<unsigned long long>(call) << 32) | __float_as_uint(t);
+    const size_t off = static_cast<size_t>(call & 1u) * p.ll_cap + idx;
 #pragma unroll
     for (int r = 0; r < kMaxWorld; ++r)
-        if (r < static_cast<int>(p.world)) p.peer_y[r][idx] = t;
+        if (r < static_cast<int>(p.world) && r != static_cast<int>(p.rank)) st_relaxed_sys_u64(p.peer_ll[r] + off, word);
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-    return v;
-}
-
-// Row-sharded completion: called by every thread at the end of the kernel.
-// The last CTA to finish signals epoch to every rank, then waits (bounded)
-// until every rank has signalled it; after that all of y is in local memory.
-__device__ __forceinline__ void sharded_finish(const RowParams& p) {
-    __syncthreads();
-    if (threadIdx.x != 0) return;
-    __threadfence_system();                                  // this CTA's peer stores before its count
-    const uint32_t done = atomicAdd(p.cta_counter, 1u);
-    if (done != gridDim.x - 1u) return;
-    __threadfence_system();                                  // every CTA's stores before the signals
-    *p.cta_counter = 0u;                                     // ready for the next launch
-    for (uint32_t r = 0; r < p.world; ++r) st_release_sys(p.peer_flags[r] + p.rank, p.epoch);
+// Row-sharded completion, by every thread of every CTA: copy the other ranks'
+// rows of this call from the receive array into y (bounded polling), then the
+// last CTA to finish records the call as completed.  A peer cannot overwrite a
+// half of the receive array before this rank has finished reading it: it
+// writes call c + 2 only after finishing call c + 1, which needs this rank's
+// rows of c + 1, which this rank computes only after this launch (call c)
+// has completed.
+__device__ __forceinline__ void sharded_gather(const RowParams& p, uint32_t call) {
+    const size_t total = static_cast<size_t>(p.M) * p.y_ld;
+    const unsigned long long* ll = p.local_ll + static_cast<size_t>(call & 1u) * p.ll_cap;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t q = 0; q < p.world; ++q) {
-        while (static_cast<int32_t>(ld_acquire_sys(p.local_flags + q) - p.epoch) < 0) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    bool ok = true;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; ok && i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint32_t row = static_cast<uint32_t>(i % p.y_ld);
+        if (row - p.row_off < p.N) continue;   // this rank's own row, stored directly
+        unsigned long long w = ld_relaxed_sys_u64(ll + i);
+        for (uint32_t it = 0; static_cast<uint32_t>(w >> 32) != call; ++it) {
+            if ((it & 31u) == 31u && globaltimer_ns() - t0 > kWaitLimitNs) {
                 raise_error(kErrWaitTimeout);
-                return;
+                ok = false;
+                break;
             }
-            __nanosleep(64);
+            w = ld_relaxed_sys_u64(ll + i);
+        }
+        if (ok) p.y_full[i] = __uint_as_float(static_cast<uint32_t>(w));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t done = atomicAdd(p.cta_counter, 1u);
+        if (done == gridDim.x - 1u) {
+            *p.cta_counter = 0u;   // ready for the next launch
+            *p.seq = call;         // read by the next launch after this grid has completed
         }
     }
 }
@@ -386,6 +409,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     // L2-coherent loads (__ldcg): under programmatic dependent launch x may have
     // just been written by the previous kernel, so no L1 copy of it may be trusted.
     if (p.pdl) pdl_wait();
+    const uint32_t call = p.world ? *reinterpret_cast<volatile const uint32_t*>(p.seq) + 1u : 0u;
     if constexpr (EXACT) {
         const uint32_t n4 = p.K / 4u;
         const uint32_t total = p.M * n4;
@@ -471,7 +495,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
 #pragma unroll
                 for (int v = 0; v < MT; ++v) {
                     const float t = warp_sum(racc[g][v]);
-                    if (lane == 0 && g < static_cast<int>(rows_s)) store_out(p, v, row0 + g, t);
+                    if (lane == 0 && g < static_cast<int>(rows_s)) store_out(p, call, v, row0 + g, t);
                 }
             }
         } else {
@@ -511,14 +535,14 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                         total = __fadd_rn(total, v.z);
                         total = __fadd_rn(total, v.w);
                     }
-                    store_out(p, m, row0 + lane, total);
+                    store_out(p, call, m, row0 + lane, total);
                 }
                 __syncwarp();
             }
             if (lane == 0 && s + nst < nstages) issue(s + nst);
         }
     }
-    if (p.world) sharded_finish(p);
+    if (p.world) sharded_gather(p, call);
 }
 
 }  // namespace qraf_dev

@@ -141,11 +141,56 @@ def _ipc_rank(rank, world, port, dt, n, k, out):
             dist.all_gather_into_tensor(gathered, local)
             ok &= bool(torch.equal(gathered, want))
         ok &= qb.device_status() == qb.OK
+        ok &= _captured_chain_matches(torch, dev, dist, world, rank)
         dist.barrier()
         comm.destroy()
         out.put((rank, ok))
     finally:
         dist.destroy_process_group()
+
+
+def _captured_chain_matches(torch, dev, dist, world, rank, n=4096, steps=8):
+    """A chain of sharded calls (each input is the previous call's gathered output,
+    or the one three calls back) captured in a CUDA graph and replayed: the calls
+    are numbered on the device, so replays stay in step across ranks and give the
+    unsharded chain's bits every time."""
+    q_full = _weight(torch, dev, qb.Q8_0, n, n, seed=7)
+    full = qb.Weight.from_device(q_full, qb.Q8_0, n, n)
+    shard = full.shard(world, rank)
+    r0 = n * rank // world
+    x0 = torch.from_numpy(qb.fill_normal(11, 0.0, 1.0, n)).to(dev)
+    outs, want = [x0], [x0]
+    for i in range(steps):
+        src = want[-3] if i % 4 == 3 else want[-1]
+        want.append(qb.matvec_q(full, src, mode=qb.MODE_FAST))
+    comm = qb.make_comm(world, rank, n, qb.torch_all_gather_bytes())
+    s = torch.cuda.Stream(dev)
+
+    def chain():
+        got = [x0]
+        for i in range(steps):
+            src = got[-3] if i % 4 == 3 else got[-1]
+            got.append(comm.matvec_q(shard, n, r0, src, mode=qb.MODE_FAST | qb.MODE_FLAG_OVERLAP)[0])
+        return got
+
+    with torch.cuda.stream(s):
+        chain()                       # eager once (first-use set-up happens outside the capture)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        got = chain()
+    ok = True
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize(dev)
+        # the last QRAF_COMM_BUFFERS outputs are still in their buffers
+        ok &= all(bool(torch.equal(a, b)) for a, b in zip(got[-qb.COMM_BUFFERS:], want[-qb.COMM_BUFFERS:]))
+    ok &= qb.device_status() == qb.OK
+    dist.barrier()
+    del g
+    comm.destroy()
+    return ok
 
 
 @pytest.mark.parametrize("dt,n,k", [(qb.Q4_0, 10240, 8192)])
