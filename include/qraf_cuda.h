@@ -47,8 +47,13 @@ extern "C" {
 /* ── arithmetic modes ───────────────────────────────────────────────────── */
 #define QRAF_MODE_EXACT 0  /* bit-identical to the reference's Linux scalar path */
 #define QRAF_MODE_FAST  1  /* fused multiply-add, reordered sums; allclose(rtol 1e-5, atol 1e-6) */
-#define QRAF_MODE_TC    2  /* tensor-core tile for M >= 16; same tolerance as FAST */
-#define QRAF_MODE_AUTO  3  /* FAST below M = 16, TC from M = 16 */
+#define QRAF_MODE_TC    2  /* tcgen05 tensor-core tile (exact per-block integer sums, fp32
+                              epilogue); same tolerance as FAST.  Needs block size 32,
+                              K % 128 == 0 (Q8_0) or K % 256 == 0 (Q4_0) and 16-byte-aligned
+                              weights.  Uses per-stream scratch memory that the library
+                              allocates at a stream's first call of a given size (make that
+                              call before capturing the stream in a CUDA graph). */
+#define QRAF_MODE_AUTO  3  /* FAST below M = 16, TC from M = 16 where the weight allows */
 /* Or-able flag: the kernel may start while the previous kernel in the stream is
  * still running and fetch the weight before waiting for it (programmatic
  * dependent launch).  Only valid when that previous kernel does not write the

@@ -2,6 +2,7 @@
 // argument checking, kernel selection and launch planning, the host-pointer
 // drop-in entry with its device weight cache, and small host utilities.
 #include <algorithm>
+#include <cudaTypedefs.h>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -13,6 +14,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "matmul_tc.cuh"
 #include "matvec_generic.cuh"
 #include "matvec_rows.cuh"
 #include "matvec_stream.cuh"
@@ -98,6 +100,12 @@ int ensure_device(int* dev_out, DeviceInfo** info_out) {
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 2>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 4>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 16>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 32>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 64>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ4, 16>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ4, 32>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ4, 64>, lim));
         d.ready = true;
     }
     if (dev_out) *dev_out = dev;
@@ -307,6 +315,213 @@ cudaError_t launch_generic(const GenericParams& gp, uint64_t tasks, cudaStream_t
     return cudaGetLastError();
 }
 
+// ── tensor-core plan and its scratch memory ──────────────────────────────
+// Scratch per call (one launch pair per group of <= 64 vectors): the prepared
+// activation tiles, the block factors, the stream-K partial results and the
+// tile counters.  The library keeps one scratch area per (device, stream),
+// grown on demand; calls on one stream run in order, so they share it safely.
+struct TcPlan {
+    TcParams p;
+    int grid = 0;
+    size_t smem = 0;
+    uint32_t mv = 0;
+    size_t off_part = 0, off_cnt = 0, bytes = 0;   // scratch layout (activation tiles at 0)
+};
+
+size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+bool tc_eligible(const qraf_weight_t& w) {
+    return w.block_size == 32 && (w.cols % 32) == 0 && (w.row_bytes % 16) == 0 && aligned16(w.data) && w.rows > 0 &&
+           w.cols > 0;
+}
+
+// M: vectors of one launch pair (1..64).
+bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* out) {
+    if (!tc_eligible(w) || M == 0 || M > kTcMaxVectors) return false;
+    const bool q4 = w.dtype == QRAF_DTYPE_Q4_0;
+    TcParams& p = out->p;
+    out->mv = M <= 16 ? 16u : (M <= 32 ? 32u : 64u);
+    p.w = static_cast<const uint8_t*>(w.data);
+    p.row_bytes = w.row_bytes;
+    p.N = w.rows;
+    p.M = M;
+    p.nblk = w.cols / 32u;
+    p.n_pad = 2u * out->mv;
+    p.act_stride = p.n_pad * 64u + out->mv * 4u;
+    p.unit_blocks = q4 ? 8u : 4u;
+    if (p.nblk % p.unit_blocks) return false;
+    p.upt = p.nblk / p.unit_blocks;
+    p.tiles = (w.rows + kTcRows - 1) / kTcRows;
+    const uint64_t units = static_cast<uint64_t>(p.tiles) * p.upt;
+    if (units > 0xFFFFFFFFull / static_cast<uint64_t>(dev.sm_count)) return false;
+    p.units = static_cast<uint32_t>(units);
+    p.nab = 8;
+    p.nd = std::min(8u, kTcTmemCols / p.n_pad);   // even: the epilogue may take blocks in pairs
+    p.ns = 16;
+    p.pdl = 1;
+    out->grid = static_cast<int>(std::min<uint64_t>(dev.sm_count, units));
+    // Shared memory: an A ring of 8 blocks (the MMA round trip is long), the
+    // scale ring, an activation ring of 8 blocks (fewer for wide batches) and
+    // as many raw units (18 KB each, up to 8) as fit.
+    const size_t avail = static_cast<size_t>(dev.smem_optin) - kSmemReserve;
+    auto layout = [&](uint32_t nraw, uint32_t nbb) {
+        return static_cast<size_t>(nraw) * kTcRawSlot + p.nab * kTcASlot + static_cast<size_t>(nbb) * p.act_stride +
+               p.ns * kTcRows * 4u + 8u * (2u * nraw + 2u * p.nab + 2u * nbb + 2u * p.nd + 2u * p.ns + 2u) + 16u;
+    };
+    p.nbb = 8;
+    p.nraw = 8;
+    while (p.nraw > 4 && layout(p.nraw, p.nbb) > avail) --p.nraw;
+    while (p.nbb > 4 && layout(p.nraw, p.nbb) > avail) --p.nbb;
+    while (p.nraw > 2 && layout(p.nraw, p.nbb) > avail) --p.nraw;
+    if (layout(p.nraw, p.nbb) > avail) return false;
+    out->smem = layout(p.nraw, p.nbb);
+    // One CTA per SM: the kernel takes all 512 TMEM columns, so a second CTA on
+    // the SM would only wait for them.
+    out->smem = std::max<size_t>(out->smem, 120u * 1024u);
+    if (out->smem + kSmemReserve > static_cast<size_t>(dev.smem_optin)) return false;
+    out->off_part = round256(static_cast<size_t>(p.nblk) * p.act_stride);
+    out->off_cnt = out->off_part + round256(static_cast<size_t>(out->grid) * 2u * M * kTcRows * sizeof(float));
+    out->bytes = out->off_cnt + round256(static_cast<size_t>(p.tiles) * sizeof(uint32_t));
+    return true;
+}
+
+struct TcScratch {
+    uint8_t* base = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_scratch_mutex;
+std::map<std::pair<int, cudaStream_t>, TcScratch> g_scratch;
+
+int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out) {
+    int dev = 0;
+    QRAF_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_scratch_mutex);
+    TcScratch& s = g_scratch[{dev, st}];
+    if (s.bytes < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        QRAF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+            return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs %zu bytes of scratch on this stream; make a "
+                                              "first call of this size on the stream before capturing it", bytes);
+        if (s.base) {
+            QRAF_CUDA_TRY(cudaStreamSynchronize(st));
+            cudaFree(s.base);
+            s.base = nullptr;
+            s.bytes = 0;
+        }
+        if (cudaMalloc(&s.base, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            s.base = nullptr;
+            return fail(QRAF_ERR_NOMEM, "tensor-core scratch of %zu bytes could not be allocated", bytes);
+        }
+        s.bytes = bytes;
+    }
+    *out = s.base;
+    return QRAF_OK;
+}
+
+void tc_scratch_release() {
+    std::lock_guard<std::mutex> lk(g_scratch_mutex);
+    for (auto& kv : g_scratch) {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        cudaSetDevice(kv.first.first);
+        cudaDeviceSynchronize();
+        if (kv.second.base) cudaFree(kv.second.base);
+        cudaSetDevice(cur);
+    }
+    g_scratch.clear();
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link to libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+bool weight_map(const qraf_weight_t& w, CUtensorMap* map) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode_tiled) return false;
+    // the weight as [rows][row_bytes / 4] 32-bit words; a box is 128 rows x 144 bytes
+    const cuuint64_t dims[2] = {w.row_bytes / 4u, w.rows};
+    const cuuint64_t strides[1] = {w.row_bytes};
+    const cuuint32_t box[2] = {kTcUnitBytes / 4u, kTcRows};
+    const cuuint32_t estr[2] = {1, 1};
+    return g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w.data), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <uint32_t DT, uint32_t MV>
+cudaError_t launch_tc_mv(const TcPlan& pl, const CUtensorMap& map, const float* x, uint32_t K, bool pdl_prep,
+                         cudaStream_t st) {
+    const TcParams& p = pl.p;
+    const uint64_t threads = static_cast<uint64_t>(p.nblk) * MV * 32u;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cfg.numAttrs = pdl_prep ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_prep_kernel<DT>, x, const_cast<uint8_t*>(p.act), p.tile_count, p.tiles,
+                                       K, p.M, p.nblk, p.n_pad, pdl_prep ? 1u : 0u);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.numAttrs = 1;   // weights stream while the prep kernel runs; activations wait for it
+    return cudaLaunchKernelEx(&cfg, qmm_tc_kernel<DT, MV>, map, p);
+}
+
+template <uint32_t DT>
+cudaError_t launch_tc_dt(const TcPlan& pl, const CUtensorMap& map, const float* x, uint32_t K, bool pdl_prep,
+                         cudaStream_t st) {
+    if (pl.mv == 16) return launch_tc_mv<DT, 16>(pl, map, x, K, pdl_prep, st);
+    if (pl.mv == 32) return launch_tc_mv<DT, 32>(pl, map, x, K, pdl_prep, st);
+    return launch_tc_mv<DT, 64>(pl, map, x, K, pdl_prep, st);
+}
+
+// Y = W X on the tensor cores, in groups of up to 64 vectors, with scratch at
+// `scratch` (pl.bytes for the largest group; nullptr: the stream's own area).
+int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool overlap, cudaStream_t st,
+              const DeviceInfo& dev, uint8_t* scratch, size_t scratch_cap) {
+    TcPlan pl;
+    const uint32_t first = std::min(M, kTcMaxVectors);
+    if (!plan_tc(w, first, dev, &pl)) return fail(QRAF_ERR_UNSUPPORTED, "no tensor-core plan for this weight");
+    CUtensorMap map;
+    if (!weight_map(w, &map)) return fail(QRAF_ERR_CUDA, "could not describe the weight to the TMA unit");
+    uint8_t* base = scratch;
+    if (!base) {
+        const int rc = tc_scratch(st, pl.bytes, &base);
+        if (rc) return rc;
+    } else if (scratch_cap < pl.bytes) {
+        return fail(QRAF_ERR_INVALID, "this call needs %zu bytes of scratch, more than the %zu available", pl.bytes,
+                    scratch_cap);
+    }
+    for (uint32_t m0 = 0; m0 < M; m0 += kTcMaxVectors) {
+        const uint32_t cnt = std::min(kTcMaxVectors, M - m0);
+        TcPlan one;
+        if (!plan_tc(w, cnt, dev, &one)) return fail(QRAF_ERR_UNSUPPORTED, "no tensor-core plan for %u vectors", cnt);
+        one.p.act = base;
+        one.p.partial = reinterpret_cast<float*>(base + one.off_part);
+        one.p.tile_count = reinterpret_cast<uint32_t*>(base + one.off_cnt);
+        one.p.y = y + static_cast<size_t>(m0) * w.rows;
+        const float* xm = x + static_cast<size_t>(m0) * w.cols;
+        const bool pdl_prep = overlap || m0 > 0;
+        const cudaError_t e = w.dtype == QRAF_DTYPE_Q8_0 ? launch_tc_dt<kDtypeQ8>(one, map, xm, w.cols, pdl_prep, st)
+                                                         : launch_tc_dt<kDtypeQ4>(one, map, xm, w.cols, pdl_prep, st);
+        if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "tensor-core launch: %s", cudaGetErrorString(e));
+    }
+    return QRAF_OK;
+}
+
 int check_weight(const qraf_weight_t* w) {
     if (!w) return fail(QRAF_ERR_INVALID, "weight is NULL");
     if (!known_dtype(w->dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", w->dtype);
@@ -325,9 +540,9 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
     if (rc) return rc;
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
     int mode = mode_in & 0xFF;
-    if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
-    if (mode == QRAF_MODE_TC) return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core tile is not built in this library");
-    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
+    if (mode == QRAF_MODE_AUTO) mode = (M >= 16 && tc_eligible(*w)) ? QRAF_MODE_TC : QRAF_MODE_FAST;
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC)
+        return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
     if (M == 0 || w->rows == 0) return QRAF_OK;
     if (!y) return fail(QRAF_ERR_INVALID, "y is NULL");
     if (w->cols == 0) {   // an empty dot is 0 (quantize.cpp:189-209 with no blocks); x is not read
@@ -338,6 +553,12 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
     DeviceInfo* dev = nullptr;
     rc = ensure_device(nullptr, &dev);
     if (rc) return rc;
+    if (mode == QRAF_MODE_TC) {
+        if (!tc_eligible(*w))
+            return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs block size 32, K a multiple of %u and "
+                                              "16-byte-aligned weights", w->dtype == QRAF_DTYPE_Q4_0 ? 256 : 128);
+        return matmul_tc(*w, x, y, M, overlap, st, *dev, nullptr, 0);
+    }
     const bool exact = (mode == QRAF_MODE_EXACT);
 
     // Row-owner streaming kernel: EXACT for any M (vectors in groups that fit in
@@ -877,6 +1098,7 @@ int qraf_cuda_host_cache_clear(void) {
 
 int qraf_cuda_shutdown(void) {
     qraf_cuda_host_cache_clear();
+    tc_scratch_release();
     std::lock_guard<std::mutex> lk(g_host_mutex);
     int cur = 0;
     cudaGetDevice(&cur);

@@ -107,6 +107,11 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// Programmatic dependent launch: wait for the previous grid in the stream to
+// complete (its memory visible), and let the next grid start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ── packed fp32x2 arithmetic (sm_100a), IEEE round-to-nearest, no ftz ────
 // CUDA's float2 intrinsics.  Used where rounding order is free (FAST mode):
 // a packed multiply followed by a packed add was measured to round like a

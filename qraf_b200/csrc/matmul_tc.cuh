@@ -1,0 +1,617 @@
+// matmul_tc.cuh — tensor-core path (tcgen05 + TMEM) for batches of activation
+// vectors: Y[m][n] = sum_b scale[n][b] * sum_{i<32} q[n][32b+i] * X[m][32b+i],
+// the reference's dispatch_matvec_q applied to M vectors
+// (src/nn/backend.cpp:131-199, batched as in include/runtime/batch_scheduler.h:187-228).
+//
+// Arithmetic.  Each 32-element activation block is written as integers
+// X = rint(x * 2^(23-e)) (2^e > max |x| of the block), split into two limbs
+// X = 4096 * hi + lo with |hi|, |lo| <= 2048, which fp16 holds exactly.  Weight
+// codes are fp16 too (Q8: -127..127, Q4: -8..7).  One kind::f16 MMA per
+// 16-element half-block accumulates q * limb products in fp32; every product
+// and partial sum is an integer below 2^24, so the per-block sums
+//     D_hi[n][m][b] = sum_i q[n][i] hi[m][i],   D_lo = sum_i q[n][i] lo[m][i]
+// are exact (the "per-block partial integer sums").  The epilogue forms
+//     y[n][m] += fl(4096 D_hi + D_lo) * fl(scale[n][b] * 2^(e[m][b]-23))
+// in fp32 on the CUDA cores, block by block.
+//
+// Work split.  A unit is 128 weight rows (the MMA's M) by 144 bytes of each
+// row (8 Q4 blocks or 4 Q8 blocks; 144 keeps every copy 16-byte aligned),
+// fetched by one 2-D TMA copy (the weight seen as [N][row_bytes / 4] words).
+// The grid is persistent (one CTA per SM) and CTA c takes the contiguous
+// units [c*U/C, (c+1)*U/C) in tile-major order ("stream-K"), so every SM gets
+// the same number of weight bytes whatever the shape.  A tile covered by one
+// CTA is written straight to y; a tile shared by several CTAs is summed from
+// their partial results (scratch memory) by the last of them to finish, in CTA
+// order, so results are deterministic.
+//
+// Warps (thread = weight row): 0-7 run the epilogue in two groups that split
+// the vectors (warp w reads TMEM lanes 32(w%4)..+31), 8-11 turn the raw bytes
+// of each block into fp16 codes in the MMA's shared-memory layout and pass the
+// block scales on through a small ring of their own.  Warp 12 streams the raw
+// weight units, warp 13 allocates TMEM and issues the MMAs, warp 14 streams
+// the prepared activation tiles.  Loops keep their ring positions as counters
+// (no division).  Every wait is bounded.
+#pragma once
+
+#include <cuda.h>   // CUtensorMap
+
+#include "common.cuh"
+
+namespace qraf_dev {
+
+constexpr uint32_t kTcRows = 128;           // weight rows per tile = MMA M = TMEM lanes
+constexpr uint32_t kTcUnitBytes = 144;      // raw bytes per row per unit
+constexpr uint32_t kTcRawSlot = kTcRows * kTcUnitBytes;
+constexpr uint32_t kTcASlot = kTcRows * 64; // one block of fp16 codes: two K=16 tiles of 4 KB
+constexpr uint32_t kTcThreads = 480;
+constexpr uint32_t kTcWarpXf = 8, kTcWarpRaw = 12, kTcWarpMma = 13, kTcWarpAct = 14;
+constexpr uint32_t kTcTmemCols = 512;
+constexpr uint32_t kTcMaxVectors = 64;      // activation vectors per launch (MMA N = 2 x 64)
+
+struct TcParams {
+    const uint8_t* w;        // [N][row_bytes], native blocks
+    const uint8_t* act;      // prepared activation tiles: [nblk][act_stride] bytes, each the fp16 limb
+                             // tile (n_pad * 64 bytes) followed by the MV block factors 2^(e - 23)
+    float* y;                // [M][N]
+    float* partial;          // [gridDim][2][M][128]
+    uint32_t* tile_count;    // [tiles], zeroed by the prep kernel of the same call
+    uint64_t row_bytes;
+    uint32_t N, M, nblk;
+    uint32_t n_pad;          // MMA N: 2 x (vectors rounded up to 16, 32 or 64)
+    uint32_t act_stride;     // n_pad * 64 + MV * 4
+    uint32_t unit_blocks;    // 8 (Q4) or 4 (Q8)
+    uint32_t upt;            // units per tile = nblk / unit_blocks
+    uint32_t tiles, units;
+    uint32_t nraw, nab, nbb, nd, ns;   // ring depths: raw units; weight, activation, accumulator, scale blocks
+    uint32_t pdl;
+};
+
+// ── shared-memory matrix layout (tcgen05 "canonical" K-major, no swizzle) ──
+// A K=16 tile of R rows is R/8 groups of 256 bytes; each group holds two 8x8
+// core matrices of fp16 (K 0-7 then K 8-15, 128 bytes apart), each core
+// matrix 8 rows of 16 bytes.  Leading-dimension offset 128, stride 256.
+__device__ __forceinline__ uint32_t tc_chunk_off(uint32_t row, uint32_t c) {
+    return (row >> 3) * 256u + c * 128u + (row & 7u) * 16u;
+}
+
+__device__ __forceinline__ uint64_t tc_smem_desc(const void* p) {
+    const uint32_t a = smem_u32(p);
+    uint64_t d = static_cast<uint64_t>((a >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(128u >> 4) << 16;   // leading-dimension byte offset
+    d |= static_cast<uint64_t>(256u >> 4) << 32;   // stride byte offset
+    d |= static_cast<uint64_t>(1u) << 46;          // descriptor version (sm_100)
+    return d;                                      // base offset 0, no swizzle
+}
+
+// Position of element i (0..31) of a block inside its two K=16 tiles.  Q4
+// codes are laid out in the order their nibbles unpack (per 8 elements:
+// 0,2,4,6,1,3,5,7); the activation tiles use the same order.
+template <uint32_t DT>
+__device__ __forceinline__ uint32_t tc_k_slot(uint32_t i) {
+    const uint32_t l = i & 7u;
+    const uint32_t s = DT == kDtypeQ4 ? ((l & 1u) ? 4u + (l >> 1) : (l >> 1)) : l;
+    return (i & ~7u) | s;
+}
+
+// ── tcgen05 wrappers ───────────────────────────────────────────────────────
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One tile of a 2-D tensor map (no multicast) into shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ── activation preparation: x (fp32) -> fp16 limb tiles + block factors ────
+// One warp per (block b, vector slot m); lane i takes element i.  Tile rows
+// 2m / 2m+1 hold hi / lo of vector m; rows of vectors >= M are zero; the
+// block's factors follow the tile (one float per vector slot).  Also
+// zeroes the stream-K tile counters of the call.  A block holding a NaN or an
+// infinity gets a NaN factor, so its outputs come out NaN.
+template <uint32_t DT>
+__global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ x, uint8_t* __restrict__ act,
+                                                      uint32_t* __restrict__ tile_count, uint32_t tiles, uint32_t K,
+                                                      uint32_t M, uint32_t nblk, uint32_t n_pad, uint32_t pdl) {
+    if (pdl) pdl_wait();
+    if (pdl) pdl_launch_dependents();
+    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    for (uint32_t i = tid; i < tiles; i += gridDim.x * blockDim.x) tile_count[i] = 0u;
+    const uint32_t half = n_pad >> 1;
+    const uint32_t gw = tid >> 5, lane = threadIdx.x & 31u;
+    if (gw >= nblk * half) return;
+    const uint32_t b = gw / half, m = gw % half;
+    float v = 0.0f;
+    if (m < M) v = __ldcg(x + static_cast<size_t>(m) * K + 32u * b + lane);
+    float mx = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    const bool finite = !__any_sync(0xFFFFFFFFu, !(fabsf(v) <= 3.402823466e38f));   // no NaN / inf in the block
+    // 2^e > mx: e = biased exponent - 126 for normal mx (and -126 for zero / subnormal)
+    const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
+    const int e = (ex == 0 ? 1 : ex) - 126;
+    int X = finite ? __float2int_rn(ldexpf(v, 23 - e)) : 0;
+    const int hi = (X + 2048) >> 12;
+    const int lo = X - hi * 4096;
+    const uint32_t pos = tc_k_slot<DT>(lane);
+    const uint32_t t = pos >> 4, c = (pos >> 3) & 1u, s = pos & 7u;
+    uint8_t* blk = act + static_cast<size_t>(b) * (n_pad * 64u + half * 4u);
+    uint8_t* tile = blk + t * (n_pad * 32u);
+    *reinterpret_cast<__half*>(tile + tc_chunk_off(2u * m, c) + 2u * s) = __int2half_rn(hi);
+    *reinterpret_cast<__half*>(tile + tc_chunk_off(2u * m + 1u, c) + 2u * s) = __int2half_rn(lo);
+    if (lane == 0)
+        reinterpret_cast<float*>(blk + n_pad * 64u)[m] = m >= M ? 0.0f : finite ? ldexpf(1.0f, e - 23) : __int_as_float(0x7FC00000);
+}
+
+// ── raw block bytes -> fp16 codes in the A layout ───────────────────────────
+// q: the row's 144 raw bytes of the current unit (36 words).  Writes block j's
+// 32 codes (four 16-byte chunks) for row `row` and returns its scale.
+template <uint32_t DT>
+__device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uint32_t j, uint8_t* a_slot, uint32_t row) {
+    if constexpr (DT == kDtypeQ8) {
+        // block j: word 9j = fp32 scale, words 9j+1..9j+8 = codes.  Code byte c
+        // (sign bit flipped) under 0x64 is the fp16 1024 + c + 128, exactly.
+        const float sc = __uint_as_float(q[9 * j]);
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {   // 8 codes per 16-byte chunk
+            const uint32_t w0 = q[9 * j + 1 + 2 * ch] ^ 0x80808080u, w1 = q[9 * j + 2 + 2 * ch] ^ 0x80808080u;
+            uint32_t h[4];
+            h[0] = __byte_perm(w0, 0x64646464u, 0x4140u);
+            h[1] = __byte_perm(w0, 0x64646464u, 0x4342u);
+            h[2] = __byte_perm(w1, 0x64646464u, 0x4140u);
+            h[3] = __byte_perm(w1, 0x64646464u, 0x4342u);
+            const __half2 off = __halves2half2(__ushort_as_half(0x6480u), __ushort_as_half(0x6480u));   // 1152
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                __half2 hv = *reinterpret_cast<__half2*>(&h[k]);
+                hv = __hsub2(hv, off);
+                h[k] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            const uint32_t tt = ch >> 1, cc = ch & 1;
+            *reinterpret_cast<uint4*>(a_slot + tt * 4096u + tc_chunk_off(row, cc)) = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+        return sc;
+    } else {
+        // block j at byte 18j: fp16 scale, then 16 bytes of nibbles.  For even
+        // j the block starts on a word; for odd j two bytes into one.
+        const uint32_t w0 = (9u * j) >> 1;   // word holding the block's first byte
+        uint32_t nib[4];
+        uint32_t s16;
+        if ((j & 1u) == 0u) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) nib[k] = __funnelshift_r(q[w0 + k], q[w0 + k + 1], 16);
+            s16 = q[w0] & 0xFFFFu;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) nib[k] = q[w0 + 1 + k];
+            s16 = q[w0] >> 16;
+        }
+        const __half2 off = __halves2half2(__ushort_as_half(0x6408u), __ushort_as_half(0x6408u));   // 1032
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {   // nibble word ch = elements 8ch..8ch+7
+            const uint32_t lo4 = nib[ch] & 0x0F0F0F0Fu, hi4 = (nib[ch] >> 4) & 0x0F0F0F0Fu;
+            uint32_t h[4];
+            h[0] = __byte_perm(lo4, 0x64646464u, 0x4140u);   // elements 0, 2
+            h[1] = __byte_perm(lo4, 0x64646464u, 0x4342u);   // 4, 6
+            h[2] = __byte_perm(hi4, 0x64646464u, 0x4140u);   // 1, 3
+            h[3] = __byte_perm(hi4, 0x64646464u, 0x4342u);   // 5, 7
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                __half2 hv = *reinterpret_cast<__half2*>(&h[k]);
+                hv = __hsub2(hv, off);
+                h[k] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+            const uint32_t tt = ch >> 1, cc = ch & 1;
+            *reinterpret_cast<uint4*>(a_slot + tt * 4096u + tc_chunk_off(row, cc)) = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+        return half_bits_to_float(s16);
+    }
+}
+
+// Wait by lane 0 for the whole warp (every lane takes the same branch after).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok = 1u;
+    if ((threadIdx.x & 31u) == 0u) ok = mbar_wait(bar, parity) ? 1u : 0u;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    __syncwarp();
+    return ok != 0u;
+}
+
+// Position in a ring of n slots, advanced one step at a time (no division in
+// the loops): `phase` is the parity of the slot's current fill, `wrapped` says
+// whether every slot has been filled once (from then on a producer waits for
+// the consumer's previous phase, parity phase ^ 1).
+struct Ring {
+    uint32_t slot = 0, phase = 0, n;
+    bool wrapped = false;
+    __device__ explicit Ring(uint32_t n_) : n(n_) {}
+    __device__ __forceinline__ void next() {
+        if (++slot == n) {
+            slot = 0;
+            phase ^= 1u;
+            wrapped = true;
+        }
+    }
+};
+
+// CTA that owns unit u (CTA c owns [floor(c U / C), floor((c+1) U / C))).
+__device__ __forceinline__ uint32_t tc_owner(uint32_t u, uint32_t units, uint32_t C) {
+    return static_cast<uint32_t>(((static_cast<uint64_t>(u) + 1u) * C - 1u) / units);
+}
+__device__ __forceinline__ uint32_t tc_start(uint32_t c, uint32_t units, uint32_t C) {
+    return static_cast<uint32_t>(static_cast<uint64_t>(c) * units / C);
+}
+
+// ── the tensor-core kernel ─────────────────────────────────────────────────
+// MV: activation vectors handled per launch (16, 32 or 64); n_pad = 2 MV.
+template <uint32_t DT, uint32_t MV>
+__global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
+    constexpr uint32_t UB = DT == kDtypeQ4 ? 8u : 4u;   // blocks per raw unit
+    constexpr uint32_t HV = MV / 2;                      // vectors per epilogue group
+    constexpr bool PAIR = MV <= 32;                      // epilogue takes two blocks per pass
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    uint8_t* raw = smem;
+    uint8_t* abuf = raw + p.nraw * kTcRawSlot;
+    uint8_t* bbuf = abuf + p.nab * kTcASlot;
+    float* sring = reinterpret_cast<float*>(bbuf + p.nbb * p.act_stride);
+    uint64_t* raw_full = reinterpret_cast<uint64_t*>(sring + p.ns * kTcRows);
+    uint64_t* raw_empty = raw_full + p.nraw;
+    uint64_t* a_full = raw_empty + p.nraw;
+    uint64_t* a_empty = a_full + p.nab;
+    uint64_t* b_full = a_empty + p.nab;
+    uint64_t* b_empty = b_full + p.nbb;
+    uint64_t* d_full = b_empty + p.nbb;
+    uint64_t* d_empty = d_full + p.nd;
+    uint64_t* s_full = d_empty + p.nd;
+    uint64_t* s_empty = s_full + p.ns;
+    uint64_t* comb = s_empty + p.ns;            // [2]: partial results stored / decision made
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(comb + 2);
+    uint32_t* bcast = tmem_slot + 1;
+
+    if (blockDim.x != kTcThreads || p.n_pad != 2u * MV || p.M > MV || p.unit_blocks != UB || (PAIR && (p.nd & 1u))) {
+        if (threadIdx.x == 0) raise_error(kErrBadLaunch);
+        return;
+    }
+    const uint32_t C = gridDim.x, cta = blockIdx.x;
+    const uint32_t u0 = tc_start(cta, p.units, C), u1 = tc_start(cta + 1, p.units, C);
+    const uint32_t nunits = u1 - u0, nstages = nunits * UB;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < p.nraw; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], 4);    // transform warps
+        }
+        for (uint32_t i = 0; i < p.nab; ++i) {
+            mbar_init(&a_full[i], 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (uint32_t i = 0; i < p.nbb; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 8);      // the epilogue reads the factors after the MMA
+        }
+        for (uint32_t i = 0; i < p.nd; ++i) {
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], 8);
+        }
+        for (uint32_t i = 0; i < p.ns; ++i) {
+            mbar_init(&s_full[i], 4);
+            mbar_init(&s_empty[i], 8);
+        }
+        mbar_init(&comb[0], 8);
+        mbar_init(&comb[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == kTcWarpMma) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTcTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (p.pdl) pdl_launch_dependents();
+
+    const uint32_t k0 = u0 % p.upt, tile0 = u0 / p.upt;   // the CTA's first unit: column k0 of tile0
+    if (warp == kTcWarpRaw) {
+        // ── raw weight units: weights are immutable, so they stream before the dependency wait
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+            const uint64_t pol = policy_evict_first();
+            Ring r(p.nraw);
+            uint32_t k = k0, tile = tile0, issued = 0;
+            for (uint32_t i = 0; i < nunits; ++i) {
+                if (r.wrapped && !mbar_wait(&raw_empty[r.slot], r.phase ^ 1u)) break;
+                mbar_arrive_expect_tx(&raw_full[r.slot], kTcRawSlot);   // rows past N arrive as zeros
+                tma_load_2d(raw + r.slot * kTcRawSlot, &wmap, static_cast<int>(k * (kTcUnitBytes / 4u)),
+                            static_cast<int>(tile * kTcRows), &raw_full[r.slot], pol);
+                ++issued;
+                r.next();
+                if (++k == p.upt) {
+                    k = 0;
+                    ++tile;
+                }
+            }
+            // the last unit issued into each slot has landed before the CTA leaves
+            for (uint32_t i = issued > p.nraw ? issued - p.nraw : 0; i < issued; ++i)
+                mbar_wait(&raw_full[i % p.nraw], (i / p.nraw) & 1u);
+        }
+    } else if (warp == kTcWarpAct) {
+        // ── prepared activation tiles (written by the prep kernel just before)
+        if (lane == 0) {
+            if (p.pdl) pdl_wait();
+            Ring r(p.nbb);
+            uint32_t issued = 0;
+            const uint8_t* src = p.act + static_cast<size_t>(k0) * UB * p.act_stride;
+            const uint8_t* row_end = p.act + static_cast<size_t>(p.upt) * UB * p.act_stride;
+            for (uint32_t st = 0; st < nstages; ++st) {
+                if (r.wrapped && !mbar_wait(&b_empty[r.slot], r.phase ^ 1u)) break;
+                mbar_arrive_expect_tx(&b_full[r.slot], p.act_stride);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_u32(bbuf + r.slot * p.act_stride)),
+                    "l"(src), "r"(p.act_stride), "r"(smem_u32(&b_full[r.slot]))
+                    : "memory");
+                ++issued;
+                r.next();
+                src += p.act_stride;
+                if (src == row_end) src = p.act;   // the next tile starts again at block 0
+            }
+            for (uint32_t st = issued > p.nbb ? issued - p.nbb : 0; st < issued; ++st)
+                mbar_wait(&b_full[st % p.nbb], (st / p.nbb) & 1u);
+        }
+    } else if (warp == kTcWarpMma) {
+        // ── MMA issue: per block, two K=16 MMAs into a fresh accumulator
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4)                            // D: fp32
+                                   | ((p.n_pad >> 3) << 17)             // N
+                                   | ((kTcRows >> 4) << 24);            // M = 128; A, B: fp16, K-major
+            const uint64_t a0 = tc_smem_desc(abuf), b0 = tc_smem_desc(bbuf);
+            const uint64_t b_step = static_cast<uint64_t>(p.act_stride >> 4), bk_step = (p.n_pad * 32u) >> 4;
+            Ring ra(p.nab), rb(p.nbb), rd(p.nd);
+            uint32_t issued = 0, last_d = 0, last_phase = 0;
+            for (uint32_t st = 0; st < nstages; ++st) {
+                if (!mbar_wait(&a_full[ra.slot], ra.phase) || !mbar_wait(&b_full[rb.slot], rb.phase)) break;
+                if (rd.wrapped && !mbar_wait(&d_empty[rd.slot], rd.phase ^ 1u)) break;
+                tc_fence_after();
+                const uint64_t da = a0 + static_cast<uint64_t>(ra.slot) * (kTcASlot >> 4);
+                const uint64_t db = b0 + static_cast<uint64_t>(rb.slot) * b_step;
+                const uint32_t d = tmem + rd.slot * p.n_pad;
+                tc_mma_f16(d, da, db, idesc, 0u);
+                tc_mma_f16(d, da + (4096u >> 4), db + bk_step, idesc, 1u);
+                tc_commit(&a_empty[ra.slot]);
+                tc_commit(&d_full[rd.slot]);
+                ++issued;
+                last_d = rd.slot;
+                last_phase = rd.phase;
+                ra.next();
+                rb.next();
+                rd.next();
+            }
+            if (issued) mbar_wait(&d_full[last_d], last_phase);
+        }
+        __syncwarp();
+    } else if (warp >= kTcWarpXf && warp < kTcWarpXf + 4) {
+        // ── transform: raw blocks -> fp16 codes in the A ring, scales into the scale ring
+        const uint32_t row = threadIdx.x - kTcWarpXf * 32u;
+        uint32_t q[36];
+        bool ok = true;
+        Ring rr(p.nraw), ra(p.nab), rs(p.ns);
+        for (uint32_t i = 0; ok && i < nunits; ++i) {
+            if (!warp_wait(&raw_full[rr.slot], rr.phase)) break;
+            const uint4* rp = reinterpret_cast<const uint4*>(raw + rr.slot * kTcRawSlot + row * kTcUnitBytes);
+#pragma unroll
+            for (int k = 0; k < 9; ++k) {
+                const uint4 v = rp[k];
+                q[4 * k] = v.x;
+                q[4 * k + 1] = v.y;
+                q[4 * k + 2] = v.z;
+                q[4 * k + 3] = v.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rr.slot]);
+            rr.next();
+#pragma unroll
+            for (uint32_t j = 0; j < UB; ++j) {
+                if ((ra.wrapped && !warp_wait(&a_empty[ra.slot], ra.phase ^ 1u)) ||
+                    (rs.wrapped && !warp_wait(&s_empty[rs.slot], rs.phase ^ 1u))) {
+                    ok = false;
+                    break;
+                }
+                sring[rs.slot * kTcRows + row] = tc_transform_block<DT>(q, j, abuf + ra.slot * kTcASlot, row);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[ra.slot]);
+                    mbar_arrive(&s_full[rs.slot]);
+                }
+                ra.next();
+                rs.next();
+            }
+        }
+    } else if (warp < 8) {
+        // ── epilogue: thread = weight row = TMEM lane; group g owns vectors [g HV, (g+1) HV)
+        const uint32_t quad = warp & 3u, grp = warp >> 2;
+        const uint32_t row = quad * 32u + lane;
+        const uint32_t tmem_row = tmem + ((quad * 32u) << 16) + grp * MV;   // hi/lo columns of this group
+        const uint32_t m0 = grp * HV;
+        float acc[HV];
+#pragma unroll
+        for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
+        bool waited = false, ok = true;
+        uint32_t ncomb = 0;
+        Ring rb(p.nbb), rd(p.nd), rs(p.ns);
+        uint32_t k = k0, tile = tile0;
+
+        // one block: d[] holds its MV accumulator columns for this group (hi, lo per vector)
+        auto fold = [&](const uint32_t (&d)[MV], float sc, const float* pfb) {
+#pragma unroll
+            for (uint32_t v = 0; v < HV; ++v) {
+                if (m0 + v < p.M) {
+                    const float t = fmaf(__uint_as_float(d[2 * v]), 4096.0f, __uint_as_float(d[2 * v + 1]));
+                    acc[v] = fmaf(t, sc * pfb[m0 + v], acc[v]);
+                }
+            }
+        };
+        auto load_block = [&](uint32_t dslot, uint32_t (&d)[MV]) {
+#pragma unroll
+            for (uint32_t c = 0; c < MV / 16; ++c) {
+                uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&d[16 * c]);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                    : "=r"(part[0]), "=r"(part[1]), "=r"(part[2]), "=r"(part[3]), "=r"(part[4]), "=r"(part[5]),
+                      "=r"(part[6]), "=r"(part[7]), "=r"(part[8]), "=r"(part[9]), "=r"(part[10]), "=r"(part[11]),
+                      "=r"(part[12]), "=r"(part[13]), "=r"(part[14]), "=r"(part[15])
+                    : "r"(tmem_row + dslot * p.n_pad + 16u * c));
+            }
+        };
+        auto release = [&]() {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&d_empty[rd.slot]);
+                mbar_arrive(&b_empty[rb.slot]);
+                mbar_arrive(&s_empty[rs.slot]);
+            }
+            rd.next();
+            rb.next();
+            rs.next();
+        };
+
+        for (uint32_t iu = 0; ok && iu < nunits; ++iu) {
+            const bool seg_first = iu == 0 || k == 0;
+            const bool seg_last = iu + 1 == nunits || k + 1 == p.upt;
+            if (seg_first) {
+#pragma unroll
+                for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
+            }
+            if constexpr (PAIR) {
+#pragma unroll 1
+                for (uint32_t j = 0; j < UB; j += 2) {
+                    // blocks j and j+1 sit in consecutive ring slots (the rings have even depth)
+                    if (!warp_wait(&d_full[rd.slot], rd.phase) || !warp_wait(&d_full[rd.slot + 1], rd.phase) ||
+                        !warp_wait(&s_full[rs.slot], rs.phase) || !warp_wait(&s_full[rs.slot + 1], rs.phase)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t d0[MV], d1[MV];
+                    load_block(rd.slot, d0);
+                    load_block(rd.slot + 1, d1);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    fold(d0, sring[rs.slot * kTcRows + row],
+                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
+                    release();
+                    fold(d1, sring[rs.slot * kTcRows + row],
+                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
+                    release();
+                }
+            } else {
+#pragma unroll 1
+                for (uint32_t j = 0; j < UB; ++j) {
+                    if (!warp_wait(&d_full[rd.slot], rd.phase) || !warp_wait(&s_full[rs.slot], rs.phase)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t d0[MV];
+                    load_block(rd.slot, d0);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    fold(d0, sring[rs.slot * kTcRows + row],
+                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
+                    release();
+                }
+            }
+            if (!ok) break;
+            const uint32_t t_now = tile;
+            if (++k == p.upt) {
+                k = 0;
+                ++tile;
+            }
+            if (!seg_last) continue;
+            // ── the segment of tile t_now ends here: write it, or hand it to the combiner
+            if (p.pdl && !waited) {
+                pdl_wait();
+                waited = true;
+            }
+            const uint32_t t0u = t_now * p.upt, t1u = t0u + p.upt;
+            const uint32_t rows = min(kTcRows, p.N - t_now * kTcRows);
+            float* yt = p.y + static_cast<size_t>(t_now) * kTcRows + row;
+            if (u0 <= t0u && u1 >= t1u) {
+                if (row < rows) {
+#pragma unroll
+                    for (uint32_t v = 0; v < HV; ++v)
+                        if (m0 + v < p.M) yt[static_cast<size_t>(m0 + v) * p.N] = acc[v];
+                }
+                continue;
+            }
+            const uint32_t slot = t_now == tile0 ? 0u : 1u;
+            float* mine = p.partial + (static_cast<size_t>(cta) * 2u + slot) * p.M * kTcRows + row;
+#pragma unroll
+            for (uint32_t v = 0; v < HV; ++v)
+                if (m0 + v < p.M) mine[static_cast<size_t>(m0 + v) * kTcRows] = acc[v];
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&comb[0]);
+            const uint32_t c_first = tc_owner(t0u, p.units, C), c_last = tc_owner(t1u - 1u, p.units, C);
+            if (threadIdx.x == 0) {
+                uint32_t decision = 0;
+                if (mbar_wait(&comb[0], ncomb & 1u)) {
+                    const uint32_t prev = atomicAdd(p.tile_count + t_now, 1u);
+                    decision = prev == c_last - c_first ? 1u : 2u;   // 1: the last one in sums the tile
+                }
+                *reinterpret_cast<volatile uint32_t*>(bcast) = decision;
+                mbar_arrive(&comb[1]);
+            }
+            if (!warp_wait(&comb[1], ncomb & 1u)) break;
+            ++ncomb;
+            if (*reinterpret_cast<volatile uint32_t*>(bcast) != 1u) continue;
+            __threadfence();
+            for (uint32_t v = 0; v < HV && m0 + v < p.M; ++v) {
+                float sum = 0.0f;
+                for (uint32_t cc = c_first; cc <= c_last; ++cc) {
+                    const uint32_t sl = tc_start(cc, p.units, C) / p.upt == t_now ? 0u : 1u;
+                    sum += __ldcg(p.partial + ((static_cast<size_t>(cc) * 2u + sl) * p.M + m0 + v) * kTcRows + row);
+                }
+                if (row < rows) yt[static_cast<size_t>(m0 + v) * p.N] = sum;
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == kTcWarpMma) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+    }
+}
+
+}  // namespace qraf_dev

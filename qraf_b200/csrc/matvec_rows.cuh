@@ -86,8 +86,6 @@ struct RowParams {
     uint32_t world, rank, y_ld, row_off;
 };
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* a, unsigned long long v) {
     asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a), "l"(v) : "memory");

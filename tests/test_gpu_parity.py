@@ -262,6 +262,9 @@ def test_config_exact_and_fast(cuda, digests, config_name, oracle_lib):
         xh = xall[:m].cpu().numpy()
         y64 = np.stack([oracle_lib.matvec_f64(d["dtype"], q_host, d["n"], d["k"], xh[j]) for j in range(m)])
         assert_fast_ok(y_fast, y_exact, y64, f"{config_name} M={m}")
+        if d["k"] % (256 if d["dtype"] == qb.Q4_0 else 128) == 0:
+            y_tc = qb.matvec_q(w, xall[:m].contiguous(), mode=qb.MODE_TC).cpu().numpy()
+            assert_fast_ok(y_tc, y_exact, y64, f"{config_name} M={m} tensor cores")
         if m == 1 and config_name in ys.files:
             assert y_exact[0].tobytes() == ys[config_name].tobytes()
     assert qb.device_status() == qb.OK
