@@ -111,6 +111,25 @@ int qraf_cuda_weight_shard(const qraf_weight_t* full, uint32_t world, uint32_t r
 int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int mode,
                        void* stream);
 
+/* The tensor-core path of qraf_cuda_matvec_q (QRAF_MODE_TC, same kernels and
+ * results) for callers that may not allocate device memory: its scratch (the
+ * prepared activation tiles, the stream-K partial sums and tile counters) lives
+ * in one fixed device array of QRAF_NOALLOC_SCRATCH_BYTES inside the library,
+ * and the call makes no cudaMalloc, cudaFree or other allocating call.  No
+ * counterpart in the reference (its CPU path needs no scratch).
+ *  - A call whose scratch would exceed QRAF_NOALLOC_SCRATCH_BYTES is rejected
+ *    with QRAF_ERR_INVALID and a message naming both sizes (among the
+ *    BASELINE shapes: only K = 28672 with more than 60 vectors in one call).
+ *  - The first call on a device does the set-up (looks up the array's device
+ *    address); make that first call before any stream capture.
+ *  - Every call on a device shares the array: calls that overlap on the GPU
+ *    (on different streams, or from different threads without ordering) race.
+ *    What must start at zero is cleared by each call's own first kernel.
+ *  - flags: QRAF_MODE_FLAG_OVERLAP or 0. */
+#define QRAF_NOALLOC_SCRATCH_BYTES (16u << 20)
+int qraf_cuda_matmul_tc_noalloc(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int flags,
+                                void* stream);
+
 /* One quantized row dotted with x (dot_q8_0_f32 / dot_q4_0_f32,
  * quantize.cpp:187-239); *out_dev receives the fp32 result. */
 int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint64_t count, uint32_t block_size,

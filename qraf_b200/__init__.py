@@ -80,6 +80,7 @@ def _load() -> C.CDLL:
         "qraf_cuda_weight_free": (i32, [W]),
         "qraf_cuda_weight_shard": (i32, [W, u32, u32, W]),
         "qraf_cuda_matvec_q": (i32, [W, vp, vp, u32, i32, vp]),
+        "qraf_cuda_matmul_tc_noalloc": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
         "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
         "qraf_cuda_quantize": (i32, [u32, vp, u64, u32, vp, vp]),

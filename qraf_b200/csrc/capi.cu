@@ -787,6 +787,48 @@ int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev,
     return matvec_impl(w, x_dev, y_dev, M, mode, static_cast<cudaStream_t>(stream));
 }
 
+// ── the tensor-core path without allocation ───────────────────────────────
+// Its scratch: one fixed array per device, shared by every call on that device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[QRAF_NOALLOC_SCRATCH_BYTES];
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_ptr[64] = {};
+
+int qraf_cuda_matmul_tc_noalloc(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int flags,
+                                void* stream) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if ((flags & ~QRAF_MODE_FLAG_OVERLAP) != 0) return fail(QRAF_ERR_INVALID, "unknown flags 0x%x", flags);
+    if (M == 0 || w->rows == 0) return QRAF_OK;
+    if (!x_dev || !y_dev) return fail(QRAF_ERR_INVALID, "x or y is NULL");
+    if (!tc_eligible(*w))
+        return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs block size 32, K a multiple of %u and "
+                                          "16-byte-aligned weights", w->dtype == QRAF_DTYPE_Q4_0 ? 256 : 128);
+    int dev_index = 0;
+    DeviceInfo* dev = nullptr;
+    rc = ensure_device(&dev_index, &dev);
+    if (rc) return rc;
+    TcPlan pl;
+    if (!plan_tc(*w, std::min(M, kTcMaxVectors), *dev, &pl))
+        return fail(QRAF_ERR_UNSUPPORTED, "no tensor-core plan for this weight");
+    if (pl.bytes > QRAF_NOALLOC_SCRATCH_BYTES)
+        return fail(QRAF_ERR_INVALID, "this call needs %zu bytes of scratch, more than the %u bytes of the "
+                                      "no-allocation scratch array", pl.bytes, QRAF_NOALLOC_SCRATCH_BYTES);
+    void* base = nullptr;
+    {
+        // set-up, once per device, with that device current
+        std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+        if (!g_noalloc_ptr[dev_index]) {
+            const cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return fail(QRAF_ERR_CUDA, "cudaGetSymbolAddress of the scratch array: %s", cudaGetErrorString(e));
+            g_noalloc_ptr[dev_index] = base;
+        }
+        base = g_noalloc_ptr[dev_index];
+    }
+    return matmul_tc(*w, x_dev, y_dev, M, (flags & QRAF_MODE_FLAG_OVERLAP) != 0, static_cast<cudaStream_t>(stream),
+                     *dev, static_cast<uint8_t*>(base), QRAF_NOALLOC_SCRATCH_BYTES);
+}
+
 int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint64_t count, uint32_t block_size,
                     float* out_dev, int mode, void* stream) {
     if (count > 0xFFFFFFFFull) return fail(QRAF_ERR_INVALID, "count %llu exceeds 2^32-1", static_cast<unsigned long long>(count));
