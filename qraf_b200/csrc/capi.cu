@@ -210,23 +210,53 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     const uint32_t grid = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), w.rows);
     const uint32_t rows_base = w.rows / grid, rows_extra = w.rows % grid;
     const uint32_t max_rows = rows_base + (rows_extra ? 1u : 0u);
+    const uint32_t bb = w.dtype == QRAF_DTYPE_Q8_0 ? 36u : 18u;
+    uint32_t G = 1, piece = nblk, npieces = 1;
     // Rows per stage: enough stages to keep all warps busy, then as many rows as
-    // fit ~18 KB (more rows share each staged activation block).
-    uint32_t G = 1;
+    // fit ~18 KB (more rows share each staged activation block).  Whole rows.
     while (G < kRowGMax && (2 * G) * rb <= 18432 && 5 * ((max_rows + 2 * G - 1) / (2 * G)) >= 4 * kRowWarps) G *= 2;
     if (!exact && mcount == 2) G = 2;
-    const uint32_t slot_stride = static_cast<uint32_t>((G * rb + 127) / 128 * 128);
+    const bool long_rows = 2 * rb > 18432;                                   // not even 2 whole rows per stage
+    const bool few_stages = (max_rows + G - 1) / G < static_cast<uint32_t>(kRowWarps) / 2;   // most warps idle
+    if (!exact && (long_rows || few_stages)) {
+        // FAST: cut rows into pieces of K so that 4 rows share each staged
+        // activation block (2 for two vectors) and there are about three stages
+        // per warp, each within ~18 KB; pieces are summed in order at the end.
+        G = mcount == 2 ? 2u : 4u;
+        while (G > 1 && G > max_rows) G >>= 1;
+        const uint32_t groups = (max_rows + G - 1) / G;
+        const uint32_t want = (3 * kRowWarps + groups - 1) / groups;
+        piece = (nblk + want - 1) / want;
+        piece = std::max<uint32_t>(std::min<uint32_t>(long_rows ? 32u : 64u, nblk), (piece + 7u) / 8u * 8u);
+        const uint32_t cap = std::max<uint32_t>(8u, 18432u / (G * bb) / 8u * 8u);
+        piece = std::min(std::min(piece, cap), nblk);
+        npieces = (nblk + piece - 1) / piece;
+        if (npieces == 1) piece = nblk;
+    }
     const uint32_t rec = exact ? 144u : kLimbRec;      // bytes per staged 32-element block
     const uint64_t x_bytes = static_cast<uint64_t>(mcount) * nblk * rec;
     const uint32_t pb_row = nblk + 4;
     const uint64_t pb_bytes = exact ? static_cast<uint64_t>(kRowWarps) * G * pb_row * 4u : 0;
-    const uint32_t stages = (max_rows + G - 1) / G;
-    const uint64_t fixed = x_bytes + pb_bytes + 64;
-    auto fit = [&](uint64_t budget) -> uint32_t {
-        if (budget <= fixed) return 0;
-        return static_cast<uint32_t>(std::min<uint64_t>({32u, stages, (budget - fixed) / (slot_stride + 12u)}));
+    const uint64_t budget = std::min<uint64_t>(kPdlSmemBudget, static_cast<uint64_t>(dev.smem_optin - kSmemReserve));
+    uint32_t piece_bytes = 0, slot_stride = 0, nst = 0;
+    uint64_t fixed = 0;
+    auto layout = [&]() {
+        npieces = (nblk + piece - 1) / piece;
+        if (npieces == 1) piece = nblk;
+        piece_bytes = piece * bb;
+        slot_stride = static_cast<uint32_t>(((npieces == 1 ? G * rb : static_cast<uint64_t>(G) * piece_bytes) + 127) / 128 * 128);
+        const uint64_t part_bytes = npieces > 1 ? ((static_cast<uint64_t>(mcount) * max_rows * npieces + 1) & ~1ull) * 4u : 0;
+        const uint32_t stages = (max_rows + G - 1) / G * npieces;
+        fixed = x_bytes + pb_bytes + part_bytes + 64;
+        nst = budget <= fixed ? 0u
+                              : static_cast<uint32_t>(std::min<uint64_t>({32u, stages, (budget - fixed) / (slot_stride + 12u)}));
     };
-    const uint32_t nst = fit(std::min<uint64_t>(kPdlSmemBudget, static_cast<uint64_t>(dev.smem_optin - kSmemReserve)));
+    layout();
+    // Pieces: keep at least 4 stages in flight (smaller pieces if need be).
+    while (npieces > 1 && nst < 4 && piece > 64) {
+        piece = std::max<uint32_t>(64u, (piece / 2 + 7u) / 8u * 8u);
+        layout();
+    }
     if (nst == 0) return false;
     RowParams& p = out->p;
     p.w = static_cast<const uint8_t*>(w.data);
@@ -237,8 +267,11 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.K = w.cols;
     p.M = mcount;
     p.nblk = nblk;
-    p.nchunk = (nblk + 31) / 32;
     p.G = G;
+    p.piece_blocks = piece;
+    p.npieces = npieces;
+    p.piece_bytes = piece_bytes;
+    p.part_rows = max_rows;
     p.nst = nst;
     p.slot_stride = slot_stride;
     p.xs_stride = nblk * rec;

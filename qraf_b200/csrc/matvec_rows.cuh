@@ -60,8 +60,14 @@ struct RowParams {
     float* y;                // [M][N]
     uint64_t row_bytes;
     uint32_t N, K, M;        // M = activation vectors of this launch
-    uint32_t nblk, nchunk;   // K / 32, ceil(nblk / 32)
+    uint32_t nblk;           // K / 32
     uint32_t G;              // rows per stage (1..kRowGMax)
+    // A stage is G rows x one piece of K: pieces of `piece_blocks` blocks
+    // (npieces per row; the last may be shorter; EXACT uses whole rows).  With
+    // several pieces, each stage leaves its G partial sums in shared memory and
+    // the rows are summed piece by piece, in order, at the end.
+    uint32_t piece_blocks, npieces, piece_bytes;
+    uint32_t part_rows;      // rows per CTA the partial-sum buffer is sized for
     uint32_t nst;            // slots in the ring
     uint32_t slot_stride;    // bytes per slot (multiple of 128)
     uint32_t xs_stride;      // bytes per staged activation vector: nblk * 144 (EXACT), nblk * kLimbRec (FAST)
@@ -238,86 +244,100 @@ __device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const Li
     return combine_limbs(d0, d1, d2, d3);
 }
 
-// Turn the staged fp32 activations into limb records, in place: on entry
-// bytes [0, 128) of every record hold the block's 32 floats.  Four threads per
-// block, eight elements each (elements 8*sub .. 8*sub+7, which for Q4 is exactly
-// one group of 8 in the 0,2,4,6,1,3,5,7 order), all of a CTA's blocks in one or
-// a few rounds; the group's maximum and plane sums need two shuffles each.
+// Turn the fp32 activations (global memory, read through L2) into limb records
+// in one pass.  Four threads per block, eight elements each (elements
+// 8*sub .. 8*sub+7, which for Q4 is exactly one group of 8 in the
+// 0,2,4,6,1,3,5,7 order); the group's maximum and plane sums need two shuffles
+// each.  Every thread has the next round's loads in flight while it converts
+// the current one.
 template <uint32_t DT>
-__device__ __forceinline__ void stage_limb_records(uint8_t* xsb, uint32_t xs_stride, uint32_t M, uint32_t nblk,
-                                                   uint32_t tid, uint32_t nthreads) {
+__device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, uint32_t K, uint8_t* xsb,
+                                                   uint32_t xs_stride, uint32_t M, uint32_t nblk, uint32_t tid,
+                                                   uint32_t nthreads) {
     const uint32_t lane = tid & 31u, sub = lane & 3u;
-    const uint32_t total = M * nblk * 4u;
-    for (uint32_t base = tid - lane; base < total; base += nthreads) {
-        const uint32_t task = base + lane;
-        const bool act = task < total;
-        const uint32_t blk = act ? task >> 2 : 0u;
-        uint8_t* rec = xsb + static_cast<size_t>(blk / nblk) * xs_stride + kLimbRec * (blk % nblk);
-        float xv[8];
-        {
-            const float4 a = *reinterpret_cast<const float4*>(rec + 32u * sub);
-            const float4 b = *reinterpret_cast<const float4*>(rec + 32u * sub + 16u);
-            xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+    const uint32_t tasks = nblk * 4u;   // per vector
+    for (uint32_t m = 0; m < M; ++m) {
+        const float4* xm = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K);
+        uint8_t* recs = xsb + static_cast<size_t>(m) * xs_stride;
+        uint32_t base = tid - lane;   // warp-uniform
+        float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
+        if (base + lane < tasks) {
+            na = __ldcg(xm + 2u * (base + lane));
+            nb = __ldcg(xm + 2u * (base + lane) + 1u);
         }
-        __syncwarp();                       // all reads of the raw floats precede the limb writes
-        float amax = 0.0f;
-        uint32_t bad = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            amax = fmaxf(amax, fabsf(xv[i]));
-            bad |= isfinite(xv[i]) ? 0u : 1u;
-        }
-        if (!act) { amax = 0.0f; bad = 0u; }
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-            bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
-        }
-        // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
-        // bits when both are normal floats, else by ldexpf.
-        const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
-        const bool live = amax > 0.0f && !bad;
-        int e = 0;
-        float up = 0.0f, cb = 0.0f;
-        bool slow = false;
-        if (live) {
-            if (ebits >= 29u) {
-                e = static_cast<int>(ebits) - 126;
-                up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
-                cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
-            } else {
-                frexpf(amax, &e);
-                slow = true;
-                cb = ldexpf(1.0f, e - 27);
+        for (; base < tasks; base += nthreads) {
+            const uint32_t task = base + lane;
+            const bool act = task < tasks;
+            const float4 a = na, b = nb;
+            if (task + nthreads < tasks) {   // next round in flight
+                na = __ldcg(xm + 2u * (task + nthreads));
+                nb = __ldcg(xm + 2u * (task + nthreads) + 1u);
             }
-        }
-        uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
-        int S[4] = {0, 0, 0, 0};
+            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint8_t* rec = recs + kLimbRec * (task >> 2);
+            float amax = 0.0f;
+            uint32_t bad = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
-            const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
-            const int sg = X < 0 ? -1 : 1;
-            const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
-                              sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
-            // byte position of element i inside this thread's 8 bytes of each plane
-            const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
-                S[j] += L[j];
+            for (int i = 0; i < 8; ++i) {
+                amax = fmaxf(amax, fabsf(xv[i]));
+                bad |= isfinite(xv[i]) ? 0u : 1u;
             }
-        }
+            if (!act) {
+                amax = 0.0f;
+                bad = 0u;
+            }
 #pragma unroll
-        for (int o = 1; o <= 2; o <<= 1)
+            for (int o = 1; o <= 2; o <<= 1) {
+                amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+                bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+            }
+            // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
+            // bits when both are normal floats, else by ldexpf.
+            const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
+            const bool live = amax > 0.0f && !bad;
+            int e = 0;
+            float up = 0.0f, cb = 0.0f;
+            bool slow = false;
+            if (live) {
+                if (ebits >= 29u) {
+                    e = static_cast<int>(ebits) - 126;
+                    up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
+                    cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
+                } else {
+                    frexpf(amax, &e);
+                    slow = true;
+                    cb = ldexpf(1.0f, e - 27);
+                }
+            }
+            uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+            int S[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
-        if (act) {
+            for (int i = 0; i < 8; ++i) {
+                const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
+                const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
+                const int sg = X < 0 ? -1 : 1;
+                const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
+                                  sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
+                // byte position of element i inside this thread's 8 bytes of each plane
+                const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
-            if (sub == 0) {
-                *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
-                *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
+                for (int j = 0; j < 4; ++j) {
+                    w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
+                    S[j] += L[j];
+                }
+            }
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
+            if (act) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
+                if (sub == 0) {
+                    *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
+                    *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
+                }
             }
         }
     }
@@ -368,8 +388,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     uint8_t* slots = smem;
     uint8_t* xsb = smem + static_cast<size_t>(nst) * p.slot_stride;                     // staged activations
     float* pbuf = reinterpret_cast<float*>(xsb + static_cast<size_t>(p.M) * p.xs_stride);   // EXACT only
-    uint64_t* full = reinterpret_cast<uint64_t*>(
-        pbuf + (EXACT ? static_cast<size_t>(kRowWarps) * p.G * p.pb_row : 0));
+    float* part = pbuf + (EXACT ? static_cast<size_t>(kRowWarps) * p.G * p.pb_row : 0);    // FAST, several pieces
+    const uint32_t part_floats = (!EXACT && p.npieces > 1) ? (p.M * p.part_rows * p.npieces + 1u) & ~1u : 0u;
+    uint64_t* full = reinterpret_cast<uint64_t*>(part + part_floats);
     volatile uint32_t* slot_stage = reinterpret_cast<volatile uint32_t*>(full + nst);
 
     if (blockDim.x != static_cast<uint32_t>(kRowThreads)) {
@@ -379,7 +400,8 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     const uint32_t c = blockIdx.x;
     const uint32_t r0 = c * p.rows_base + min(c, p.rows_extra);
     const uint32_t nrows = p.rows_base + (c < p.rows_extra ? 1u : 0u);
-    const uint32_t nstages = (nrows + p.G - 1) / p.G;
+    const uint32_t nstages = (nrows + p.G - 1) / p.G * p.npieces;
+    constexpr uint32_t kBlockBytes = DT == kDtypeQ8 ? 36u : 18u;
 
     for (uint32_t s = threadIdx.x; s < nst; s += kRowThreads) {
         mbar_init(&full[s], 1);
@@ -392,16 +414,25 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     // Issue one stage's rows into its slot (one lane).  Weights are read-only
     // model data, so the first stages go out before the dependency wait.
     const uint64_t pol = policy_evict_first();
-    auto issue = [&](uint32_t s) {
-        const uint32_t slot = s % nst;
-        const uint32_t bytes = min(p.G, nrows - s * p.G) * static_cast<uint32_t>(p.row_bytes);
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(slots + static_cast<size_t>(slot) * p.slot_stride,
-                 p.w + static_cast<size_t>(r0 + s * p.G) * p.row_bytes, bytes, &full[slot], pol);
+    auto issue = [&](uint32_t s, uint32_t slot) {
+        const uint32_t g = p.npieces == 1 ? s : s / p.npieces, pc = s - g * p.npieces;
+        const uint32_t rows = min(p.G, nrows - g * p.G);
+        const uint8_t* src = p.w + static_cast<size_t>(r0 + g * p.G) * p.row_bytes + static_cast<size_t>(pc) * p.piece_bytes;
+        uint8_t* dst = slots + static_cast<size_t>(slot) * p.slot_stride;
+        if (p.npieces == 1) {   // whole rows: one copy
+            const uint32_t bytes = rows * static_cast<uint32_t>(p.row_bytes);
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            bulk_g2s(dst, src, bytes, &full[slot], pol);
+        } else {                // one copy per row of this piece
+            const uint32_t pb = min(p.piece_blocks, p.nblk - pc * p.piece_blocks) * kBlockBytes;
+            mbar_arrive_expect_tx(&full[slot], rows * pb);
+            for (uint32_t i = 0; i < rows; ++i)
+                bulk_g2s(dst + i * p.piece_bytes, src + static_cast<size_t>(i) * p.row_bytes, pb, &full[slot], pol);
+        }
         slot_stage[slot] = s;   // the slot's barrier is now in stage s's phase
     };
     if (lane == 0)
-        for (uint32_t s = warp; s < min(nst, nstages); s += kRowWarps) issue(s);
+        for (uint32_t s = warp; s < min(nst, nstages); s += kRowWarps) issue(s, s);
 
     // ── stage the activations (after the previous kernel finished) ──
     // L2-coherent loads (__ldcg): under programmatic dependent launch x may have
@@ -410,33 +441,27 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     const uint32_t call = p.world ? *reinterpret_cast<volatile const uint32_t*>(p.seq) + 1u : 0u;
     if constexpr (EXACT) {
         const uint32_t n4 = p.K / 4u;
-        const uint32_t total = p.M * n4;
-        for (uint32_t i = threadIdx.x; i < total; i += kRowWarps * 32u) {
-            const uint32_t m = i / n4, e = (i % n4) * 4u;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K) + (i % n4));
-            *reinterpret_cast<float4*>(xsb + static_cast<size_t>(m) * p.xs_stride + 144u * (e >> 5) + 4u * (e & 31u)) = v;
+        for (uint32_t m = 0; m < p.M; ++m) {
+            const float4* xm = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K);
+            uint8_t* xs = xsb + static_cast<size_t>(m) * p.xs_stride;
+            for (uint32_t i = threadIdx.x; i < n4; i += kRowWarps * 32u)
+                *reinterpret_cast<float4*>(xs + 144u * (i >> 3) + 16u * (i & 7u)) = __ldcg(xm + i);
         }
     } else {
-        // pass 1: every thread's loads in flight at once (raw floats into the records)
-        const uint32_t n4 = p.K / 4u;
-        const uint32_t total = p.M * n4;
-        for (uint32_t i = threadIdx.x; i < total; i += kRowWarps * 32u) {
-            const uint32_t m = i / n4, e = (i % n4) * 4u;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.x + static_cast<size_t>(m) * p.K) + (i % n4));
-            *reinterpret_cast<float4*>(xsb + static_cast<size_t>(m) * p.xs_stride + kLimbRec * (e >> 5) + 4u * (e & 31u)) = v;
-        }
-        __syncthreads();
-        // pass 2: four threads per block turn the floats into limbs
-        stage_limb_records<DT>(xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u);
+        stage_limb_records<DT>(p.x, p.K, xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u);
     }
     __syncthreads();
 
+    // this warp's stages s = warp, warp + 16, ...: ring slot s % nst and phase
+    // parity (s / nst) & 1, advanced by subtraction (no division in the loop)
+    uint32_t slot = warp % nst, phase = (warp / nst) & 1u;
     for (uint32_t s = warp; s < nstages; s += kRowWarps) {
-        const uint32_t slot = s % nst;
         if (!wait_stage_id(slot_stage + slot, s)) break;      // error raised; every warp still reaches the end
-        if (!mbar_wait(&full[slot], (s / nst) & 1u)) break;
-        const uint32_t rows_s = min(p.G, nrows - s * p.G);
-        const uint32_t row0 = r0 + s * p.G;
+        if (!mbar_wait(&full[slot], phase)) break;
+        const uint32_t sg = p.npieces == 1 ? s : s / p.npieces, pc = s - sg * p.npieces;
+        const uint32_t rows_s = min(p.G, nrows - sg * p.G);
+        const uint32_t row0 = r0 + sg * p.G;
+        const uint32_t pblocks = min(p.piece_blocks, p.nblk - pc * p.piece_blocks), pbase = pc * p.piece_blocks;
         const uint8_t* sb = slots + static_cast<size_t>(slot) * p.slot_stride;
 
         if constexpr (!EXACT) {
@@ -444,19 +469,18 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
             const uint8_t* rowp[GT];
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
-                rowp[g] = sb + static_cast<size_t>(min(static_cast<uint32_t>(g), rows_s - 1u)) * p.row_bytes;
+                rowp[g] = sb + static_cast<size_t>(min(static_cast<uint32_t>(g), rows_s - 1u)) * p.piece_bytes;
 #pragma unroll
                 for (int v = 0; v < MT; ++v) racc[g][v] = 0.0f;
             }
-            for (uint32_t ch = 0; ch < p.nchunk; ++ch) {
-                const uint32_t b = ch * 32u + lane;
-                if (b < p.nblk) {
+            for (uint32_t b = lane; b < pblocks; b += 32u) {   // b: block within the piece
+                {
                     LimbBlock lb[MT];
                     float cb[MT];
                     int4 S[MT];
 #pragma unroll
                     for (int v = 0; v < MT; ++v) {
-                        const uint8_t* rec = xsb + static_cast<size_t>(v) * p.xs_stride + kLimbRec * b;
+                        const uint8_t* rec = xsb + static_cast<size_t>(v) * p.xs_stride + kLimbRec * (pbase + b);
                         lds_limbs(rec, lb[v]);
                         cb[v] = *reinterpret_cast<const float*>(rec + 128);
                         if constexpr (DT == kDtypeQ4) S[v] = *reinterpret_cast<const int4*>(rec + 144);
@@ -487,20 +511,25 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                 }
             }
             __syncwarp();
-            if (lane == 0 && s + nst < nstages) issue(s + nst);   // the slot's bytes are no longer read
+            if (lane == 0 && s + nst < nstages) issue(s + nst, slot);   // the slot's bytes are no longer read
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
 #pragma unroll
                 for (int v = 0; v < MT; ++v) {
                     const float t = warp_sum(racc[g][v]);
-                    if (lane == 0 && g < static_cast<int>(rows_s)) store_out(p, call, v, row0 + g, t);
+                    if (lane == 0 && g < static_cast<int>(rows_s)) {
+                        if (p.npieces == 1)
+                            store_out(p, call, v, row0 + g, t);
+                        else
+                            part[(static_cast<size_t>(v) * p.part_rows + (row0 - r0 + g)) * p.npieces + pc] = t;
+                    }
                 }
             }
         } else {
             float* pb = pbuf + static_cast<size_t>(warp) * p.G * p.pb_row;
             for (uint32_t m = 0; m < p.M; ++m) {
                 const float* xm = reinterpret_cast<const float*>(xsb + static_cast<size_t>(m) * p.xs_stride);
-                for (uint32_t ch = 0; ch < p.nchunk; ++ch) {
+                    for (uint32_t ch = 0; ch < (p.nblk + 31u) / 32u; ++ch) {
                     const uint32_t b = ch * 32u + lane;
                     if (b < p.nblk) {
                         float4 xv[8];
@@ -537,7 +566,25 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                 }
                 __syncwarp();
             }
-            if (lane == 0 && s + nst < nstages) issue(s + nst);
+            if (lane == 0 && s + nst < nstages) issue(s + nst, slot);
+        }
+        slot += kRowWarps;
+        while (slot >= nst) {
+            slot -= nst;
+            phase ^= 1u;
+        }
+    }
+    if constexpr (!EXACT) {
+        if (p.npieces > 1) {   // rows summed piece by piece, in order
+            __syncthreads();
+            const uint32_t total = p.M * nrows;
+            for (uint32_t i = threadIdx.x; i < total; i += kRowThreads) {
+                const uint32_t v = i / nrows, rl = i - v * nrows;
+                const float* pr = part + (static_cast<size_t>(v) * p.part_rows + rl) * p.npieces;
+                float t = 0.0f;
+                for (uint32_t q = 0; q < p.npieces; ++q) t += pr[q];
+                store_out(p, call, v, r0 + rl, t);
+            }
         }
     }
     if (p.world) sharded_gather(p, call);
