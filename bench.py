@@ -65,9 +65,10 @@ def measured_peaks():
     return 6650.0, "fallback (6.65 TB/s, profiling recipe)"
 
 
-def profiled_traffic(dt, n, k):
+def profiled_traffic(kernel, dt, n, k, m=1):
     """DRAM bytes per launch from the committed ncu summary of the same kernel and shape, if present."""
-    name = f"matvec_rows_{'q4' if dt == Q4 else 'q8'}_{n}x{k}.md"
+    stem = "matmul_tc" if kernel == "qmm_tc_kernel" else "matvec_rows"
+    name = f"{stem}_{'q4' if dt == Q4 else 'q8'}_{n}x{k}{f'_m{m}' if m > 1 else ''}.md"
     path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
         return None
@@ -232,7 +233,9 @@ def run_ours(args, dt, n, k, m):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     qb.init(local)
-    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC}[args.mode]
+    kernel = "qmm_tc_kernel" if args.mode == "tc" else ("qmv_rows_kernel" if m <= 2 or args.mode == "exact"
+                                                         else "qmv_stream_kernel")
 
     # Seeded weight, quantized on the GPU (byte-exact with the reference quantizer).
     wf = torch.from_numpy(qb.fill_normal(42, 0.0, 0.02, n * k)).to(dev).reshape(n, k)
@@ -366,8 +369,8 @@ def run_ours(args, dt, n, k, m):
             "e2e": e2e,
             "gpu_launches": args.steps * R,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profiled_traffic(dt, n, k), "peak_source": peak_src,
-                         "kernel": "qmv_rows_kernel" if m <= 2 else "qmv_stream_kernel",
+                         "frac": achieved / peak, "traffic": profiled_traffic(kernel, dt, n, k, m),
+                         "peak_source": peak_src, "kernel": kernel,
                          "kernel_us": kern_ms * 1e3,
                          "kernel_timing": "average launch duration of back-to-back launches without overlap "
                                           "(CUDA events around a graph of launches, inter-launch gaps included)",
@@ -723,7 +726,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="q4_4096x4096")
-    ap.add_argument("--mode", choices=["fast", "exact"], default="fast")
+    ap.add_argument("--mode", choices=["fast", "exact", "tc"], default="fast")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
