@@ -279,6 +279,7 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.rows_base = rows_base;
     p.rows_extra = rows_extra;
     p.pdl = 0;
+    p.xrec = nullptr;
     p.world = 0;
     p.rank = 0;
     p.seq = nullptr;
@@ -323,6 +324,42 @@ cudaError_t launch_rows(uint32_t dtype, const RowPlan& pl, bool exact, int MT, b
     p.pdl = pdl ? 1u : 0u;
     return dtype == QRAF_DTYPE_Q8_0 ? launch_rows_dt<kDtypeQ8>(pl, p, exact, MT, pdl, st)
                                     : launch_rows_dt<kDtypeQ4>(pl, p, exact, MT, pdl, st);
+}
+
+int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out);
+
+// FAST row kernel, with the activation limbs built once by limb_prep_kernel (into
+// the stream's scratch) when every CTA would otherwise spend a large share of its
+// time building them (long K, few rows per CTA: long-K projections, row shards on
+// many GPUs); the row kernel then copies the records and waits for the prep kernel
+// through programmatic dependent launch (its weight copies start meanwhile).
+constexpr uint32_t kPrepMinBlocks = 256;   // K >= 8192
+constexpr uint32_t kPrepMaxRows = 96;      // rows per CTA
+
+int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStream_t st) {
+    if (pl.p.nblk >= kPrepMinBlocks && pl.p.rows_base + (pl.p.rows_extra ? 1u : 0u) <= kPrepMaxRows) {
+        const size_t bytes = static_cast<size_t>(pl.p.M) * pl.p.nblk * kLimbRec;
+        uint8_t* recs = nullptr;
+        const int rc = tc_scratch(st, bytes, &recs);
+        if (rc) return rc;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = overlap ? 1 : 0;
+        cfg.gridDim = dim3((pl.p.M * pl.p.nblk * 4u + 255u) / 256u);
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, dtype == QRAF_DTYPE_Q8_0 ? limb_prep_kernel<kDtypeQ8> : limb_prep_kernel<kDtypeQ4>,
+                                                 pl.p.x, pl.p.K, pl.p.M, pl.p.nblk, recs, overlap ? 1u : 0u);
+        if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "limb prep launch: %s", cudaGetErrorString(e));
+        pl.p.xrec = recs;
+        overlap = true;   // the row kernel waits for the prep kernel, not for the one before it
+    }
+    const cudaError_t e = launch_rows(dtype, pl, false, MT, overlap, st);
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "row kernel launch: %s", cudaGetErrorString(e));
+    return QRAF_OK;
 }
 
 template <uint32_t DT>
@@ -608,6 +645,11 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
                 one.p.y = y + static_cast<size_t>(m0) * w->rows;
                 one.p.M = cnt;
                 const int MT = exact ? 1 : static_cast<int>(cnt);
+                if (!exact) {
+                    const int rc2 = launch_rows_fast(w->dtype, one, MT, overlap, st);
+                    if (rc2) return rc2;
+                    continue;
+                }
                 const cudaError_t e = launch_rows(w->dtype, one, exact, MT, overlap, st);
                 if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "row kernel launch: %s", cudaGetErrorString(e));
             }
@@ -1108,9 +1150,13 @@ int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32
     p.ll_cap = c->cap;
     p.cta_counter = c->counter;
     for (int r = 0; r < c->world; ++r) p.peer_ll[r] = c->peer_ll[r];
-    const cudaError_t e = launch_rows(shard->dtype, pl, exact, exact ? 1 : static_cast<int>(M), overlap,
-                                      static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));
+    if (exact) {
+        const cudaError_t e = launch_rows(shard->dtype, pl, true, 1, overlap, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));
+    } else {
+        rc = launch_rows_fast(shard->dtype, pl, static_cast<int>(M), overlap, static_cast<cudaStream_t>(stream));
+        if (rc) return rc;
+    }
     *y_out = c->y[buf];
     return QRAF_OK;
 }

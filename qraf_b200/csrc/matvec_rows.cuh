@@ -74,6 +74,7 @@ struct RowParams {
     uint32_t pb_row;         // EXACT: floats per row of the per-warp partial buffer
     uint32_t rows_base, rows_extra;
     uint32_t pdl;            // 1: programmatic dependent launch protocol
+    const uint8_t* xrec;     // FAST: limb records built by limb_prep_kernel ([M][nblk] x kLimbRec), or null
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
     // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
     // output element goes into this rank's y and, as one 8-byte word (call number
@@ -244,12 +245,81 @@ __device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const Li
     return combine_limbs(d0, d1, d2, d3);
 }
 
+// One thread's share of a limb record: elements 8*sub .. 8*sub+7 of a block
+// (for Q4 exactly one group of 8 in the 0,2,4,6,1,3,5,7 order).  The four
+// threads of a block are lanes 4k..4k+3 of one warp, all active (`act` false
+// for padding threads): the group's maximum and plane sums take two shuffles.
+template <uint32_t DT>
+__device__ __forceinline__ void limb_record_part(const float4 a, const float4 b, bool act, uint8_t* rec, uint32_t sub) {
+    const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float amax = 0.0f;
+    uint32_t bad = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        amax = fmaxf(amax, fabsf(xv[i]));
+        bad |= isfinite(xv[i]) ? 0u : 1u;
+    }
+    if (!act) {
+        amax = 0.0f;
+        bad = 0u;
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
+    }
+    // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
+    // bits when both are normal floats, else by ldexpf.
+    const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
+    const bool live = amax > 0.0f && !bad;
+    int e = 0;
+    float up = 0.0f, cb = 0.0f;
+    bool slow = false;
+    if (live) {
+        if (ebits >= 29u) {
+            e = static_cast<int>(ebits) - 126;
+            up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
+            cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
+        } else {
+            frexpf(amax, &e);
+            slow = true;
+            cb = ldexpf(1.0f, e - 27);
+        }
+    }
+    uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+    int S[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
+        const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
+        const int sg = X < 0 ? -1 : 1;
+        const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
+                          sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
+        // byte position of element i inside this thread's 8 bytes of each plane
+        const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
+            S[j] += L[j];
+        }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
+    if (act) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
+        if (sub == 0) {
+            *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
+            *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
+        }
+    }
+}
+
 // Turn the fp32 activations (global memory, read through L2) into limb records
-// in one pass.  Four threads per block, eight elements each (elements
-// 8*sub .. 8*sub+7, which for Q4 is exactly one group of 8 in the
-// 0,2,4,6,1,3,5,7 order); the group's maximum and plane sums need two shuffles
-// each.  Every thread has the next round's loads in flight while it converts
-// the current one.
+// in shared memory, in one pass, four threads per block; every thread has the
+// next round's loads in flight while it converts the current one.
 template <uint32_t DT>
 __device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, uint32_t K, uint8_t* xsb,
                                                    uint32_t xs_stride, uint32_t M, uint32_t nblk, uint32_t tid,
@@ -267,80 +337,35 @@ __device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, 
         }
         for (; base < tasks; base += nthreads) {
             const uint32_t task = base + lane;
-            const bool act = task < tasks;
             const float4 a = na, b = nb;
             if (task + nthreads < tasks) {   // next round in flight
                 na = __ldcg(xm + 2u * (task + nthreads));
                 nb = __ldcg(xm + 2u * (task + nthreads) + 1u);
             }
-            const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            uint8_t* rec = recs + kLimbRec * (task >> 2);
-            float amax = 0.0f;
-            uint32_t bad = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                amax = fmaxf(amax, fabsf(xv[i]));
-                bad |= isfinite(xv[i]) ? 0u : 1u;
-            }
-            if (!act) {
-                amax = 0.0f;
-                bad = 0u;
-            }
-#pragma unroll
-            for (int o = 1; o <= 2; o <<= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-                bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
-            }
-            // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
-            // bits when both are normal floats, else by ldexpf.
-            const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
-            const bool live = amax > 0.0f && !bad;
-            int e = 0;
-            float up = 0.0f, cb = 0.0f;
-            bool slow = false;
-            if (live) {
-                if (ebits >= 29u) {
-                    e = static_cast<int>(ebits) - 126;
-                    up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
-                    cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
-                } else {
-                    frexpf(amax, &e);
-                    slow = true;
-                    cb = ldexpf(1.0f, e - 27);
-                }
-            }
-            uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
-            int S[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
-                const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
-                const int sg = X < 0 ? -1 : 1;
-                const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
-                                  sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
-                // byte position of element i inside this thread's 8 bytes of each plane
-                const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
-                    S[j] += L[j];
-                }
-            }
-#pragma unroll
-            for (int o = 1; o <= 2; o <<= 1)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
-            if (act) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
-                if (sub == 0) {
-                    *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
-                    *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
-                }
-            }
+            limb_record_part<DT>(a, b, task < tasks, recs + kLimbRec * (task >> 2), sub);
         }
     }
+}
+
+// The same records built once per call for every CTA of the matvec that follows
+// (global memory, [M][nblk] records of kLimbRec bytes): one thread per 8
+// elements over the whole grid.
+template <uint32_t DT>
+__global__ void __launch_bounds__(256) limb_prep_kernel(const float* __restrict__ x, uint32_t K, uint32_t M,
+                                                        uint32_t nblk, uint8_t* __restrict__ recs, uint32_t pdl) {
+    if (pdl) pdl_wait();
+    if (pdl) pdl_launch_dependents();
+    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t per = nblk * 4u, total = M * per;
+    const bool act = tid < total;
+    const uint32_t m = act ? tid / per : 0u, task = act ? tid - m * per : 0u;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (act) {
+        const float4* xm = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K);
+        a = __ldcg(xm + 2u * task);
+        b = __ldcg(xm + 2u * task + 1u);
+    }
+    limb_record_part<DT>(a, b, act, recs + (static_cast<size_t>(m) * nblk + (task >> 2)) * kLimbRec, task & 3u);
 }
 
 // ── EXACT block dots: the reference's order, scalar, never fused ─────────
@@ -391,7 +416,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     float* part = pbuf + (EXACT ? static_cast<size_t>(kRowWarps) * p.G * p.pb_row : 0);    // FAST, several pieces
     const uint32_t part_floats = (!EXACT && p.npieces > 1) ? (p.M * p.part_rows * p.npieces + 1u) & ~1u : 0u;
     uint64_t* full = reinterpret_cast<uint64_t*>(part + part_floats);
-    volatile uint32_t* slot_stage = reinterpret_cast<volatile uint32_t*>(full + nst);
+    volatile uint32_t* slot_stage = reinterpret_cast<volatile uint32_t*>(full + nst + 1);
 
     if (blockDim.x != static_cast<uint32_t>(kRowThreads)) {
         if (threadIdx.x == 0) raise_error(kErrBadLaunch);
@@ -403,9 +428,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     const uint32_t nstages = (nrows + p.G - 1) / p.G * p.npieces;
     constexpr uint32_t kBlockBytes = DT == kDtypeQ8 ? 36u : 18u;
 
-    for (uint32_t s = threadIdx.x; s < nst; s += kRowThreads) {
+    for (uint32_t s = threadIdx.x; s <= nst; s += kRowThreads) {   // full[nst]: the activation records
         mbar_init(&full[s], 1);
-        slot_stage[s] = 0xFFFFFFFFu;
+        if (s < nst) slot_stage[s] = 0xFFFFFFFFu;
     }
     fence_mbar_init();
     __syncthreads();
@@ -447,6 +472,15 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
             for (uint32_t i = threadIdx.x; i < n4; i += kRowWarps * 32u)
                 *reinterpret_cast<float4*>(xs + 144u * (i >> 3) + 16u * (i & 7u)) = __ldcg(xm + i);
         }
+    } else if (p.xrec) {
+        // records already built: one bulk copy (L2 -> shared memory), completion on full[nst]
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = p.M * p.nblk * kLimbRec;
+            mbar_arrive_expect_tx(&full[nst], bytes);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+                bulk_g2s(xsb + off, p.xrec + off, min(32768u, bytes - off), &full[nst], policy_evict_first());
+        }
+        mbar_wait(&full[nst], 0u);
     } else {
         stage_limb_records<DT>(p.x, p.K, xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u);
     }
