@@ -417,7 +417,7 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     p.M = M;
     p.nblk = w.cols / 32u;
     p.n_pad = 2u * out->mv;
-    p.act_stride = p.n_pad * 64u + out->mv * 4u;
+    p.act_stride = p.n_pad * 128u + 2u * out->mv * 4u;   // per pair of blocks
     p.unit_blocks = q4 ? 8u : 4u;
     if (p.nblk % p.unit_blocks) return false;
     p.upt = p.nblk / p.unit_blocks;
@@ -425,20 +425,23 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     const uint64_t units = static_cast<uint64_t>(p.tiles) * p.upt;
     if (units > 0xFFFFFFFFull / static_cast<uint64_t>(dev.sm_count)) return false;
     p.units = static_cast<uint32_t>(units);
-    p.nab = 8;
-    p.nd = std::min(8u, kTcTmemCols / p.n_pad);   // even: the epilogue may take blocks in pairs
+    // Rings in stages of two blocks: accumulators (2 x n_pad TMEM columns each),
+    // weight codes (16 KB each), activation tiles (n_pad x 128 bytes, from L2, so
+    // deep), scales and factors; then as many raw units (18 KB) as fit, up to 8.
+    p.nd = std::min(8u, kTcTmemCols / (2u * p.n_pad));
+    p.nab = 4;
     p.ns = 16;
+    p.nf = 16;
     p.pdl = 1;
     out->grid = static_cast<int>(std::min<uint64_t>(dev.sm_count, units));
-    // Shared memory: an A ring of 8 blocks (the MMA round trip is long), the
-    // scale ring, an activation ring of 8 blocks (fewer for wide batches) and
-    // as many raw units (18 KB each, up to 8) as fit.
     const size_t avail = static_cast<size_t>(dev.smem_optin) - kSmemReserve;
+    const uint32_t tile_bytes = p.n_pad * 128u;
     auto layout = [&](uint32_t nraw, uint32_t nbb) {
-        return static_cast<size_t>(nraw) * kTcRawSlot + p.nab * kTcASlot + static_cast<size_t>(nbb) * p.act_stride +
-               p.ns * kTcRows * 4u + 8u * (2u * nraw + 2u * p.nab + 2u * nbb + 2u * p.nd + 2u * p.ns + 2u) + 16u;
+        return 1024u + static_cast<size_t>(nraw) * kTcRawSlot + p.nab * kTcASlot + static_cast<size_t>(nbb) * tile_bytes +
+               p.ns * 2u * kTcRows * 4u + p.nf * 2u * out->mv * 4u +
+               8u * (2u * nraw + p.nab + nbb + 32u + p.nd + 2u * p.ns + 2u * p.nf + 2u) + 16u;
     };
-    p.nbb = 8;
+    p.nbb = 16;
     p.nraw = 8;
     while (p.nraw > 4 && layout(p.nraw, p.nbb) > avail) --p.nraw;
     while (p.nbb > 4 && layout(p.nraw, p.nbb) > avail) --p.nbb;
@@ -449,7 +452,7 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     // the SM would only wait for them.
     out->smem = std::max<size_t>(out->smem, 120u * 1024u);
     if (out->smem + kSmemReserve > static_cast<size_t>(dev.smem_optin)) return false;
-    out->off_part = round256(static_cast<size_t>(p.nblk) * p.act_stride);
+    out->off_part = round256(static_cast<size_t>(p.nblk / 2u) * p.act_stride);
     out->off_cnt = out->off_part + round256(static_cast<size_t>(out->grid) * 2u * M * kTcRows * sizeof(float));
     out->bytes = out->off_cnt + round256(static_cast<size_t>(p.tiles) * sizeof(uint32_t));
     return true;

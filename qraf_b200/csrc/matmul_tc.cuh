@@ -14,7 +14,11 @@
 //     y[n][m] += fl(4096 D_hi + D_lo) * fl(scale[n][b] * 2^(e[m][b]-23))
 // in fp32 on the CUDA cores, block by block.
 //
-// Work split.  A unit is 128 weight rows (the MMA's M) by 144 bytes of each
+// Work split.  A stage is two blocks (64 elements of K) of 128 weight rows:
+// four K=16 MMAs with 128-byte-swizzled operands (two per block, each block
+// into its own accumulator) and one commit, which every consumer of the stage
+// (weight ring, activation ring, epilogue) waits on.
+// A unit is 128 weight rows (the MMA's M) by 144 bytes of each
 // row (8 Q4 blocks or 4 Q8 blocks; 144 keeps every copy 16-byte aligned),
 // fetched by one 2-D TMA copy (the weight seen as [N][row_bytes / 4] words).
 // The grid is persistent (one CTA per SM) and CTA c takes the contiguous
@@ -42,7 +46,7 @@ namespace qraf_dev {
 constexpr uint32_t kTcRows = 128;           // weight rows per tile = MMA M = TMEM lanes
 constexpr uint32_t kTcUnitBytes = 144;      // raw bytes per row per unit
 constexpr uint32_t kTcRawSlot = kTcRows * kTcUnitBytes;
-constexpr uint32_t kTcASlot = kTcRows * 64; // one block of fp16 codes: two K=16 tiles of 4 KB
+constexpr uint32_t kTcASlot = kTcRows * 128; // one stage of fp16 codes: 128 rows x 64 elements, 128-byte swizzle
 constexpr uint32_t kTcThreads = 480;
 constexpr uint32_t kTcWarpXf = 8, kTcWarpRaw = 12, kTcWarpMma = 13, kTcWarpAct = 14;
 constexpr uint32_t kTcTmemCols = 512;
@@ -50,40 +54,43 @@ constexpr uint32_t kTcMaxVectors = 64;      // activation vectors per launch (MM
 
 struct TcParams {
     const uint8_t* w;        // [N][row_bytes], native blocks
-    const uint8_t* act;      // prepared activation tiles: [nblk][act_stride] bytes, each the fp16 limb
-                             // tile (n_pad * 64 bytes) followed by the MV block factors 2^(e - 23)
+    const uint8_t* act;      // prepared activation tiles: [nblk / 2][act_stride] bytes, each the fp16 limb
+                             // tile of two blocks (n_pad * 128 bytes, 128-byte swizzle) followed by the
+                             // 2 x MV block factors 2^(e - 23)
     float* y;                // [M][N]
     float* partial;          // [gridDim][2][M][128]
     uint32_t* tile_count;    // [tiles], zeroed by the prep kernel of the same call
     uint64_t row_bytes;
     uint32_t N, M, nblk;
     uint32_t n_pad;          // MMA N: 2 x (vectors rounded up to 16, 32 or 64)
-    uint32_t act_stride;     // n_pad * 64 + MV * 4
+    uint32_t act_stride;     // n_pad * 128 + 2 * MV * 4
     uint32_t unit_blocks;    // 8 (Q4) or 4 (Q8)
     uint32_t upt;            // units per tile = nblk / unit_blocks
     uint32_t tiles, units;
-    uint32_t nraw, nab, nbb, nd, ns;   // ring depths: raw units; weight, activation, accumulator, scale blocks
+    uint32_t nraw, nab, nbb, nd, ns, nf;   // ring depths: raw units; weight, activation, accumulator, scale,
+                                           // factor stages (two blocks each)
     uint32_t pdl;
 };
 
-// ── shared-memory matrix layout (tcgen05 "canonical" K-major, no swizzle) ──
-// A K=16 tile of R rows is R/8 groups of 256 bytes; each group holds two 8x8
-// core matrices of fp16 (K 0-7 then K 8-15, 128 bytes apart), each core
-// matrix 8 rows of 16 bytes.  Leading-dimension offset 128, stride 256.
-__device__ __forceinline__ uint32_t tc_chunk_off(uint32_t row, uint32_t c) {
-    return (row >> 3) * 256u + c * 128u + (row & 7u) * 16u;
+// ── shared-memory matrix layout: K-major, 128-byte swizzle ─────────────────
+// A tile of R rows x 64 fp16 (128 bytes per row) is R/8 atoms of 1024 bytes;
+// in an atom, row r's 16-byte chunk c sits at chunk position c ^ r.  The MMA
+// descriptor's stride is 1024 (one atom); a K=16 step moves its start 32 bytes
+// on.  Atoms must start on 1024-byte boundaries.
+__device__ __forceinline__ uint32_t tc_sw128_off(uint32_t row, uint32_t chunk) {
+    return (row >> 3) * 1024u + (row & 7u) * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-__device__ __forceinline__ uint64_t tc_smem_desc(const void* p) {
-    const uint32_t a = smem_u32(p);
-    uint64_t d = static_cast<uint64_t>((a >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(128u >> 4) << 16;   // leading-dimension byte offset
-    d |= static_cast<uint64_t>(256u >> 4) << 32;   // stride byte offset
+__device__ __forceinline__ uint64_t tc_smem_desc(uint32_t saddr) {
+    uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;          // leading-dimension offset (unused with K-major swizzle)
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;  // stride byte offset: one 8-row atom
     d |= static_cast<uint64_t>(1u) << 46;          // descriptor version (sm_100)
-    return d;                                      // base offset 0, no swizzle
+    d |= static_cast<uint64_t>(2u) << 61;          // 128-byte swizzle
+    return d;
 }
 
-// Position of element i (0..31) of a block inside its two K=16 tiles.  Q4
+// Position of element i (0..31) of a block inside its 32 elements of K.  Q4
 // codes are laid out in the order their nibbles unpack (per 8 elements:
 // 0,2,4,6,1,3,5,7); the activation tiles use the same order.
 template <uint32_t DT>
@@ -132,8 +139,9 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 // ── activation preparation: x (fp32) -> fp16 limb tiles + block factors ────
 // One warp per (block b, vector slot m); lane i takes element i.  Tile rows
-// 2m / 2m+1 hold hi / lo of vector m; rows of vectors >= M are zero; the
-// block's factors follow the tile (one float per vector slot).  Also
+// 2m / 2m+1 hold hi / lo of vector m; rows of vectors >= M are zero; each
+// block pair's tile is followed by its factors (one float per block and vector
+// slot).  Also
 // zeroes the stream-K tile counters of the call.  A block holding a NaN or an
 // infinity gets a NaN factor, so its outputs come out NaN.
 template <uint32_t DT>
@@ -160,21 +168,22 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ 
     int X = finite ? __float2int_rn(ldexpf(v, 23 - e)) : 0;
     const int hi = (X + 2048) >> 12;
     const int lo = X - hi * 4096;
-    const uint32_t pos = tc_k_slot<DT>(lane);
-    const uint32_t t = pos >> 4, c = (pos >> 3) & 1u, s = pos & 7u;
-    uint8_t* blk = act + static_cast<size_t>(b) * (n_pad * 64u + half * 4u);
-    uint8_t* tile = blk + t * (n_pad * 32u);
-    *reinterpret_cast<__half*>(tile + tc_chunk_off(2u * m, c) + 2u * s) = __int2half_rn(hi);
-    *reinterpret_cast<__half*>(tile + tc_chunk_off(2u * m + 1u, c) + 2u * s) = __int2half_rn(lo);
+    const uint32_t kk = 32u * (b & 1u) + tc_k_slot<DT>(lane);   // element of the block pair's 64
+    uint8_t* tile = act + static_cast<size_t>(b >> 1) * (n_pad * 128u + 2u * half * 4u);
+    *reinterpret_cast<__half*>(tile + tc_sw128_off(2u * m, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(hi);
+    *reinterpret_cast<__half*>(tile + tc_sw128_off(2u * m + 1u, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(lo);
     if (lane == 0)
-        reinterpret_cast<float*>(blk + n_pad * 64u)[m] = m >= M ? 0.0f : finite ? ldexpf(1.0f, e - 23) : __int_as_float(0x7FC00000);
+        reinterpret_cast<float*>(tile + n_pad * 128u)[(b & 1u) * half + m] =
+            m >= M ? 0.0f : finite ? ldexpf(1.0f, e - 23) : __int_as_float(0x7FC00000);
 }
 
 // ── raw block bytes -> fp16 codes in the A layout ───────────────────────────
 // q: the row's 144 raw bytes of the current unit (36 words).  Writes block j's
-// 32 codes (four 16-byte chunks) for row `row` and returns its scale.
+// 32 codes (four 16-byte chunks) for row `row` into half `half` (elements
+// 32 half .. 32 half + 31) of a stage's A slot and returns the block's scale.
 template <uint32_t DT>
-__device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uint32_t j, uint8_t* a_slot, uint32_t row) {
+__device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uint32_t j, uint8_t* a_slot, uint32_t row,
+                                                    uint32_t half) {
     if constexpr (DT == kDtypeQ8) {
         // block j: word 9j = fp32 scale, words 9j+1..9j+8 = codes.  Code byte c
         // (sign bit flipped) under 0x64 is the fp16 1024 + c + 128, exactly.
@@ -194,8 +203,7 @@ __device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uin
                 hv = __hsub2(hv, off);
                 h[k] = *reinterpret_cast<uint32_t*>(&hv);
             }
-            const uint32_t tt = ch >> 1, cc = ch & 1;
-            *reinterpret_cast<uint4*>(a_slot + tt * 4096u + tc_chunk_off(row, cc)) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(a_slot + tc_sw128_off(row, 4u * half + ch)) = make_uint4(h[0], h[1], h[2], h[3]);
         }
         return sc;
     } else {
@@ -228,8 +236,7 @@ __device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uin
                 hv = __hsub2(hv, off);
                 h[k] = *reinterpret_cast<uint32_t*>(&hv);
             }
-            const uint32_t tt = ch >> 1, cc = ch & 1;
-            *reinterpret_cast<uint4*>(a_slot + tt * 4096u + tc_chunk_off(row, cc)) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(a_slot + tc_sw128_off(row, 4u * half + ch)) = make_uint4(h[0], h[1], h[2], h[3]);
         }
         return half_bits_to_float(s16);
     }
@@ -271,59 +278,62 @@ __device__ __forceinline__ uint32_t tc_start(uint32_t c, uint32_t units, uint32_
 
 // ── the tensor-core kernel ─────────────────────────────────────────────────
 // MV: activation vectors handled per launch (16, 32 or 64); n_pad = 2 MV.
+// Stage st covers blocks 2st, 2st+1 of the CTA's sequence of units.
 template <uint32_t DT, uint32_t MV>
 __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
     constexpr uint32_t UB = DT == kDtypeQ4 ? 8u : 4u;   // blocks per raw unit
+    constexpr uint32_t SPU = UB / 2u;                    // stages per raw unit
     constexpr uint32_t HV = MV / 2;                      // vectors per epilogue group
-    constexpr bool PAIR = MV <= 32;                      // epilogue takes two blocks per pass
-    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t R = 32;                           // ring of per-stage "MMA done" barriers
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand tiles (the host adds the slack)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t tile_bytes = p.n_pad * 128u;
     uint8_t* raw = smem;
     uint8_t* abuf = raw + p.nraw * kTcRawSlot;
     uint8_t* bbuf = abuf + p.nab * kTcASlot;
-    float* sring = reinterpret_cast<float*>(bbuf + p.nbb * p.act_stride);
-    uint64_t* raw_full = reinterpret_cast<uint64_t*>(sring + p.ns * kTcRows);
+    float* sring = reinterpret_cast<float*>(bbuf + p.nbb * tile_bytes);   // [ns][2][128] block scales
+    float* fring = sring + p.ns * 2u * kTcRows;                           // [nf][2][MV] block factors
+    uint64_t* raw_full = reinterpret_cast<uint64_t*>(fring + p.nf * 2u * MV);
     uint64_t* raw_empty = raw_full + p.nraw;
     uint64_t* a_full = raw_empty + p.nraw;
-    uint64_t* a_empty = a_full + p.nab;
-    uint64_t* b_full = a_empty + p.nab;
-    uint64_t* b_empty = b_full + p.nbb;
-    uint64_t* d_full = b_empty + p.nbb;
-    uint64_t* d_empty = d_full + p.nd;
+    uint64_t* b_full = a_full + p.nab;
+    uint64_t* mma_done = b_full + p.nbb;        // [R], one phase per stage
+    uint64_t* d_empty = mma_done + R;
     uint64_t* s_full = d_empty + p.nd;
     uint64_t* s_empty = s_full + p.ns;
-    uint64_t* comb = s_empty + p.ns;            // [2]: partial results stored / decision made
+    uint64_t* f_full = s_empty + p.ns;
+    uint64_t* f_empty = f_full + p.nf;
+    uint64_t* comb = f_empty + p.nf;            // [2]: partial results stored / decision made
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(comb + 2);
     uint32_t* bcast = tmem_slot + 1;
 
-    if (blockDim.x != kTcThreads || p.n_pad != 2u * MV || p.M > MV || p.unit_blocks != UB || (PAIR && (p.nd & 1u))) {
+    if (blockDim.x != kTcThreads || p.n_pad != 2u * MV || p.M > MV || p.unit_blocks != UB || p.nab >= R ||
+        p.nbb >= R || p.nd > R || 2u * p.nd * p.n_pad > kTcTmemCols) {
         if (threadIdx.x == 0) raise_error(kErrBadLaunch);
         return;
     }
     const uint32_t C = gridDim.x, cta = blockIdx.x;
     const uint32_t u0 = tc_start(cta, p.units, C), u1 = tc_start(cta + 1, p.units, C);
-    const uint32_t nunits = u1 - u0, nstages = nunits * UB;
+    const uint32_t nunits = u1 - u0, nstages = nunits * SPU;
 
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < p.nraw; ++i) {
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], 4);    // transform warps
         }
-        for (uint32_t i = 0; i < p.nab; ++i) {
-            mbar_init(&a_full[i], 4);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (uint32_t i = 0; i < p.nbb; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 8);      // the epilogue reads the factors after the MMA
-        }
-        for (uint32_t i = 0; i < p.nd; ++i) {
-            mbar_init(&d_full[i], 1);
-            mbar_init(&d_empty[i], 8);
-        }
+        for (uint32_t i = 0; i < p.nab; ++i) mbar_init(&a_full[i], 4);
+        for (uint32_t i = 0; i < p.nbb; ++i) mbar_init(&b_full[i], 1);
+        for (uint32_t i = 0; i < R; ++i) mbar_init(&mma_done[i], 1);
+        for (uint32_t i = 0; i < p.nd; ++i) mbar_init(&d_empty[i], 8);
         for (uint32_t i = 0; i < p.ns; ++i) {
             mbar_init(&s_full[i], 4);
             mbar_init(&s_empty[i], 8);
+        }
+        for (uint32_t i = 0; i < p.nf; ++i) {
+            mbar_init(&f_full[i], 1);
+            mbar_init(&f_empty[i], 8);
         }
         mbar_init(&comb[0], 8);
         mbar_init(&comb[1], 1);
@@ -366,58 +376,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                 mbar_wait(&raw_full[i % p.nraw], (i / p.nraw) & 1u);
         }
     } else if (warp == kTcWarpAct) {
-        // ── prepared activation tiles (written by the prep kernel just before)
+        // ── prepared activation tiles and factors (written by the prep kernel just before)
         if (lane == 0) {
             if (p.pdl) pdl_wait();
-            Ring r(p.nbb);
+            Ring rb(p.nbb), rf(p.nf), rm(R);   // rm: the stage whose MMA frees this stage's tile slot
             uint32_t issued = 0;
-            const uint8_t* src = p.act + static_cast<size_t>(k0) * UB * p.act_stride;
-            const uint8_t* row_end = p.act + static_cast<size_t>(p.upt) * UB * p.act_stride;
-            for (uint32_t st = 0; st < nstages; ++st) {
-                if (r.wrapped && !mbar_wait(&b_empty[r.slot], r.phase ^ 1u)) break;
-                mbar_arrive_expect_tx(&b_full[r.slot], p.act_stride);
+            const uint8_t* src = p.act + static_cast<size_t>(k0) * SPU * p.act_stride;
+            const uint8_t* row_end = p.act + static_cast<size_t>(p.upt) * SPU * p.act_stride;
+            const uint32_t fbytes = 2u * MV * 4u;
+            bool ok = true;
+            for (uint32_t st = 0; ok && st < nstages; ++st) {
+                if (rb.wrapped) {   // the MMA of stage st - nbb has read the slot
+                    ok = mbar_wait(&mma_done[rm.slot], rm.phase);
+                    rm.next();
+                    if (!ok) break;
+                }
+                mbar_arrive_expect_tx(&b_full[rb.slot], tile_bytes);
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        smem_u32(bbuf + r.slot * p.act_stride)),
-                    "l"(src), "r"(p.act_stride), "r"(smem_u32(&b_full[r.slot]))
+                        smem_u32(bbuf + rb.slot * tile_bytes)),
+                    "l"(src), "r"(tile_bytes), "r"(smem_u32(&b_full[rb.slot]))
+                    : "memory");
+                if (rf.wrapped && !mbar_wait(&f_empty[rf.slot], rf.phase ^ 1u)) break;
+                mbar_arrive_expect_tx(&f_full[rf.slot], fbytes);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_u32(fring + rf.slot * 2u * MV)),
+                    "l"(src + tile_bytes), "r"(fbytes), "r"(smem_u32(&f_full[rf.slot]))
                     : "memory");
                 ++issued;
-                r.next();
+                rb.next();
+                rf.next();
                 src += p.act_stride;
-                if (src == row_end) src = p.act;   // the next tile starts again at block 0
+                if (src == row_end) src = p.act;   // the next tile starts again at K = 0
             }
             for (uint32_t st = issued > p.nbb ? issued - p.nbb : 0; st < issued; ++st)
                 mbar_wait(&b_full[st % p.nbb], (st / p.nbb) & 1u);
+            for (uint32_t st = issued > p.nf ? issued - p.nf : 0; st < issued; ++st)
+                mbar_wait(&f_full[st % p.nf], (st / p.nf) & 1u);
         }
     } else if (warp == kTcWarpMma) {
-        // ── MMA issue: per block, two K=16 MMAs into a fresh accumulator
+        // ── MMA issue: per stage, two K=16 MMAs per block into the block's own accumulator, one commit
         if (lane == 0) {
             const uint32_t idesc = (1u << 4)                            // D: fp32
                                    | ((p.n_pad >> 3) << 17)             // N
                                    | ((kTcRows >> 4) << 24);            // M = 128; A, B: fp16, K-major
-            const uint64_t a0 = tc_smem_desc(abuf), b0 = tc_smem_desc(bbuf);
-            const uint64_t b_step = static_cast<uint64_t>(p.act_stride >> 4), bk_step = (p.n_pad * 32u) >> 4;
-            Ring ra(p.nab), rb(p.nbb), rd(p.nd);
-            uint32_t issued = 0, last_d = 0, last_phase = 0;
+            const uint32_t a_base = smem_u32(abuf), b_base = smem_u32(bbuf);
+            Ring ra(p.nab), rb(p.nbb), rd(p.nd), rm(R);
+            uint32_t issued = 0, last_slot = 0, last_phase = 0;
             for (uint32_t st = 0; st < nstages; ++st) {
                 if (!mbar_wait(&a_full[ra.slot], ra.phase) || !mbar_wait(&b_full[rb.slot], rb.phase)) break;
                 if (rd.wrapped && !mbar_wait(&d_empty[rd.slot], rd.phase ^ 1u)) break;
                 tc_fence_after();
-                const uint64_t da = a0 + static_cast<uint64_t>(ra.slot) * (kTcASlot >> 4);
-                const uint64_t db = b0 + static_cast<uint64_t>(rb.slot) * b_step;
-                const uint32_t d = tmem + rd.slot * p.n_pad;
-                tc_mma_f16(d, da, db, idesc, 0u);
-                tc_mma_f16(d, da + (4096u >> 4), db + bk_step, idesc, 1u);
-                tc_commit(&a_empty[ra.slot]);
-                tc_commit(&d_full[rd.slot]);
+                const uint32_t sa = a_base + ra.slot * kTcASlot, sb = b_base + rb.slot * tile_bytes;
+                const uint32_t d = tmem + rd.slot * 2u * p.n_pad;
+#pragma unroll
+                for (uint32_t k = 0; k < 4; ++k)   // K = 16 steps: 32 bytes along the swizzled rows
+                    tc_mma_f16(d + (k >> 1) * p.n_pad, tc_smem_desc(sa + 32u * k), tc_smem_desc(sb + 32u * k), idesc,
+                               k & 1u);
+                tc_commit(&mma_done[rm.slot]);
                 ++issued;
-                last_d = rd.slot;
-                last_phase = rd.phase;
+                last_slot = rm.slot;
+                last_phase = rm.phase;
                 ra.next();
                 rb.next();
                 rd.next();
+                rm.next();
             }
-            if (issued) mbar_wait(&d_full[last_d], last_phase);
+            if (issued) mbar_wait(&mma_done[last_slot], last_phase);
         }
         __syncwarp();
     } else if (warp >= kTcWarpXf && warp < kTcWarpXf + 4) {
@@ -425,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         const uint32_t row = threadIdx.x - kTcWarpXf * 32u;
         uint32_t q[36];
         bool ok = true;
-        Ring rr(p.nraw), ra(p.nab), rs(p.ns);
+        Ring rr(p.nraw), ra(p.nab), rs(p.ns), rm(R);   // rm: the stage whose MMA frees this stage's A slot
         for (uint32_t i = 0; ok && i < nunits; ++i) {
             if (!warp_wait(&raw_full[rr.slot], rr.phase)) break;
             const uint4* rp = reinterpret_cast<const uint4*>(raw + rr.slot * kTcRawSlot + row * kTcUnitBytes);
@@ -441,13 +467,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&raw_empty[rr.slot]);
             rr.next();
 #pragma unroll
-            for (uint32_t j = 0; j < UB; ++j) {
-                if ((ra.wrapped && !warp_wait(&a_empty[ra.slot], ra.phase ^ 1u)) ||
-                    (rs.wrapped && !warp_wait(&s_empty[rs.slot], rs.phase ^ 1u))) {
+            for (uint32_t j = 0; j < UB; j += 2) {
+                if (ra.wrapped) {
+                    ok = warp_wait(&mma_done[rm.slot], rm.phase);
+                    rm.next();
+                }
+                if (!ok || (rs.wrapped && !warp_wait(&s_empty[rs.slot], rs.phase ^ 1u))) {
                     ok = false;
                     break;
                 }
-                sring[rs.slot * kTcRows + row] = tc_transform_block<DT>(q, j, abuf + ra.slot * kTcASlot, row);
+                uint8_t* a_slot = abuf + ra.slot * kTcASlot;
+                sring[(rs.slot * 2u) * kTcRows + row] = tc_transform_block<DT>(q, j, a_slot, row, 0u);
+                sring[(rs.slot * 2u + 1u) * kTcRows + row] = tc_transform_block<DT>(q, j + 1u, a_slot, row, 1u);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
@@ -469,7 +500,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
         bool waited = false, ok = true;
         uint32_t ncomb = 0;
-        Ring rb(p.nbb), rd(p.nd), rs(p.ns);
+        Ring rd(p.nd), rs(p.ns), rf(p.nf), rm(R);
         uint32_t k = k0, tile = tile0;
 
         // one block: d[] holds its MV accumulator columns for this group (hi, lo per vector)
@@ -482,7 +513,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                 }
             }
         };
-        auto load_block = [&](uint32_t dslot, uint32_t (&d)[MV]) {
+        auto load_block = [&](uint32_t col, uint32_t (&d)[MV]) {
 #pragma unroll
             for (uint32_t c = 0; c < MV / 16; ++c) {
                 uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&d[16 * c]);
@@ -491,20 +522,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                     : "=r"(part[0]), "=r"(part[1]), "=r"(part[2]), "=r"(part[3]), "=r"(part[4]), "=r"(part[5]),
                       "=r"(part[6]), "=r"(part[7]), "=r"(part[8]), "=r"(part[9]), "=r"(part[10]), "=r"(part[11]),
                       "=r"(part[12]), "=r"(part[13]), "=r"(part[14]), "=r"(part[15])
-                    : "r"(tmem_row + dslot * p.n_pad + 16u * c));
+                    : "r"(tmem_row + col + 16u * c));
             }
-        };
-        auto release = [&]() {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&d_empty[rd.slot]);
-                mbar_arrive(&b_empty[rb.slot]);
-                mbar_arrive(&s_empty[rs.slot]);
-            }
-            rd.next();
-            rb.next();
-            rs.next();
         };
 
         for (uint32_t iu = 0; ok && iu < nunits; ++iu) {
@@ -514,42 +533,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
 #pragma unroll
                 for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
             }
-            if constexpr (PAIR) {
 #pragma unroll 1
-                for (uint32_t j = 0; j < UB; j += 2) {
-                    // blocks j and j+1 sit in consecutive ring slots (the rings have even depth)
-                    if (!warp_wait(&d_full[rd.slot], rd.phase) || !warp_wait(&d_full[rd.slot + 1], rd.phase) ||
-                        !warp_wait(&s_full[rs.slot], rs.phase) || !warp_wait(&s_full[rs.slot + 1], rs.phase)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+            for (uint32_t j = 0; j < SPU; ++j) {
+                if (!warp_wait(&mma_done[rm.slot], rm.phase) || !warp_wait(&s_full[rs.slot], rs.phase) ||
+                    !warp_wait(&f_full[rf.slot], rf.phase)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t col = rd.slot * 2u * p.n_pad;
+                const float* sc = sring + (rs.slot * 2u) * kTcRows + row;
+                const float* pf = fring + rf.slot * 2u * MV;
+                if constexpr (MV <= 32) {   // both blocks' accumulators at once
                     uint32_t d0[MV], d1[MV];
-                    load_block(rd.slot, d0);
-                    load_block(rd.slot + 1, d1);
+                    load_block(col, d0);
+                    load_block(col + p.n_pad, d1);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    fold(d0, sring[rs.slot * kTcRows + row],
-                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
-                    release();
-                    fold(d1, sring[rs.slot * kTcRows + row],
-                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
-                    release();
-                }
-            } else {
-#pragma unroll 1
-                for (uint32_t j = 0; j < UB; ++j) {
-                    if (!warp_wait(&d_full[rd.slot], rd.phase) || !warp_wait(&s_full[rs.slot], rs.phase)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                    fold(d0, sc[0], pf);
+                    fold(d1, sc[kTcRows], pf + MV);
+                } else {
                     uint32_t d0[MV];
-                    load_block(rd.slot, d0);
+                    load_block(col, d0);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    fold(d0, sring[rs.slot * kTcRows + row],
-                         reinterpret_cast<const float*>(bbuf + rb.slot * p.act_stride + p.n_pad * 64u));
-                    release();
+                    fold(d0, sc[0], pf);
+                    load_block(col + p.n_pad, d0);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    fold(d0, sc[kTcRows], pf + MV);
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&d_empty[rd.slot]);
+                    mbar_arrive(&s_empty[rs.slot]);
+                    mbar_arrive(&f_empty[rf.slot]);
+                }
+                rd.next();
+                rs.next();
+                rf.next();
+                rm.next();
             }
             if (!ok) break;
             const uint32_t t_now = tile;
