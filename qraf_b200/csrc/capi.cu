@@ -216,22 +216,20 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     // fit ~18 KB (more rows share each staged activation block).  Whole rows.
     while (G < kRowGMax && (2 * G) * rb <= 18432 && 5 * ((max_rows + 2 * G - 1) / (2 * G)) >= 4 * kRowWarps) G *= 2;
     if (!exact && mcount == 2) G = 2;
-    const bool long_rows = 2 * rb > 18432;                                   // not even 2 whole rows per stage
-    const bool few_stages = (max_rows + G - 1) / G < static_cast<uint32_t>(kRowWarps) / 2;   // most warps idle
-    if (!exact && (long_rows || few_stages)) {
-        // FAST: cut rows into pieces of K so that 4 rows share each staged
-        // activation block (2 for two vectors) and there are about three stages
-        // per warp, each within ~18 KB; pieces are summed in order at the end.
+    const bool long_rows = 2 * rb > 18432;   // not even 2 whole rows per stage
+    if (!exact && long_rows) {
+        // FAST, long rows: stages of 4 rows (2 for two vectors) x one piece of K, so
+        // that each staged activation block serves several rows; each stage leaves
+        // its partial sums in shared memory and rows are summed piece by piece, in
+        // order, at the end.  The pieces depend on K and the dtype only, so a row's
+        // arithmetic is the same however the rows are spread over CTAs or GPUs
+        // (row shards give the unsharded bits).
         G = mcount == 2 ? 2u : 4u;
         while (G > 1 && G > max_rows) G >>= 1;
-        const uint32_t groups = (max_rows + G - 1) / G;
-        const uint32_t want = (3 * kRowWarps + groups - 1) / groups;
-        piece = (nblk + want - 1) / want;
-        piece = std::max<uint32_t>(std::min<uint32_t>(long_rows ? 32u : 64u, nblk), (piece + 7u) / 8u * 8u);
-        const uint32_t cap = std::max<uint32_t>(8u, 18432u / (G * bb) / 8u * 8u);
-        piece = std::min(std::min(piece, cap), nblk);
+        const uint32_t cap = 18432u / (4u * bb) / 8u * 8u;   // blocks per piece at 4 rows per ~18 KB stage
+        npieces = (nblk + cap - 1) / cap;
+        piece = ((nblk + npieces - 1) / npieces + 7u) / 8u * 8u;
         npieces = (nblk + piece - 1) / piece;
-        if (npieces == 1) piece = nblk;
     }
     const uint32_t rec = exact ? 144u : kLimbRec;      // bytes per staged 32-element block
     const uint64_t x_bytes = static_cast<uint64_t>(mcount) * nblk * rec;
@@ -252,11 +250,6 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
                               : static_cast<uint32_t>(std::min<uint64_t>({32u, stages, (budget - fixed) / (slot_stride + 12u)}));
     };
     layout();
-    // Pieces: keep at least 4 stages in flight (smaller pieces if need be).
-    while (npieces > 1 && nst < 4 && piece > 64) {
-        piece = std::max<uint32_t>(64u, (piece / 2 + 7u) / 8u * 8u);
-        layout();
-    }
     if (nst == 0) return false;
     RowParams& p = out->p;
     p.w = static_cast<const uint8_t*>(w.data);

@@ -39,6 +39,27 @@ def test_single_rank_group_equals_plain_matvec(cuda, dt, mode):
     comm.destroy()
 
 
+@pytest.mark.parametrize("dt,n,k", [(qb.Q4_0, 8192, 4096), (qb.Q4_0, 2048, 28672), (qb.Q8_0, 2048, 11008),
+                                     (qb.Q4_0, 10240, 8192)])
+@pytest.mark.parametrize("world", [2, 8])
+def test_row_shards_compute_the_unsharded_bits(cuda, dt, n, k, world):
+    """On one GPU: each row shard, as a plain matvec, gives exactly the rows of the
+    full weight's result in both modes (a row's arithmetic does not depend on how
+    rows are spread over CTAs), which is what makes sharded results bit-identical."""
+    import torch
+
+    q = _weight(torch, cuda, dt, n, k)
+    full = qb.Weight.from_device(q, dt, n, k)
+    x = torch.from_numpy(qb.fill_normal(44, 0.0, 1.0, k)).to(cuda)
+    for md in (qb.MODE_EXACT, qb.MODE_FAST):
+        want = qb.matvec_q(full, x, mode=md).cpu().numpy()
+        for r in range(world):
+            r0, r1 = n * r // world, n * (r + 1) // world
+            got = qb.matvec_q(full.shard(world, r), x, mode=md).cpu().numpy()
+            assert got.tobytes() == want[r0:r1].tobytes(), f"mode {md} shard {r}/{world}"
+    assert qb.device_status() == qb.OK
+
+
 def test_missing_peer_times_out_and_is_reported(cuda):
     """Rank 0 of a 2-rank group runs alone: its wait for rank 1's signal (a flag
     nothing sets) must end after its time limit with an error status, leaving the
