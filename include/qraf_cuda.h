@@ -135,6 +135,16 @@ int qraf_cuda_matmul_tc_noalloc(const qraf_weight_t* w, const float* x_dev, floa
 int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint64_t count, uint32_t block_size,
                     float* out_dev, int mode, void* stream);
 
+/* Per-block integer partial sums of the FAST batch-1 arithmetic, for bit-exact
+ * checks against a CPU restatement (verification entry; no counterpart in the
+ * reference, whose path has no integer sums).  For one vector x and every (row
+ * n, block b): d_dev[n][b][j] = sum_i q_i * L_j,i (int32, j = 0..3; codes with
+ * their bias removed; L_j the signed 7-bit digits of X_i = rint(x_i 2^(27-e_b)))
+ * and c_dev[b] = 2^(e_b - 27), exactly as the FAST kernels form them.  Block
+ * size 32, K % 32 == 0, 4-byte-aligned rows, K up to the shared memory (176 B per
+ * block). */
+int qraf_cuda_limb_partials(const qraf_weight_t* w, const float* x_dev, int32_t* d_dev, float* c_dev, void* stream);
+
 /* Per-block partial products p[n][b] = fl(block_sum * scale) exactly as the
  * reference forms them before `total += ...` (quantize.cpp:201-205, 226-234).
  * partials_dev is [rows][ceil(cols / block_size)].  For bit-exact checking. */

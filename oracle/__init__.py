@@ -78,6 +78,9 @@ class Oracle:
         lib.qo_block_partials.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f32p]
         lib.qo_matvec_q_f64.restype = None
         lib.qo_matvec_q_f64.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f64p]
+        lib.qo_limb_partials.restype = None
+        lib.qo_limb_partials.argtypes = [_u8p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p,
+                                         np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"), _f32p]
         self.lib = lib
 
     def fp32_to_fp16(self, f: float) -> int:
@@ -135,6 +138,15 @@ class Oracle:
         self.lib.qo_block_partials(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k,
                                    np.ascontiguousarray(x, dtype=np.float32).ravel(), p.ravel())
         return p
+
+    def limb_partials(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray):
+        """(D [n][k/32][4] int32, c [k/32] float32): the FAST kernels' per-block integer partial sums."""
+        nb = k // 32
+        d = np.zeros((n, nb, 4), dtype=np.int32)
+        c = np.zeros(nb, dtype=np.float32)
+        self.lib.qo_limb_partials(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, n, k,
+                                  np.ascontiguousarray(x, dtype=np.float32).ravel(), d.reshape(-1), c)
+        return d, c
 
     def matvec_f64(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32):
         y = np.zeros(n, dtype=np.float64)

@@ -11,6 +11,7 @@
 #include "qraf_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 /* ── fp16 helpers ───────────────────────────────────────────────────────── */
@@ -324,4 +325,57 @@ void qo_matvec_q_f64(const void* w, uint32_t dtype, int bs, uint32_t N, uint32_t
         }
         y[r] = total;
     }
+}
+
+/* Integer limb partials (the FAST kernels' integer path; see qraf_oracle.h).
+ * Not a restatement of reference code: the reference has no integer path.  The
+ * dot it reconstructs, sum_b scale_b * c_b * sum_j 2^(7(3-j)) D_j, approximates
+ * dot_q*_0_f32 (quantize.cpp:187-239) with X_i carrying 27 bits of each block's
+ * scale. */
+void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, const float* x, int32_t* D,
+                      float* c) {
+    const size_t nb = (size_t)K / 32;
+    const size_t rb = qo_row_bytes(dtype, 32, K);
+    const size_t bb = qo_block_bytes(dtype, 32);
+    int32_t* L = (int32_t*)malloc(sizeof(int32_t) * 4 * 32 * (nb ? nb : 1));
+    for (size_t b = 0; b < nb; b++) {
+        const float* xb = x + 32 * b;
+        float amax = 0.0f;
+        int bad = 0;
+        for (int i = 0; i < 32; i++) {
+            float a = fabsf(xb[i]);
+            if (!isfinite(xb[i])) bad = 1;
+            else if (a > amax) amax = a;
+        }
+        int e = 0;
+        int live = amax > 0.0f && !bad;
+        if (live) frexpf(amax, &e);   /* amax = m * 2^e, m in [0.5, 1) */
+        c[b] = bad ? NAN : (live ? ldexpf(1.0f, e - 27) : 0.0f);
+        for (int i = 0; i < 32; i++) {
+            long X = live ? lrintf(ldexpf(xb[i], 27 - e)) : 0;   /* exact scaling, round half to even */
+            unsigned long ua = (unsigned long)(X < 0 ? -X : X);
+            int sg = X < 0 ? -1 : 1;
+            int32_t* l = L + (b * 32 + (size_t)i) * 4;
+            l[0] = sg * (int)(ua >> 21);
+            l[1] = sg * (int)((ua >> 14) & 127u);
+            l[2] = sg * (int)((ua >> 7) & 127u);
+            l[3] = sg * (int)(ua & 127u);
+        }
+    }
+    for (uint32_t r = 0; r < N; r++) {
+        const uint8_t* row = (const uint8_t*)w + (size_t)r * rb;
+        for (size_t b = 0; b < nb; b++) {
+            const uint8_t* p = row + b * bb;
+            int32_t d[4] = {0, 0, 0, 0};
+            for (int i = 0; i < 32; i++) {
+                int q;
+                if (dtype == QO_DTYPE_Q8_0) q = (int)((const int8_t*)(p + 4))[i];
+                else q = (int)((i & 1) ? ((p[2 + i / 2] >> 4) & 0x0F) : (p[2 + i / 2] & 0x0F)) - 8;
+                const int32_t* l = L + (b * 32 + (size_t)i) * 4;
+                for (int j = 0; j < 4; j++) d[j] += q * l[j];
+            }
+            for (int j = 0; j < 4; j++) D[((size_t)r * nb + b) * 4 + (size_t)j] = d[j];
+        }
+    }
+    free(L);
 }

@@ -83,6 +83,7 @@ def _load() -> C.CDLL:
         "qraf_cuda_matmul_tc_noalloc": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
         "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
+        "qraf_cuda_limb_partials": (i32, [W, vp, vp, vp, vp]),
         "qraf_cuda_quantize": (i32, [u32, vp, u64, u32, vp, vp]),
         "qraf_cuda_quantize_rows": (i32, [u32, vp, u32, u32, u32, vp, vp]),
         "qraf_cuda_dequantize": (i32, [u32, vp, u64, u32, vp, vp]),
@@ -261,6 +262,17 @@ def block_partials(w: Weight, x, stream=None):
     check(_get_lib().qraf_cuda_block_partials(C.byref(w.desc), C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),
                                        _stream(stream)))
     return out
+
+
+def limb_partials(w: Weight, x, stream=None):
+    """(D [rows][cols/32][4] int32, c [cols/32] fp32): the FAST kernels' per-block integer partial sums for x."""
+    torch = _torch()
+    nb = w.cols // 32
+    d = torch.empty((w.rows, nb, 4), dtype=torch.int32, device=x.device)
+    c = torch.empty(nb, dtype=torch.float32, device=x.device)
+    check(_get_lib().qraf_cuda_limb_partials(C.byref(w.desc), C.c_void_p(x.data_ptr()), C.c_void_p(d.data_ptr()),
+                                              C.c_void_p(c.data_ptr()), _stream(stream)))
+    return d, c
 
 
 def quantize(dtype: int, x, block_size: int = 32, stream=None):

@@ -100,6 +100,8 @@ int ensure_device(int* dev_out, DeviceInfo** info_out) {
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 2>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 4>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(limb_partials_kernel<kDtypeQ8>, lim));
+        QRAF_CUDA_TRY(allow_smem(limb_partials_kernel<kDtypeQ4>, lim));
         QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 16>, lim));
         QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 32>, lim));
         QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 64>, lim));
@@ -908,6 +910,33 @@ int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint6
     int rc = qraf_cuda_weight_wrap(q_dev, rb, dtype, block_size, 1, static_cast<uint32_t>(count), &w);
     if (rc) return rc;
     return matvec_impl(&w, x_dev, out_dev, 1, mode, static_cast<cudaStream_t>(stream));
+}
+
+int qraf_cuda_limb_partials(const qraf_weight_t* w, const float* x_dev, int32_t* d_dev, float* c_dev, void* stream) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (!x_dev || !d_dev || !c_dev) return fail(QRAF_ERR_INVALID, "x, d or c is NULL");
+    if (w->block_size != 32 || (w->cols % 32) != 0 || (w->row_bytes % 4) != 0 || (reinterpret_cast<uintptr_t>(w->data) & 3) ||
+        (reinterpret_cast<uintptr_t>(x_dev) & 15))
+        return fail(QRAF_ERR_UNSUPPORTED, "limb partials need block size 32, K %% 32 == 0, 4-byte rows and a "
+                                          "16-byte-aligned x");
+    if (w->rows == 0 || w->cols == 0) return QRAF_OK;
+    DeviceInfo* dev = nullptr;
+    rc = ensure_device(nullptr, &dev);
+    if (rc) return rc;
+    const uint32_t nblk = w->cols / 32;
+    const size_t smem = static_cast<size_t>(nblk) * kLimbRec;
+    if (smem + kSmemReserve > static_cast<size_t>(dev->smem_optin))
+        return fail(QRAF_ERR_UNSUPPORTED, "K = %u needs %zu bytes of shared memory", w->cols, smem);
+    const unsigned grid = (w->rows + 7u) / 8u;
+    if (w->dtype == QRAF_DTYPE_Q8_0)
+        limb_partials_kernel<kDtypeQ8><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev);
+    else
+        limb_partials_kernel<kDtypeQ4><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev);
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
 }
 
 int qraf_cuda_block_partials(const qraf_weight_t* w, const float* x_dev, float* partials_dev, void* stream) {

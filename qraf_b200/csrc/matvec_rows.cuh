@@ -212,37 +212,51 @@ __device__ __forceinline__ float combine_limbs(int d0, int d1, int d2, int d3) {
     return fmaf(__int2float_rn(d0 * 128 + d1), 16384.0f, __int2float_rn(d2 * 128 + d3));
 }
 
-__device__ __forceinline__ float q8_block_limb(const uint32_t (&wv)[9], const LimbBlock& lb) {
-    int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+// D_j = sum_i q_i L_j,i for one block: exact int32 dot products (dp4a).
+__device__ __forceinline__ void q8_block_dsums(const uint32_t (&wv)[9], const LimbBlock& lb, int (&d)[4]) {
+    d[0] = d[1] = d[2] = d[3] = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
         const int q = static_cast<int>(wv[1 + w]);
-        d0 = __dp4a(q, static_cast<int>(lb.L[0][w]), d0);
-        d1 = __dp4a(q, static_cast<int>(lb.L[1][w]), d1);
-        d2 = __dp4a(q, static_cast<int>(lb.L[2][w]), d2);
-        d3 = __dp4a(q, static_cast<int>(lb.L[3][w]), d3);
+        d[0] = __dp4a(q, static_cast<int>(lb.L[0][w]), d[0]);
+        d[1] = __dp4a(q, static_cast<int>(lb.L[1][w]), d[1]);
+        d[2] = __dp4a(q, static_cast<int>(lb.L[2][w]), d[2]);
+        d[3] = __dp4a(q, static_cast<int>(lb.L[3][w]), d[3]);
     }
-    return combine_limbs(d0, d1, d2, d3);
+}
+
+__device__ __forceinline__ float q8_block_limb(const uint32_t (&wv)[9], const LimbBlock& lb) {
+    int d[4];
+    q8_block_dsums(wv, lb, d);
+    return combine_limbs(d[0], d[1], d[2], d[3]);
 }
 
 // Q4: nibbles (0..15, the +8-biased codes) are exact as signed bytes; the bias
 // is removed with the plane sums: sum (nib - 8) L = sum nib L - 8 S.
-__device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const LimbBlock& lb, const int4 S) {
-    int d0 = -8 * S.x, d1 = -8 * S.y, d2 = -8 * S.z, d3 = -8 * S.w;
+__device__ __forceinline__ void q4_block_dsums(const uint32_t (&qw)[4], const LimbBlock& lb, const int4 S, int (&d)[4]) {
+    d[0] = -8 * S.x;
+    d[1] = -8 * S.y;
+    d[2] = -8 * S.z;
+    d[3] = -8 * S.w;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
         const int lo = static_cast<int>(qw[w] & 0x0F0F0F0Fu);          // elements 8w + 0, 2, 4, 6
         const int hi = static_cast<int>((qw[w] >> 4) & 0x0F0F0F0Fu);   // elements 8w + 1, 3, 5, 7
-        d0 = __dp4a(lo, static_cast<int>(lb.L[0][2 * w]), d0);
-        d1 = __dp4a(lo, static_cast<int>(lb.L[1][2 * w]), d1);
-        d2 = __dp4a(lo, static_cast<int>(lb.L[2][2 * w]), d2);
-        d3 = __dp4a(lo, static_cast<int>(lb.L[3][2 * w]), d3);
-        d0 = __dp4a(hi, static_cast<int>(lb.L[0][2 * w + 1]), d0);
-        d1 = __dp4a(hi, static_cast<int>(lb.L[1][2 * w + 1]), d1);
-        d2 = __dp4a(hi, static_cast<int>(lb.L[2][2 * w + 1]), d2);
-        d3 = __dp4a(hi, static_cast<int>(lb.L[3][2 * w + 1]), d3);
+        d[0] = __dp4a(lo, static_cast<int>(lb.L[0][2 * w]), d[0]);
+        d[1] = __dp4a(lo, static_cast<int>(lb.L[1][2 * w]), d[1]);
+        d[2] = __dp4a(lo, static_cast<int>(lb.L[2][2 * w]), d[2]);
+        d[3] = __dp4a(lo, static_cast<int>(lb.L[3][2 * w]), d[3]);
+        d[0] = __dp4a(hi, static_cast<int>(lb.L[0][2 * w + 1]), d[0]);
+        d[1] = __dp4a(hi, static_cast<int>(lb.L[1][2 * w + 1]), d[1]);
+        d[2] = __dp4a(hi, static_cast<int>(lb.L[2][2 * w + 1]), d[2]);
+        d[3] = __dp4a(hi, static_cast<int>(lb.L[3][2 * w + 1]), d[3]);
     }
-    return combine_limbs(d0, d1, d2, d3);
+}
+
+__device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const LimbBlock& lb, const int4 S) {
+    int d[4];
+    q4_block_dsums(qw, lb, S, d);
+    return combine_limbs(d[0], d[1], d[2], d[3]);
 }
 
 // One thread's share of a limb record: elements 8*sub .. 8*sub+7 of a block
@@ -366,6 +380,42 @@ __global__ void __launch_bounds__(256) limb_prep_kernel(const float* __restrict_
         b = __ldcg(xm + 2u * task + 1u);
     }
     limb_record_part<DT>(a, b, act, recs + (static_cast<size_t>(m) * nblk + (task >> 2)) * kLimbRec, task & 3u);
+}
+
+// Per-block integer partial sums for verification (qraf_cuda_limb_partials):
+// the records are staged as the row kernel stages them, then one warp per row,
+// lane = block, writes D[row][block][0..3] and (row 0) c[block].
+template <uint32_t DT>
+__global__ void __launch_bounds__(256) limb_partials_kernel(const uint8_t* __restrict__ w, uint64_t row_bytes,
+                                                            uint32_t N, uint32_t K, uint32_t nblk,
+                                                            const float* __restrict__ x, int32_t* __restrict__ d_out,
+                                                            float* __restrict__ c_out) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    stage_limb_records<DT>(x, K, smem, nblk * kLimbRec, 1u, nblk, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= N) return;
+    const uint8_t* row = w + static_cast<size_t>(r) * row_bytes;
+    for (uint32_t b = lane; b < nblk; b += 32u) {
+        const uint8_t* rec = smem + kLimbRec * b;
+        LimbBlock lb;
+        lds_limbs(rec, lb);
+        int d[4];
+        if constexpr (DT == kDtypeQ8) {
+            uint32_t wv[9];
+            const uint32_t* pw = reinterpret_cast<const uint32_t*>(row + 36u * b);
+#pragma unroll
+            for (int i = 0; i < 9; ++i) wv[i] = __ldg(pw + i);
+            q8_block_dsums(wv, lb, d);
+        } else {
+            uint32_t qw[4], s16;
+            load_q4_block(row, b, qw, s16);
+            q4_block_dsums(qw, lb, *reinterpret_cast<const int4*>(rec + 144), d);
+        }
+        *reinterpret_cast<int4*>(d_out + (static_cast<size_t>(r) * nblk + b) * 4u) = make_int4(d[0], d[1], d[2], d[3]);
+        if (r == 0) c_out[b] = *reinterpret_cast<const float*>(rec + 128);
+    }
 }
 
 // ── EXACT block dots: the reference's order, scalar, never fused ─────────

@@ -154,6 +154,31 @@ def test_block_partials_bit_exact(cuda, small_cases):
         assert p.tobytes() == c["partials"].tobytes(), f"case {i}"
 
 
+@pytest.mark.parametrize("dt", [qb.Q8_0, qb.Q4_0])
+@pytest.mark.parametrize("n,k", [(64, 4096), (8, 28672), (300, 2048)])
+def test_limb_partials_bit_exact(cuda, oracle_lib, dt, n, k):
+    """The FAST kernels' per-block integer partial sums D_j (and the block factors)
+    equal the oracle's integer restatement bit for bit, on ordinary blocks and on
+    blocks of zeros, tiny (subnormal-range), huge and non-finite values."""
+    import torch
+
+    wf = torch.from_numpy(qb.fill_normal(42, 0.0, 0.02, n * k)).to(cuda).reshape(n, k)
+    q = qb.quantize_rows(dt, wf).reshape(-1)
+    w = qb.Weight.from_device(q, dt, n, k)
+    x = qb.fill_normal(43, 0.0, 1.0, k)
+    x[32:64] = 0.0
+    x[64:96] *= np.float32(1e-40)
+    x[96:128] *= np.float32(1e30)
+    x[130] = np.float32(3e-42)
+    x[200] = np.float32("nan")
+    x[290] = np.float32("inf")
+    d, c = qb.limb_partials(w, torch.from_numpy(x).to(cuda))
+    d_ref, c_ref = oracle_lib.limb_partials(dt, q.cpu().numpy(), n, k, x)
+    assert np.array_equal(d.cpu().numpy(), d_ref)
+    assert np.array_equal(c.cpu().numpy(), c_ref, equal_nan=True)
+    assert qb.device_status() == qb.OK
+
+
 def test_unaligned_pointers_take_the_generic_path(cuda, small_cases):
     import torch
 

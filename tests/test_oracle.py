@@ -106,3 +106,50 @@ def test_oracle_matches_reference_randomised(oracle_lib):
         a = np.float32(oracle_lib.fp16_to_fp32(h))
         b = np.float32(ref.lib.qref_fp16_to_fp32(h))
         assert a.tobytes() == b.tobytes() or (np.isnan(a) and np.isnan(b))
+
+
+def _block_scales(dt, q, n, k):
+    nb = k // 32
+    raw = np.asarray(q, np.uint8).reshape(n, nb, 36 if dt == 10 else 18)
+    if dt == 10:
+        return raw[:, :, :4].copy().view(np.float32)[:, :, 0].astype(np.float64)
+    return raw[:, :, :2].copy().view(np.float16)[:, :, 0].astype(np.float64)
+
+
+@pytest.mark.parametrize("dt", [10, 20])
+def test_limb_partials_reconstruct_the_dot(oracle_lib, dt):
+    """The integer restatement of the FAST path: sum_b scale_b c_b sum_j 2^(7(3-j)) D_j
+    matches the fp64 dot up to the rounding of X_i (half a unit of c_b per element),
+    including blocks of zeros, of tiny (subnormal-range) and of huge values."""
+    n, k = 16, 512
+    rng = np.random.default_rng(7)
+    w = rng.normal(0.0, 0.02, (n, k)).astype(np.float32)
+    x = rng.normal(0.0, 1.0, k).astype(np.float32)
+    x[32:64] = 0.0
+    x[64:96] *= np.float32(1e-40)
+    x[96:128] *= np.float32(1e30)
+    x[130] = np.float32(3e-42)
+    q = oracle_lib.quantize_rows(dt, w)
+    d, c = oracle_lib.limb_partials(dt, q, n, k, x)
+    assert c[1] == 0.0 and not d[:, 1].any()
+    ints = (d.astype(np.int64) * np.array([1 << 21, 1 << 14, 1 << 7, 1], np.int64)).sum(-1)
+    sc = _block_scales(dt, q, n, k)
+    rec = (sc * c.astype(np.float64)[None, :] * ints).sum(1)
+    y64 = oracle_lib.matvec_f64(dt, q, n, k, x)
+    qmax = 127.0 if dt == 10 else 8.0
+    bound = (np.abs(sc) * c.astype(np.float64)[None, :] * 0.5 * 32 * qmax).sum(1) * (1 + 1e-12) + 1e-300
+    assert (np.abs(rec - y64) <= bound).all(), (np.abs(rec - y64) / bound).max()
+
+
+def test_limb_partials_known_block(oracle_lib):
+    """Block max 0.75 (so e = 0, c = 2^-27 and X_i = rint(x_i 2^27)) against codes all 1."""
+    k = 32
+    raw = np.zeros(36, np.uint8)
+    raw[:4] = np.frombuffer(np.float32(1.0).tobytes(), np.uint8)
+    raw[4:] = 1
+    x = (np.arange(1, 33, dtype=np.float32) / np.float32(64.0)) * np.float32(0.98)
+    x[-1] = np.float32(0.75)
+    d, c = oracle_lib.limb_partials(10, raw, 1, k, x)
+    assert c[0] == np.float32(2.0 ** -27)
+    ints = int((d[0, 0].astype(np.int64) * np.array([1 << 21, 1 << 14, 1 << 7, 1])).sum())
+    assert ints == int(sum(int(np.rint(float(v) * 2.0 ** 27)) for v in x))
