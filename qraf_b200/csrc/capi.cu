@@ -716,8 +716,32 @@ std::mutex g_host_mutex;
 std::map<CacheKey, qraf_weight_t> g_cache;
 HostStaging g_staging[64];
 
-int grow(HostStaging& s, size_t xn, size_t yn) {
+// Per cached weight, M and mode: a CUDA graph of the call's device work (x in,
+// kernels, y out) on the staging stream, captured after a first eager call.
+// Graphs hold the staging buffers and the cached weight, so they are dropped
+// when either changes.  A null exec records that capture did not succeed.
+struct GraphKey {
+    CacheKey w;
+    uint32_t M;
+    int mode;
+    bool operator<(const GraphKey& o) const { return std::tie(w, M, mode) < std::tie(o.w, o.M, o.mode); }
+};
+std::map<GraphKey, cudaGraphExec_t> g_graphs;
+
+void drop_graphs(int device) {
+    for (auto it = g_graphs.begin(); it != g_graphs.end();) {
+        if (device < 0 || it->first.w.device == device) {
+            if (it->second) cudaGraphExecDestroy(it->second);
+            it = g_graphs.erase(it);
+        } else {
+            ++it;
+        }
+    }
+}
+
+int grow(HostStaging& s, size_t xn, size_t yn, int device) {
     if (!s.stream) QRAF_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    if (xn > s.x_cap || yn > s.y_cap) drop_graphs(device);   // they hold the old buffers
     if (xn > s.x_cap) {
         if (s.x_pinned) cudaFreeHost(s.x_pinned);
         if (s.x_dev) cudaFree(s.x_dev);
@@ -1214,23 +1238,49 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     HostStaging& s = g_staging[dev];
     const size_t xn = std::max<size_t>(static_cast<size_t>(M) * in_dim, 4);
     const size_t yn = static_cast<size_t>(M) * out_dim;
-    rc = grow(s, xn, yn);
+    rc = grow(s, xn, yn, dev);
     if (rc) return rc;
-    if (in_dim) {
-        std::memcpy(s.x_pinned, x_host, static_cast<size_t>(M) * in_dim * sizeof(float));
-        QRAF_CUDA_TRY(cudaMemcpyAsync(s.x_dev, s.x_pinned, static_cast<size_t>(M) * in_dim * sizeof(float),
-                                      cudaMemcpyHostToDevice, s.stream));
+    const size_t x_bytes = static_cast<size_t>(M) * in_dim * sizeof(float);
+    // the device work of one call: x in, the kernels, y out (all on the staging stream)
+    auto enqueue = [&]() -> int {
+        if (in_dim) QRAF_CUDA_TRY(cudaMemcpyAsync(s.x_dev, s.x_pinned, x_bytes, cudaMemcpyHostToDevice, s.stream));
+        const int r = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mode, s.stream);
+        if (r) return r;
+        QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+        return QRAF_OK;
+    };
+    if (in_dim) std::memcpy(s.x_pinned, x_host, x_bytes);
+    const GraphKey gk{key, M, mode};
+    auto g = g_graphs.find(gk);
+    if (g != g_graphs.end() && g->second) {
+        QRAF_CUDA_TRY(cudaGraphLaunch(g->second, s.stream));
+    } else {
+        rc = enqueue();   // first call: eager (sets up plans and any scratch)
+        if (rc) return rc;
     }
-    rc = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mode, s.stream);
-    if (rc) return rc;
-    QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
     QRAF_CUDA_TRY(cudaStreamSynchronize(s.stream));
     std::memcpy(y_host, s.y_pinned, yn * sizeof(float));
+    if (g == g_graphs.end()) {
+        // capture the same work for the next calls with this weight, M and mode
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        if (cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int crc = enqueue();
+            const cudaError_t e = cudaStreamEndCapture(s.stream, &graph);
+            if (crc == QRAF_OK && e == cudaSuccess && graph &&
+                cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+                exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+        }
+        cudaGetLastError();   // a capture that did not work only means eager calls
+        g_graphs.emplace(gk, exec);
+    }
     return QRAF_OK;
 }
 
 int qraf_cuda_host_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_host_mutex);
+    drop_graphs(-1);
     int cur = 0;
     cudaGetDevice(&cur);
     for (auto& kv : g_cache) {

@@ -234,6 +234,28 @@ def test_host_entry_matches_reference(cuda, small_cases, oracle_lib):
     qb.host_cache_clear()
 
 
+def test_host_entry_repeated_calls(cuda, oracle_lib):
+    """Repeated host-entry calls with one weight replay a cached graph of the call's
+    device work: every call still reads its own x and returns its own exact result,
+    for the row kernel, the long-K path with limb prep, and the tensor cores."""
+    for dt, n, k, m, mode in [(qb.Q8_0, 512, 4096, 1, qb.MODE_EXACT), (qb.Q4_0, 96, 28672, 1, qb.MODE_FAST),
+                              (qb.Q8_0, 640, 2048, 20, qb.MODE_TC)]:
+        w = qb.fill_normal(42, 0.0, 0.02, n * k).reshape(n, k)
+        q = oracle_lib.quantize_rows(dt, w).reshape(-1)
+        for call in range(4):
+            x = qb.fill_normal(100 + call, 0.0, 1.0, m * k).reshape(m, k)
+            y = np.zeros((m, n), np.float32)
+            qb.dispatch_matvec_q(q, q.size, dt, 32, n, k, x, y, m=m, mode=mode)
+            y_ref = np.stack([oracle_lib.matvec(dt, q, n, k, x[j]) for j in range(m)])
+            if mode == qb.MODE_EXACT:
+                assert y.tobytes() == y_ref.tobytes(), f"call {call}"
+            else:
+                y64 = np.stack([oracle_lib.matvec_f64(dt, q, n, k, x[j]) for j in range(m)])
+                assert_fast_ok(y, y_ref, y64, f"dt={dt} mode={mode} call {call}")
+    qb.host_cache_clear()
+    assert qb.device_status() == qb.OK
+
+
 # ── full-size configurations (BASELINE.json configs 1-5) ──────────────────
 _W_CACHE = {}
 _Q_HOST = {}
