@@ -439,7 +439,7 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     p.nbb = 16;
     p.nraw = 8;
     while (p.nraw > 4 && layout(p.nraw, p.nbb) > avail) --p.nraw;
-    while (p.nbb > 4 && layout(p.nraw, p.nbb) > avail) --p.nbb;
+    while (p.nbb > 4 && layout(p.nraw, p.nbb) > avail) p.nbb -= 2;   // ring depths stay even (pairs of stages)
     while (p.nraw > 2 && layout(p.nraw, p.nbb) > avail) --p.nraw;
     if (layout(p.nraw, p.nbb) > avail) return false;
     out->smem = layout(p.nraw, p.nbb);

@@ -233,13 +233,22 @@ __device__ __forceinline__ float tc_transform_block(const uint32_t (&q)[36], uin
     }
 }
 
-// Wait by lane 0 for the whole warp (every lane takes the same branch after).
+// Wait for the whole warp: every lane polls the same phase (one warp-wide
+// instruction, no divergent branch), and the vote gives every lane the same answer.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok = 1u;
-    if ((threadIdx.x & 31u) == 0u) ok = mbar_wait(bar, parity) ? 1u : 0u;
-    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-    __syncwarp();
-    return ok != 0u;
+    const bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xFFFFFFFFu, ok);
+}
+
+// One lane of a converged warp (the lowest); the others skip the guarded code.
+__device__ __forceinline__ bool tc_elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
 }
 
 // Position in a ring of n slots, advanced one step at a time (no division in
@@ -269,7 +278,13 @@ __device__ __forceinline__ uint32_t tc_start(uint32_t c, uint32_t units, uint32_
 
 // ── the tensor-core kernel ─────────────────────────────────────────────────
 // MV: activation vectors handled per launch (16, 32 or 64); n_pad = 2 MV.
-// Stage st covers blocks 2st, 2st+1 of the CTA's sequence of units.
+// Stage st covers blocks 2st, 2st+1 of the CTA's sequence of units.  Every role
+// synchronises once per PAIR of stages (2s, 2s+1): every ring depth and every
+// CTA's stage count are even, so a pair sits in slots (i, i+1) of one lap of
+// each ring.  Where one party arrives on a ring in stage order (the transform
+// warps, the epilogue warps, tcgen05.commit), the second stage's phase implies
+// the first's and only it is waited for; slots filled by separate bulk copies
+// are waited for one by one.
 template <uint32_t DT, uint32_t MV>
 __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
     constexpr uint32_t UB = DT == kDtypeQ4 ? 8u : 4u;   // blocks per raw unit
@@ -301,7 +316,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     uint32_t* bcast = tmem_slot + 1;
 
     if (blockDim.x != kTcThreads || p.n_pad != 2u * MV || p.M > MV || p.unit_blocks != UB || p.nab >= R ||
-        p.nbb >= R || p.nd > R || 2u * p.nd * p.n_pad > kTcTmemCols) {
+        p.nbb >= R || p.nd > R || 2u * p.nd * p.n_pad > kTcTmemCols ||
+        ((p.nab | p.nbb | p.nd | p.ns | p.nf) & 1u) != 0u) {
         if (threadIdx.x == 0) raise_error(kErrBadLaunch);
         return;
     }
@@ -376,30 +392,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             const uint8_t* row_end = p.act + static_cast<size_t>(p.upt) * SPU * p.act_stride;
             const uint32_t fbytes = 2u * MV * 4u;
             bool ok = true;
-            for (uint32_t st = 0; ok && st < nstages; ++st) {
-                if (rb.wrapped) {   // the MMA of stage st - nbb has read the slot
-                    ok = mbar_wait(&mma_done[rm.slot], rm.phase);
+            for (uint32_t st = 0; ok && st < nstages; st += 2) {
+                if (rb.wrapped) {   // the MMAs up to stage st + 1 - nbb have read both slots
+                    ok = mbar_wait(&mma_done[rm.slot + 1u], rm.phase);
+                    rm.next();
                     rm.next();
                     if (!ok) break;
                 }
-                mbar_arrive_expect_tx(&b_full[rb.slot], tile_bytes);
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        smem_u32(bbuf + rb.slot * tile_bytes)),
-                    "l"(src), "r"(tile_bytes), "r"(smem_u32(&b_full[rb.slot]))
-                    : "memory");
-                if (rf.wrapped && !mbar_wait(&f_empty[rf.slot], rf.phase ^ 1u)) break;
-                mbar_arrive_expect_tx(&f_full[rf.slot], fbytes);
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                        smem_u32(fring + rf.slot * 2u * MV)),
-                    "l"(src + tile_bytes), "r"(fbytes), "r"(smem_u32(&f_full[rf.slot]))
-                    : "memory");
-                ++issued;
+                const uint8_t* srcs[2];
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    srcs[h] = src;
+                    mbar_arrive_expect_tx(&b_full[rb.slot + h], tile_bytes);
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            smem_u32(bbuf + (rb.slot + h) * tile_bytes)),
+                        "l"(src), "r"(tile_bytes), "r"(smem_u32(&b_full[rb.slot + h]))
+                        : "memory");
+                    src += p.act_stride;
+                    if (src == row_end) src = p.act;   // the next tile starts again at K = 0
+                }
+                if (rf.wrapped && !mbar_wait(&f_empty[rf.slot + 1u], rf.phase ^ 1u)) break;
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    mbar_arrive_expect_tx(&f_full[rf.slot + h], fbytes);
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            smem_u32(fring + (rf.slot + h) * 2u * MV)),
+                        "l"(srcs[h] + tile_bytes), "r"(fbytes), "r"(smem_u32(&f_full[rf.slot + h]))
+                        : "memory");
+                }
+                issued += 2;
+                rb.next();
                 rb.next();
                 rf.next();
-                src += p.act_stride;
-                if (src == row_end) src = p.act;   // the next tile starts again at K = 0
+                rf.next();
             }
             for (uint32_t st = issued > p.nbb ? issued - p.nbb : 0; st < issued; ++st)
                 mbar_wait(&b_full[st % p.nbb], (st / p.nbb) & 1u);
@@ -407,36 +434,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                 mbar_wait(&f_full[st % p.nf], (st / p.nf) & 1u);
         }
     } else if (warp == kTcWarpMma) {
-        // ── MMA issue: per stage, two K=16 MMAs per block into the block's own accumulator, one commit
-        if (lane == 0) {
-            const uint32_t idesc = (1u << 4)                            // D: fp32
-                                   | ((p.n_pad >> 3) << 17)             // N
-                                   | ((kTcRows >> 4) << 24);            // M = 128; A, B: fp16, K-major
-            const uint32_t a_base = smem_u32(abuf), b_base = smem_u32(bbuf);
-            Ring ra(p.nab), rb(p.nbb), rd(p.nd), rm(R);
-            uint32_t issued = 0, last_slot = 0, last_phase = 0;
-            for (uint32_t st = 0; st < nstages; ++st) {
-                if (!mbar_wait(&a_full[ra.slot], ra.phase) || !mbar_wait(&b_full[rb.slot], rb.phase)) break;
-                if (rd.wrapped && !mbar_wait(&d_empty[rd.slot], rd.phase ^ 1u)) break;
-                tc_fence_after();
-                const uint32_t sa = a_base + ra.slot * kTcASlot, sb = b_base + rb.slot * tile_bytes;
-                const uint32_t d = tmem + rd.slot * 2u * p.n_pad;
+        // ── MMA issue: per stage, two K=16 MMAs per block into the block's own
+        // accumulator and one commit.  The whole warp runs the loop (its operands
+        // stay warp-uniform) and one elected lane issues.
+        const uint32_t idesc = (1u << 4)                            // D: fp32
+                               | ((p.n_pad >> 3) << 17)             // N
+                               | ((kTcRows >> 4) << 24);            // M = 128; A, B: fp16, K-major
+        const uint32_t a_base = smem_u32(abuf), b_base = smem_u32(bbuf);
+        Ring ra(p.nab), rb(p.nbb), rd(p.nd), rm(R);
+        uint32_t issued = 0, last_slot = 0, last_phase = 0;
+        for (uint32_t st = 0; st < nstages; st += 2) {
+            if (!warp_wait(&a_full[ra.slot + 1u], ra.phase) || !warp_wait(&b_full[rb.slot], rb.phase) ||
+                !warp_wait(&b_full[rb.slot + 1u], rb.phase))
+                break;
+            if (rd.wrapped && !warp_wait(&d_empty[rd.slot + 1u], rd.phase ^ 1u)) break;
+            tc_fence_after();
+            if (tc_elect_one()) {
 #pragma unroll
-                for (uint32_t k = 0; k < 4; ++k)   // K = 16 steps: 32 bytes along the swizzled rows
-                    tc_mma_f16(d + (k >> 1) * p.n_pad, tc_smem_desc(sa + 32u * k), tc_smem_desc(sb + 32u * k), idesc,
-                               k & 1u);
-                tc_commit(&mma_done[rm.slot]);
-                ++issued;
-                last_slot = rm.slot;
-                last_phase = rm.phase;
-                ra.next();
-                rb.next();
-                rd.next();
-                rm.next();
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t sa = a_base + (ra.slot + h) * kTcASlot, sb = b_base + (rb.slot + h) * tile_bytes;
+                    const uint32_t d = tmem + (rd.slot + h) * 2u * p.n_pad;
+#pragma unroll
+                    for (uint32_t k = 0; k < 4; ++k)   // K = 16 steps: 32 bytes along the swizzled rows
+                        tc_mma_f16(d + (k >> 1) * p.n_pad, tc_smem_desc(sa + 32u * k), tc_smem_desc(sb + 32u * k),
+                                   idesc, k & 1u);
+                    tc_commit(&mma_done[rm.slot + h]);
+                }
             }
-            if (issued) mbar_wait(&mma_done[last_slot], last_phase);
+            __syncwarp();
+            issued += 2;
+            last_slot = rm.slot + 1u;
+            last_phase = rm.phase;
+            ra.next();
+            ra.next();
+            rb.next();
+            rb.next();
+            rd.next();
+            rd.next();
+            rm.next();
+            rm.next();
         }
-        __syncwarp();
+        if (issued) warp_wait(&mma_done[last_slot], last_phase);
     } else if (warp >= kTcWarpXf && warp < kTcWarpXf + 4) {
         // ── transform: raw blocks -> fp16 codes in the A ring, scales into the scale ring
         const uint32_t row = threadIdx.x - kTcWarpXf * 32u;
@@ -458,25 +496,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&raw_empty[rr.slot]);
             rr.next();
 #pragma unroll
-            for (uint32_t j = 0; j < UB; j += 2) {
-                if (ra.wrapped) {
-                    ok = warp_wait(&mma_done[rm.slot], rm.phase);
+            for (uint32_t j = 0; j < UB; j += 4) {   // two stages of two blocks
+                if (ra.wrapped) {   // the MMAs up to stage s + 1 - nab have read both A slots
+                    ok = warp_wait(&mma_done[rm.slot + 1u], rm.phase);
+                    rm.next();
                     rm.next();
                 }
-                if (!ok || (rs.wrapped && !warp_wait(&s_empty[rs.slot], rs.phase ^ 1u))) {
+                if (!ok || (rs.wrapped && !warp_wait(&s_empty[rs.slot + 1u], rs.phase ^ 1u))) {
                     ok = false;
                     break;
                 }
-                uint8_t* a_slot = abuf + ra.slot * kTcASlot;
-                sring[(rs.slot * 2u) * kTcRows + row] = tc_transform_block<DT>(q, j, a_slot, row, 0u);
-                sring[(rs.slot * 2u + 1u) * kTcRows + row] = tc_transform_block<DT>(q, j + 1u, a_slot, row, 1u);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    uint8_t* a_slot = abuf + (ra.slot + h) * kTcASlot;
+                    float* srow = sring + ((rs.slot + h) * 2u) * kTcRows + row;
+                    srow[0] = tc_transform_block<DT>(q, j + 2u * h, a_slot, row, 0u);
+                    srow[kTcRows] = tc_transform_block<DT>(q, j + 2u * h + 1u, a_slot, row, 1u);
+                }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&a_full[ra.slot]);
                     mbar_arrive(&s_full[rs.slot]);
+                    mbar_arrive(&a_full[ra.slot + 1u]);
+                    mbar_arrive(&s_full[rs.slot + 1u]);
                 }
                 ra.next();
+                ra.next();
+                rs.next();
                 rs.next();
             }
         }
@@ -525,42 +572,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                 for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
             }
 #pragma unroll 1
-            for (uint32_t j = 0; j < SPU; ++j) {
-                if (!warp_wait(&mma_done[rm.slot], rm.phase) || !warp_wait(&s_full[rs.slot], rs.phase) ||
-                    !warp_wait(&f_full[rf.slot], rf.phase)) {
+            for (uint32_t j = 0; j < SPU; j += 2) {   // a pair of stages
+                if (!warp_wait(&mma_done[rm.slot + 1u], rm.phase) || !warp_wait(&s_full[rs.slot + 1u], rs.phase) ||
+                    !warp_wait(&f_full[rf.slot], rf.phase) || !warp_wait(&f_full[rf.slot + 1u], rf.phase)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t col = rd.slot * 2u * p.n_pad;
-                const float* sc = sring + (rs.slot * 2u) * kTcRows + row;
-                const float* pf = fring + rf.slot * 2u * MV;
-                if constexpr (MV <= 32) {   // both blocks' accumulators at once
-                    uint32_t d0[MV], d1[MV];
-                    load_block(col, d0);
-                    load_block(col + p.n_pad, d1);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    fold(d0, sc[0], pf);
-                    fold(d1, sc[kTcRows], pf + MV);
-                } else {
-                    uint32_t d0[MV];
-                    load_block(col, d0);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    fold(d0, sc[0], pf);
-                    load_block(col + p.n_pad, d0);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    fold(d0, sc[kTcRows], pf + MV);
+#pragma unroll 1
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t col = (rd.slot + h) * 2u * p.n_pad;
+                    const float* sc = sring + ((rs.slot + h) * 2u) * kTcRows + row;
+                    const float* pf = fring + (rf.slot + h) * 2u * MV;
+                    if constexpr (MV <= 32) {   // both blocks' accumulators at once
+                        uint32_t d0[MV], d1[MV];
+                        load_block(col, d0);
+                        load_block(col + p.n_pad, d1);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        fold(d0, sc[0], pf);
+                        fold(d1, sc[kTcRows], pf + MV);
+                    } else {
+                        uint32_t d0[MV];
+                        load_block(col, d0);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        fold(d0, sc[0], pf);
+                        load_block(col + p.n_pad, d0);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        fold(d0, sc[kTcRows], pf + MV);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&d_empty[rd.slot]);
-                    mbar_arrive(&s_empty[rs.slot]);
-                    mbar_arrive(&f_empty[rf.slot]);
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h) {
+                        mbar_arrive(&d_empty[rd.slot + h]);
+                        mbar_arrive(&s_empty[rs.slot + h]);
+                        mbar_arrive(&f_empty[rf.slot + h]);
+                    }
                 }
                 rd.next();
+                rd.next();
+                rs.next();
                 rs.next();
                 rf.next();
+                rf.next();
+                rm.next();
                 rm.next();
             }
             if (!ok) break;
