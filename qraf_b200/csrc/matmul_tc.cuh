@@ -665,13 +665,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             ++ncomb;
             if (*reinterpret_cast<volatile uint32_t*>(bcast) != 1u) continue;
             __threadfence();
-            for (uint32_t v = 0; v < HV && m0 + v < p.M; ++v) {
-                float sum = 0.0f;
-                for (uint32_t cc = c_first; cc <= c_last; ++cc) {
-                    const uint32_t sl = tc_start(cc, p.units, C) / p.upt == t_now ? 0u : 1u;
-                    sum += __ldcg(p.partial + ((static_cast<size_t>(cc) * 2u + sl) * p.M + m0 + v) * kTcRows + row);
-                }
-                if (row < rows) yt[static_cast<size_t>(m0 + v) * p.N] = sum;
+            // every vector's sum runs over the CTAs in order; one CTA's HV loads are in
+            // flight together instead of one L2 round trip per (vector, CTA)
+            float sum[HV];
+#pragma unroll
+            for (uint32_t v = 0; v < HV; ++v) sum[v] = 0.0f;
+            for (uint32_t cc = c_first; cc <= c_last; ++cc) {
+                const uint32_t sl = tc_start(cc, p.units, C) / p.upt == t_now ? 0u : 1u;
+                const float* src = p.partial + ((static_cast<size_t>(cc) * 2u + sl) * p.M + m0) * kTcRows + row;
+#pragma unroll
+                for (uint32_t v = 0; v < HV; ++v)
+                    if (m0 + v < p.M) sum[v] += __ldcg(src + static_cast<size_t>(v) * kTcRows);
+            }
+            if (row < rows) {
+#pragma unroll
+                for (uint32_t v = 0; v < HV; ++v)
+                    if (m0 + v < p.M) yt[static_cast<size_t>(m0 + v) * p.N] = sum[v];
             }
         }
         tc_fence_before();
