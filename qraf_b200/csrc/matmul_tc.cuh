@@ -579,6 +579,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                     break;
                 }
                 tc_fence_after();
+                if constexpr (MV == 16) {   // the pair's four blocks: every load, then one wait
+                    uint32_t d[4][MV];
+#pragma unroll
+                    for (uint32_t b = 0; b < 4; ++b) load_block((rd.slot * 2u + b) * p.n_pad, d[b]);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (uint32_t b = 0; b < 4; ++b)
+                        fold(d[b], sring[((rs.slot + (b >> 1)) * 2u + (b & 1u)) * kTcRows + row],
+                             fring + (rf.slot + (b >> 1)) * 2u * MV + (b & 1u) * MV);
+                } else {
 #pragma unroll 1
                 for (uint32_t h = 0; h < 2; ++h) {
                     const uint32_t col = (rd.slot + h) * 2u * p.n_pad;
@@ -600,6 +610,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                         fold(d0, sc[kTcRows], pf + MV);
                     }
+                }
                 }
                 tc_fence_before();
                 __syncwarp();
