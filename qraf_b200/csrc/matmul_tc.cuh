@@ -130,7 +130,8 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 
 // ── activation preparation: x (fp32) -> fp16 limb tiles + block factors ────
 // One warp per (block b, vector slot m); lane i takes element i.  Tile rows
-// 2m / 2m+1 hold hi / lo of vector m; rows of vectors >= M are zero; each
+// m / MV+m hold hi / lo of vector m (so the accumulator columns of the hi limbs
+// of consecutive vectors are adjacent, as are the lo limbs'); rows of vectors >= M are zero; each
 // block pair's tile is followed by its factors (one float per block and vector
 // slot).  Also
 // zeroes the stream-K tile counters of the call.  A block holding a NaN or an
@@ -161,8 +162,8 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ 
     const int lo = X - hi * 4096;
     const uint32_t kk = 32u * (b & 1u) + tc_k_slot<DT>(lane);   // element of the block pair's 64
     uint8_t* tile = act + static_cast<size_t>(b >> 1) * (n_pad * 128u + 2u * half * 4u);
-    *reinterpret_cast<__half*>(tile + tc_sw128_off(2u * m, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(hi);
-    *reinterpret_cast<__half*>(tile + tc_sw128_off(2u * m + 1u, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(lo);
+    *reinterpret_cast<__half*>(tile + tc_sw128_off(m, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(hi);
+    *reinterpret_cast<__half*>(tile + tc_sw128_off(half + m, kk >> 3) + 2u * (kk & 7u)) = __int2half_rn(lo);
     if (lane == 0)
         reinterpret_cast<float*>(tile + n_pad * 128u)[(b & 1u) * half + m] =
             m >= M ? 0.0f : finite ? ldexpf(1.0f, e - 23) : __int_as_float(0x7FC00000);
@@ -531,7 +532,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         // ── epilogue: thread = weight row = TMEM lane; group g owns vectors [g HV, (g+1) HV)
         const uint32_t quad = warp & 3u, grp = warp >> 2;
         const uint32_t row = quad * 32u + lane;
-        const uint32_t tmem_row = tmem + ((quad * 32u) << 16) + grp * MV;   // hi/lo columns of this group
+        const uint32_t tmem_row = tmem + ((quad * 32u) << 16) + grp * HV;   // this group's hi columns; lo at +MV
         const uint32_t m0 = grp * HV;
         float acc[HV];
 #pragma unroll
@@ -541,26 +542,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         Ring rd(p.nd), rs(p.ns), rf(p.nf), rm(R);
         uint32_t k = k0, tile = tile0;
 
-        // one block: d[] holds its MV accumulator columns for this group (hi, lo per vector)
+        // one block: d[0, HV) holds the hi sums of this group's vectors, d[HV, 2 HV) the lo
+        // sums.  Pairs of vectors go through the packed fp32x2 units; per element the
+        // operations (and roundings) are t = fma(hi, 4096, lo), s = scale * factor,
+        // acc = fma(t, s, acc).
         auto fold = [&](const uint32_t (&d)[MV], float sc, const float* pfb) {
+            const float2 k4096 = make_float2(4096.0f, 4096.0f), sc2 = make_float2(sc, sc);
 #pragma unroll
-            for (uint32_t v = 0; v < HV; ++v) {
+            for (uint32_t v = 0; v < HV; v += 2) {
                 if (m0 + v < p.M) {
-                    const float t = fmaf(__uint_as_float(d[2 * v]), 4096.0f, __uint_as_float(d[2 * v + 1]));
-                    acc[v] = fmaf(t, sc * pfb[m0 + v], acc[v]);
+                    const float2 dh = make_float2(__uint_as_float(d[v]), __uint_as_float(d[v + 1]));
+                    const float2 dl = make_float2(__uint_as_float(d[HV + v]), __uint_as_float(d[HV + v + 1]));
+                    const float2 t = __ffma2_rn(dh, k4096, dl);
+                    const float2 s2 = __fmul2_rn(sc2, *reinterpret_cast<const float2*>(pfb + m0 + v));
+                    const float2 a = __ffma2_rn(t, s2, make_float2(acc[v], acc[v + 1]));
+                    acc[v] = a.x;
+                    acc[v + 1] = a.y;
                 }
             }
         };
+        auto ld8 = [&](uint32_t taddr, uint32_t* part) {
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                         : "=r"(part[0]), "=r"(part[1]), "=r"(part[2]), "=r"(part[3]), "=r"(part[4]), "=r"(part[5]),
+                           "=r"(part[6]), "=r"(part[7])
+                         : "r"(taddr));
+        };
+        auto ld16 = [&](uint32_t taddr, uint32_t* part) {
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                : "=r"(part[0]), "=r"(part[1]), "=r"(part[2]), "=r"(part[3]), "=r"(part[4]), "=r"(part[5]),
+                  "=r"(part[6]), "=r"(part[7]), "=r"(part[8]), "=r"(part[9]), "=r"(part[10]), "=r"(part[11]),
+                  "=r"(part[12]), "=r"(part[13]), "=r"(part[14]), "=r"(part[15])
+                : "r"(taddr));
+        };
         auto load_block = [&](uint32_t col, uint32_t (&d)[MV]) {
+            if constexpr (HV == 8) {
+                ld8(tmem_row + col, &d[0]);
+                ld8(tmem_row + col + MV, &d[HV]);
+            } else {
 #pragma unroll
-            for (uint32_t c = 0; c < MV / 16; ++c) {
-                uint32_t (&part)[16] = *reinterpret_cast<uint32_t(*)[16]>(&d[16 * c]);
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                    : "=r"(part[0]), "=r"(part[1]), "=r"(part[2]), "=r"(part[3]), "=r"(part[4]), "=r"(part[5]),
-                      "=r"(part[6]), "=r"(part[7]), "=r"(part[8]), "=r"(part[9]), "=r"(part[10]), "=r"(part[11]),
-                      "=r"(part[12]), "=r"(part[13]), "=r"(part[14]), "=r"(part[15])
-                    : "r"(tmem_row + col + 16u * c));
+                for (uint32_t c = 0; c < HV / 16; ++c) {
+                    ld16(tmem_row + col + 16u * c, &d[16 * c]);
+                    ld16(tmem_row + col + MV + 16u * c, &d[HV + 16 * c]);
+                }
             }
         };
 
