@@ -16,8 +16,8 @@
 //
 // Work split.  A stage is two blocks (64 elements of K) of 128 weight rows:
 // four K=16 MMAs with 128-byte-swizzled operands (two per block, each block
-// into its own accumulator) and one commit, which every consumer of the stage
-// (weight ring, activation ring, epilogue) waits on.
+// into its own accumulator) and one commit, which the consumers of the stage
+// (weight ring, activation ring, epilogue) wait on, a pair of stages at a time.
 // A unit is 128 weight rows (the MMA's M) by 144 bytes of each
 // row (8 Q4 blocks or 4 Q8 blocks; 144 keeps every copy 16-byte aligned),
 // fetched by one 2-D TMA copy (the weight seen as [N][row_bytes / 4] words).
@@ -29,7 +29,8 @@
 // order, so results are deterministic.
 //
 // Warps (thread = weight row): 0-7 run the epilogue in two groups that split
-// the vectors (warp w reads TMEM lanes 32(w%4)..+31), 8-11 turn the raw bytes
+// the vectors (warp w reads TMEM lanes 32(w%4)..+31; the hi limbs of the
+// vectors sit in accumulator columns [0, MV), the lo limbs in [MV, 2 MV)), 8-11 turn the raw bytes
 // of each block into fp16 codes in the MMA's shared-memory layout and pass the
 // block scales on through a small ring of their own.  Warp 12 streams the raw
 // weight units, warp 13 allocates TMEM and issues the MMAs, warp 14 streams
