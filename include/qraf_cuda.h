@@ -53,7 +53,7 @@ extern "C" {
                               weights.  Uses per-stream scratch memory that the library
                               allocates at a stream's first call of a given size (make that
                               call before capturing the stream in a CUDA graph). */
-#define QRAF_MODE_AUTO  3  /* FAST below M = 16, TC from M = 16 where the weight allows */
+#define QRAF_MODE_AUTO  3  /* FAST for M <= 2, TC from M = 3 where the weight allows (else FAST) */
 /* Or-able flag: the kernel may start while the previous kernel in the stream is
  * still running and fetch the weight before waiting for it (programmatic
  * dependent launch).  Only valid when that previous kernel does not write the

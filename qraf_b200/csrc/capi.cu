@@ -603,12 +603,16 @@ int check_weight(const qraf_weight_t* w) {
     return QRAF_OK;
 }
 
+constexpr uint32_t kAutoTcMinVectors = 3;
+
 int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode_in, cudaStream_t st) {
     int rc = check_weight(w);
     if (rc) return rc;
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
     int mode = mode_in & 0xFF;
-    if (mode == QRAF_MODE_AUTO) mode = (M >= 16 && tc_eligible(*w)) ? QRAF_MODE_TC : QRAF_MODE_FAST;
+    // AUTO: the row kernel for one or two vectors, the tensor-core tile from three (measured on B200: at M = 3 the
+    // tile matches or beats the CUDA-core kernels on every BASELINE shape, at M = 2 it is slower on all of them)
+    if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(*w)) ? QRAF_MODE_TC : QRAF_MODE_FAST;
     if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC)
         return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
     if (M == 0 || w->rows == 0) return QRAF_OK;

@@ -1,4 +1,4 @@
-"""Tensor-core path (MODE_TC; MODE_AUTO takes it for M >= 16): the tcgen05 tile
+"""Tensor-core path (MODE_TC; MODE_AUTO takes it for M >= 3): the tcgen05 tile
 against the oracle's reference-order result, with the FAST bar (assert_fast_ok):
 every output within allclose(rtol 1e-5, atol 1e-6) of the reference, or no
 farther from the fp64 value than the reference's own worst error.  Shapes cover
@@ -52,7 +52,7 @@ def test_tc_matches_reference(cuda, oracle_lib, dt, n, k, m):
 @pytest.mark.parametrize("dt,n,k", [(qb.Q8_0, 11008, 2048), (qb.Q4_0, 2048, 11008)])
 def test_tc_batching_shapes(cuda, oracle_lib, dt, n, k):
     """BASELINE config 4 shapes at M = 16, 32, 64 through MODE_AUTO (which takes
-    the tensor cores for M >= 16); outputs checked on a sample of rows."""
+    the tensor cores for M >= 3); outputs checked on a sample of rows."""
     import torch
 
     q, w, x = _setup(torch, cuda, dt, n, k, 64)
@@ -66,6 +66,21 @@ def test_tc_batching_shapes(cuda, oracle_lib, dt, n, k):
         y_ref = np.stack([oracle_lib.matvec(dt, qh, rows.size, k, xh[j]) for j in range(m)])
         y64 = np.stack([oracle_lib.matvec_f64(dt, qh, rows.size, k, xh[j]) for j in range(m)])
         assert_fast_ok(y[:, rows], y_ref, y64, f"AUTO dt={dt} {n}x{k} M={m}")
+    assert qb.device_status() == qb.OK
+
+
+def test_auto_switches_to_the_tile_at_three_vectors(cuda, oracle_lib):
+    """MODE_AUTO: the row kernel (FAST) for one or two vectors, the tensor-core tile
+    from three; both against the reference."""
+    import torch
+
+    q, w, x = _setup(torch, cuda, qb.Q4_0, 640, 2048, 8)
+    for m in (1, 2, 3, 8):
+        xm = x[:m].contiguous()
+        y = qb.matvec_q(w, xm, mode=qb.MODE_AUTO)
+        want = qb.matvec_q(w, xm, mode=qb.MODE_TC if m >= 3 else qb.MODE_FAST)
+        assert torch.equal(y, want), f"M={m}"
+        _check(oracle_lib, qb.Q4_0, q, 640, 2048, xm, y.cpu().numpy(), f"AUTO M={m}")
     assert qb.device_status() == qb.OK
 
 
