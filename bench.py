@@ -14,7 +14,8 @@ bytes (N*K/32*block_bytes + 4K + 4N per matvec) of every launch of every rank
 / max-over-ranks device time of the K timed steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>]] [--mode fast|exact]
+                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>]|<model>_token[_m<M>]]
+                  [--mode fast|exact|tc|auto]
 
 With --gpus N > 1 (launched by torch.distributed.run) every rank runs the same
 workload on its own weights (independent matvec objects, no data-path
@@ -233,9 +234,10 @@ def run_ours(args, dt, n, k, m):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     qb.init(local)
-    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC}[args.mode]
-    kernel = "qmm_tc_kernel" if args.mode == "tc" else ("qmv_rows_kernel" if m <= 2 or args.mode == "exact"
-                                                         else "qmv_stream_kernel")
+    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
+    use_tc = args.mode == "tc" or (args.mode == "auto" and m >= 3)   # AUTO's switch (every bench shape qualifies)
+    kernel = "qmm_tc_kernel" if use_tc else ("qmv_rows_kernel" if m <= 2 or args.mode == "exact"
+                                             else "qmv_stream_kernel")
 
     # Seeded weight, quantized on the GPU (byte-exact with the reference quantizer).
     wf = torch.from_numpy(qb.fill_normal(42, 0.0, 0.02, n * k)).to(dev).reshape(n, k)
@@ -493,10 +495,10 @@ def run_token(args, model, m):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     qb.init(local)
-    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
     fused = world > 1 and args.allgather == "fused"
-    if world > 1 and m > 2 and mode == qb.MODE_FAST:
-        raise SystemExit("the row-sharded FAST path takes M <= 2; use --mode exact for larger M")
+    if fused and (mode in (qb.MODE_TC, qb.MODE_AUTO) or (m > 2 and mode == qb.MODE_FAST)):
+        raise SystemExit("the fused row-sharded path runs EXACT, or FAST with M <= 2; use --allgather nccl")
 
     # Seeded weights, generated on the device in 1024-row chunks (so every rank
     # draws the same rows whatever the world size), quantized byte-exactly, one
@@ -726,7 +728,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="q4_4096x4096")
-    ap.add_argument("--mode", choices=["fast", "exact", "tc"], default="fast")
+    ap.add_argument("--mode", choices=["fast", "exact", "tc", "auto"], default="fast")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
