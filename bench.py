@@ -341,8 +341,10 @@ def run_ours(args, dt, n, k, m):
         e2e_s = float(t[0])
     e2e = {"value": world * e2e_steps * R * per_launch / e2e_s / 1e9, "unit": "GB/s",
            "h2d_bytes_per_step": R * m * k * 4, "d2h_bytes_per_step": R * m * n * 4, "steps": e2e_steps,
-           "path": "qraf_cuda_matvec_q_host (drop-in body of qraf::dispatch_matvec_q): pinned staging, H2D x, "
-                   "kernel, D2H y, stream sync per call; weights cached on the device after their first call"}
+           "path": "qraf_cuda_matvec_q_host (drop-in body of qraf::dispatch_matvec_q): pinned staging, H2D x and "
+                   "D2H y by SM copy kernels over the mapped pinned buffers, the matvec kernel, stream sync per call "
+                   "(one cached CUDA graph per weight, M and mode); weights cached on the device after their first "
+                   "call"}
     qb.host_cache_clear()
 
     cpu = None

@@ -711,6 +711,8 @@ struct HostStaging {
     cudaStream_t stream = nullptr;
     float* x_pinned = nullptr;
     float* y_pinned = nullptr;
+    float* x_map = nullptr;   // the pinned buffers as device pointers (null: copies go through cudaMemcpyAsync)
+    float* y_map = nullptr;
     float* x_dev = nullptr;
     float* y_dev = nullptr;
     size_t x_cap = 0, y_cap = 0;   // in floats
@@ -750,23 +752,29 @@ int grow(HostStaging& s, size_t xn, size_t yn, int device) {
         if (s.x_pinned) cudaFreeHost(s.x_pinned);
         if (s.x_dev) cudaFree(s.x_dev);
         s.x_pinned = nullptr;
+        s.x_map = nullptr;
         s.x_dev = nullptr;
         s.x_cap = 0;
         if (cudaMallocHost(&s.x_pinned, xn * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&s.x_dev, xn * sizeof(float)) != cudaSuccess)
             return fail(QRAF_ERR_NOMEM, "staging allocation of %zu floats failed", xn);
         s.x_cap = xn;
+        if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.x_map), s.x_pinned, 0) != cudaSuccess) s.x_map = nullptr;
+        cudaGetLastError();
     }
     if (yn > s.y_cap) {
         if (s.y_pinned) cudaFreeHost(s.y_pinned);
         if (s.y_dev) cudaFree(s.y_dev);
         s.y_pinned = nullptr;
+        s.y_map = nullptr;
         s.y_dev = nullptr;
         s.y_cap = 0;
         if (cudaMallocHost(&s.y_pinned, yn * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&s.y_dev, yn * sizeof(float)) != cudaSuccess)
             return fail(QRAF_ERR_NOMEM, "staging allocation of %zu floats failed", yn);
         s.y_cap = yn;
+        if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.y_map), s.y_pinned, 0) != cudaSuccess) s.y_map = nullptr;
+        cudaGetLastError();
     }
     return QRAF_OK;
 }
@@ -1245,11 +1253,27 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     rc = grow(s, xn, yn, dev);
     if (rc) return rc;
     const size_t x_bytes = static_cast<size_t>(M) * in_dim * sizeof(float);
-    // the device work of one call: x in, the kernels, y out (all on the staging stream)
+    // the device work of one call: x in, the kernels, y out (all on the staging stream).
+    // x and y cross by SM copies of the mapped pinned buffers where the device maps
+    // them; the matvec then overlaps its weight prefetch with the copy of x (the
+    // copy kernel writes no weight).
+    auto sm_copy = [&](bool from_host, const float* src, float* dst, size_t n) -> int {
+        const size_t n4 = std::max<size_t>(n / 4, 1);
+        const int grid = static_cast<int>(std::min<size_t>((n4 + 255) / 256, 4u * 148u));
+        if (from_host) host_copy_kernel<true><<<grid, 256, 0, s.stream>>>(src, dst, n);
+        else host_copy_kernel<false><<<grid, 256, 0, s.stream>>>(src, dst, n);
+        QRAF_CUDA_TRY(cudaGetLastError());
+        return QRAF_OK;
+    };
     auto enqueue = [&]() -> int {
-        if (in_dim) QRAF_CUDA_TRY(cudaMemcpyAsync(s.x_dev, s.x_pinned, x_bytes, cudaMemcpyHostToDevice, s.stream));
-        const int r = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mode, s.stream);
+        int r = QRAF_OK;
+        if (in_dim && s.x_map) r = sm_copy(true, s.x_map, s.x_dev, static_cast<size_t>(M) * in_dim);
+        else if (in_dim) QRAF_CUDA_TRY(cudaMemcpyAsync(s.x_dev, s.x_pinned, x_bytes, cudaMemcpyHostToDevice, s.stream));
         if (r) return r;
+        const int mv_mode = (in_dim && s.x_map) ? (mode | QRAF_MODE_FLAG_OVERLAP) : mode;
+        r = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mv_mode, s.stream);
+        if (r) return r;
+        if (s.y_map) return sm_copy(false, s.y_dev, s.y_map, yn);
         QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
         return QRAF_OK;
     };

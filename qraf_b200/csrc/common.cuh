@@ -112,6 +112,31 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Copy n floats between pinned host memory (mapped into the device's address
+// space) and device memory with the SMs: for the few kilobytes of one host
+// call's x or y this takes a fraction of a copy engine's latency.  Reads of
+// host memory skip the caches (ld.global.cv), writes to it go straight through
+// (st.global.wt).  The next kernel in the stream may launch at once; a kernel
+// launched as its programmatic dependent waits for this grid before it reads dst.
+template <bool FROM_HOST>
+__global__ void __launch_bounds__(256) host_copy_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                        size_t n) {
+    pdl_launch_dependents();
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t n4 = n >> 2;   // src and dst are 16-byte aligned
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (size_t i = t; i < n4; i += stride) {
+        if constexpr (FROM_HOST) d4[i] = __ldcv(s4 + i);
+        else __stwt(d4 + i, s4[i]);
+    }
+    for (size_t i = 4 * n4 + t; i < n; i += stride) {
+        if constexpr (FROM_HOST) dst[i] = __ldcv(src + i);
+        else __stwt(dst + i, src[i]);
+    }
+}
+
 // ── packed fp32x2 arithmetic (sm_100a), IEEE round-to-nearest, no ftz ────
 // CUDA's float2 intrinsics.  Used where rounding order is free (FAST mode):
 // a packed multiply followed by a packed add was measured to round like a
