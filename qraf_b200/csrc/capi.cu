@@ -1259,10 +1259,17 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     // copy kernel writes no weight).
     auto sm_copy = [&](bool from_host, const float* src, float* dst, size_t n) -> int {
         const size_t n4 = std::max<size_t>(n / 4, 1);
-        const int grid = static_cast<int>(std::min<size_t>((n4 + 255) / 256, 4u * 148u));
-        if (from_host) host_copy_kernel<true><<<grid, 256, 0, s.stream>>>(src, dst, n);
-        else host_copy_kernel<false><<<grid, 256, 0, s.stream>>>(src, dst, n);
-        QRAF_CUDA_TRY(cudaGetLastError());
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = from_host ? 0 : 1;   // y's copy launches under the matvec and waits for it in the kernel
+        cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 4u * 148u)));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s.stream;
+        QRAF_CUDA_TRY(from_host ? cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n)
+                                : cudaLaunchKernelEx(&cfg, host_copy_kernel<false>, src, dst, n));
         return QRAF_OK;
     };
     auto enqueue = [&]() -> int {

@@ -118,10 +118,14 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // host memory skip the caches (ld.global.cv), writes to it go straight through
 // (st.global.wt).  The next kernel in the stream may launch at once; a kernel
 // launched as its programmatic dependent waits for this grid before it reads dst.
+// The device-to-host copy is itself launched as a programmatic dependent of the
+// matvec before it (so it waits here, before reading src); a wait without such
+// a launch returns at once.
 template <bool FROM_HOST>
 __global__ void __launch_bounds__(256) host_copy_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                                         size_t n) {
     pdl_launch_dependents();
+    if constexpr (!FROM_HOST) pdl_wait();
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t n4 = n >> 2;   // src and dst are 16-byte aligned
