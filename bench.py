@@ -45,12 +45,23 @@ METRIC = "Q8/Q4 matvec HBM GB/s"
 
 
 def parse_workload(name: str):
-    """'q4_4096x4096' -> (dtype, N, K, M); an optional '_m<M>' suffix sets the batch."""
-    parts = name.split("_")
+    """'q4_4096x4096' -> (dtype, N, K, M); an optional '_m<M>' suffix sets the batch
+    (a trailing '_shard' is read by is_shard_workload)."""
+    parts = [p for p in name.split("_") if p != "shard"]
     dt = {"q4": Q4, "q8": Q8}[parts[0]]
     n, k = (int(v) for v in parts[1].split("x"))
     m = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("m") else 1
     return dt, n, k, m
+
+
+def is_shard_workload(name: str) -> bool:
+    return name.endswith("_shard")
+
+
+def launches_per_call(n_rows, k, sm_count):
+    """Kernels one FAST M <= 2 matvec launches: the activation-limb prep kernel runs
+    when a row has at least 256 blocks and a CTA gets at most 96 rows (capi.cu)."""
+    return 2 if k // 32 >= 256 and -(-n_rows // sm_count) <= 96 else 1
 
 
 def alg_bytes(dt, n, k, m):
@@ -471,6 +482,195 @@ def qb_fill(seed, n):
     return qb.fill_normal(seed, 0.0, 1.0, n)
 
 
+def run_shard(args, dt, n, k, m):
+    """One projection split by output rows over the N ranks (rank r: rows
+    [r N/W, (r+1) N/W)); every call all-gathers the rows into every rank's y,
+    inside the kernel (peer stores over NVLink, default) or by NCCL after the
+    plain kernel (--allgather nccl).  On one GPU: the unsharded kernel.  A STEP is
+    R calls over a pool of shard copies (>= 4x L2 per GPU, R a multiple of 4),
+    replayed from a CUDA graph with overlapping launches; single-call latency is
+    the same calls one after another.  value = bytes of the WHOLE projection x
+    calls / max-over-ranks device time ("strong": the work per call is fixed)."""
+    import torch
+
+    import qraf_b200 as qb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    qb.init(local)
+    if m > 2 or args.mode not in ("fast", "exact"):
+        raise SystemExit("sharded projections run FAST with M <= 2, or EXACT")
+    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+    fused = world > 1 and args.allgather == "fused"
+    r0, r1 = n * rank // world, n * (rank + 1) // world
+    rows = r1 - r0
+
+    # the shard's rows of the seeded weight (seeded per 1024-row chunk, so every
+    # world size draws the same rows), quantized byte-exactly on the device
+    gen = torch.Generator(device=dev)
+    wf = torch.empty((rows, k), device=dev)
+    for c0 in range(r0 // 1024 * 1024, r1, 1024):
+        gen.manual_seed(42 * 1_000_003 + c0 // 1024)
+        blk = torch.randn((min(1024, n - c0), k), generator=gen, device=dev) * 0.02
+        a, b = max(c0, r0), min(c0 + 1024, r1)
+        wf[a - r0:b - r0] = blk[a - c0:b - c0]
+    q = qb.quantize_rows(dt, wf, 32).reshape(-1)
+    del wf
+    sbytes = q.numel()
+    props = torch.cuda.get_device_properties(dev)
+    free, _ = torch.cuda.mem_get_info(dev)
+    R = max(4, math.ceil(4 * props.L2_cache_size / sbytes))
+    R = min(R, max(4, int(0.5 * free // sbytes)))
+    R = (R + 3) // 4 * 4   # whole rounds of the comm's four output buffers
+    pool = torch.empty((R, sbytes), dtype=torch.uint8, device=dev)
+    pool[:] = q
+    weights = [qb.Weight.from_device(pool[i], dt, rows, k) for i in range(R)]
+    x = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * k)).to(dev).reshape(m, k)
+
+    comm = None
+    ys = [torch.empty((m, n), device=dev) for _ in range(R)] if world == 1 else None
+    loc = gat = None
+    if fused:
+        comm = qb.make_comm(world, rank, m * n, qb.torch_all_gather_bytes())
+    elif world > 1:
+        loc = [torch.empty((m, rows), device=dev) for _ in range(R)]
+        gat = [torch.empty((world * m * rows,), device=dev) for _ in range(R)]
+
+    def call(i, flags):
+        if world == 1:
+            return qb.matvec_q(weights[i], x, ys[i], mode=mode | flags)
+        if fused:
+            return comm.matvec_q(weights[i], n, r0, x, mode=mode | flags)
+        qb.matvec_q(weights[i], x, loc[i], mode=mode | flags)
+        dist.all_gather_into_tensor(gat[i], loc[i])
+        return gat[i]
+
+    ov = qb.MODE_FLAG_OVERLAP if args.overlap else 0
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        for i in range(R):
+            call(i, ov)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(R):
+            last = call(i, ov)
+    g_seq = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_seq, stream=s):
+        for i in range(R):
+            call(i, 0)
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    g_seq.replay()
+    torch.cuda.synchronize(dev)
+    if qb.device_status() != qb.OK:
+        raise SystemExit("device status not OK after warm-up")
+
+    clocks = ClockSampler(local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    seq_reps = max(3, min(20, args.steps // 10))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    with torch.cuda.stream(s):
+        t0.record()
+        for _ in range(args.steps):
+            g.replay()
+        t1.record()
+        t2.record()
+        for _ in range(seq_reps):
+            g_seq.replay()
+        t3.record()
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    elapsed_ms, call_ms = t0.elapsed_time(t1), t2.elapsed_time(t3) / (seq_reps * R)
+
+    # e2e: the step's x in from pinned host memory, its last call's y out
+    x_host = torch.from_numpy(qb.fill_normal(44, 0.0, 1.0, m * k)).reshape(m, k).pin_memory()
+    y_host = torch.empty((m, n), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    if dist:
+        dist.barrier()
+    te = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(s):
+            x.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(last.reshape(world, m, rows).permute(1, 0, 2).reshape(m, n) if (world > 1 and not fused
+                                                                                      and m > 1) else
+                         last.reshape(m, n), non_blocking=True)
+        s.synchronize()
+    e2e_s = time.perf_counter() - te
+    status = qb.device_status()
+    if dist:
+        t = torch.tensor([elapsed_ms, call_ms, e2e_s, float(status != qb.OK)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, call_ms, e2e_s = float(t[0]), float(t[1]), float(t[2])
+        status = status if not float(t[3]) else max(status, 1)
+
+    full = alg_bytes(dt, n, k, m)
+    shard = alg_bytes(dt, rows, k, m)
+    peak, peak_src = measured_peaks()
+    cpu = None
+    if rank == 0 and world == 1:
+        q_host = q.cpu().numpy()
+        xh = x.cpu().numpy()
+        ops, el, kind = cpu_reference(dt, n, k, m, q_host, xh, 1, args.cpu_seconds, max_ops=1000)
+        cpu = {"value": ops * full / el / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+               "sample": f"{ops} full {n}x{k} matvecs (M={m}) through dispatch_matvec_q's scalar path, "
+                         "single-threaded as the reference runs it on Linux"}
+    if rank == 0:
+        calls = args.steps * R
+        line = {
+            "metric": METRIC, "value": calls * full / (elapsed_ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "N": n, "K": k, "M": m, "block": 32,
+                       "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode,
+                       "parallelism": (f"rows split over {world} GPUs ({rows} per GPU), all-gather "
+                                       f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
+                       if world > 1 else "single GPU (unsharded kernel)",
+                       "pool_copies": R, "l2_policy": "inputs larger than L2: rotating pool of shard copies",
+                       "step": f"{R} calls (CUDA graph replay, overlapping launches)",
+                       "us_per_call_pipelined": elapsed_ms * 1e3 / calls,
+                       "us_per_call_alone": call_ms * 1e3},
+            "e2e": {"value": e2e_steps * R * full / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": m * k * 4,
+                    "d2h_bytes_per_step": m * n * 4, "steps": e2e_steps,
+                    "path": "H2D x from pinned memory, the step's graph, D2H of the last call's y, stream sync"},
+            "gpu_launches": calls * launches_per_call(rows, k, props.multi_processor_count),
+            "roofline": {"bound": "hbm", "achieved": shard / (call_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": shard / (call_ms / 1e3) / 1e9 / peak, "traffic": None, "peak_source": peak_src,
+                         "what": "per GPU: shard bytes of one call / the call's duration alone",
+                         "kernel": "qmv_rows_kernel"},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    del g, g_seq
+    if dist:
+        dist.barrier()
+    if comm is not None:
+        comm.destroy()
+    if dist:
+        dist.destroy_process_group()
+
+
 def run_token(args, model, m):
     """One STEP = one decode token of M vectors through every projection of the model
     (layers x projections + LM head), captured as one CUDA graph and replayed.
@@ -744,6 +944,8 @@ def main():
     dt, n, k, m = parse_workload(args.workload)
     if args.impl == "reference":
         run_reference_arm(args, dt, n, k, m)
+    elif is_shard_workload(args.workload):
+        run_shard(args, dt, n, k, m)
     else:
         run_ours(args, dt, n, k, m)
 
