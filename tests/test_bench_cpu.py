@@ -1,0 +1,61 @@
+"""bench.py host logic on the CPU: workload names, the algorithmic byte counts the
+roofline divides by, the launch count rule, and the reference arm's JSON line
+(the driver's contract) on a small workload."""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def test_workload_names():
+    assert bench.parse_workload("q4_4096x4096") == (bench.Q4, 4096, 4096, 1)
+    assert bench.parse_workload("q8_11008x2048_m16") == (bench.Q8, 11008, 2048, 16)
+    assert bench.parse_workload("q4_28672x8192_shard") == (bench.Q4, 28672, 8192, 1)
+    assert bench.parse_workload("q4_28672x8192_m2_shard") == (bench.Q4, 28672, 8192, 2)
+    assert bench.is_shard_workload("q4_28672x8192_shard")
+    assert not bench.is_shard_workload("q4_4096x4096")
+    assert bench.parse_token_workload("llama70b_token") == ("llama70b", 1)
+    assert bench.parse_token_workload("qwen3b_token_m16") == ("qwen3b", 16)
+    assert bench.parse_token_workload("q4_4096x4096") is None
+
+
+def test_algorithmic_bytes_match_the_measurement_plan():
+    """Per-call bytes = weights + x + y (configs 1 and 2 of the measurement plan)."""
+    assert bench.alg_bytes(bench.Q8, 4096, 4096, 1) == 18_907_136
+    assert bench.alg_bytes(bench.Q4, 4096, 4096, 1) == 9_469_952
+    # config 4, weights only: Q8 25,362,432 B and Q4 12,681,216 B for 11008 x 2048
+    assert bench.alg_bytes(bench.Q8, 11008, 2048, 16) - 4 * 16 * (2048 + 11008) == 25_362_432
+    assert bench.alg_bytes(bench.Q4, 2048, 11008, 16) - 4 * 16 * (2048 + 11008) == 12_681_216
+
+
+def test_launch_count_rule():
+    """The limb-prep kernel runs for rows of >= 256 blocks when a CTA gets <= 96 rows."""
+    assert bench.launches_per_call(4096, 4096, 148) == 1        # 128 blocks per row
+    assert bench.launches_per_call(10240, 8192, 148) == 2       # 70 rows per CTA
+    assert bench.launches_per_call(14336, 8192, 148) == 1       # 97 rows per CTA
+    assert bench.launches_per_call(8192, 28672, 148) == 2
+
+
+def test_reference_arm_prints_the_contract_line():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+                          "q8_256x512", "--steps", "2", "--warmup", "1"], capture_output=True, text=True, env=env,
+                         timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "GB/s"
+    assert d["value"] > 0 and d["higher_is_better"] is True
+    assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
