@@ -1234,7 +1234,8 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     if (block_size == 0) block_size = 32;   // a null QuantScheme means 32 (backend.cpp:135)
     if (!w_host || (!x_host && in_dim)) return fail(QRAF_ERR_INVALID, "w or x is NULL");
     int dev = 0;
-    int rc = ensure_device(&dev, nullptr);
+    DeviceInfo* dinfo = nullptr;
+    int rc = ensure_device(&dev, &dinfo);
     if (rc) return rc;
     const uint64_t need = qraf_row_bytes(dtype, block_size, in_dim) * out_dim;
     (void)w_size;   // the reference never reads it either; it reads exactly `need` bytes
@@ -1265,7 +1266,7 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = from_host ? 0 : 1;   // y's copy launches under the matvec and waits for it in the kernel
-        cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 4u * 148u)));
+        cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 4u * dinfo->sm_count)));
         cfg.blockDim = dim3(256);
         cfg.stream = s.stream;
         QRAF_CUDA_TRY(from_host ? cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n)
