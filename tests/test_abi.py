@@ -80,3 +80,27 @@ def test_product_has_no_cpu_fallback():
                 text = open(os.path.join(dirpath, f)).read()
                 assert "import oracle" not in text and "from oracle" not in text, f
                 assert "qraf_oracle" not in text, f
+
+
+@pytest.mark.parametrize("lang,std", [("c", "c99"), ("c++", "c++17")])
+def test_header_is_plain_c_abi(lang, std, tmp_path):
+    """include/*.h compiles as C99 and as C++17, and a C program that calls an
+    entry point links against the library (plain pointers and sizes, extern "C")."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc" if lang == "c" else "g++")
+    if cc is None:
+        pytest.skip("no host compiler")
+    src = tmp_path / ("t.c" if lang == "c" else "t.cpp")
+    src.write_text('#include "qraf_cuda.h"\n#include <stdio.h>\n'
+                   'int main(void) { printf("%llu\\n", (unsigned long long)qraf_row_bytes(QRAF_DTYPE_Q4_0, 32, 4096));'
+                   ' return 0; }\n')
+    exe = tmp_path / "t"
+    libdir = os.path.dirname(qraf_b200.LIB_PATH)
+    out = subprocess.run([cc, f"-std={std}", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                          "-L", libdir, "-lqraf_cuda", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                         capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.strip() == "2304", (run.stdout, run.stderr)
