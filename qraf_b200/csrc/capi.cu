@@ -321,7 +321,7 @@ cudaError_t launch_rows(uint32_t dtype, const RowPlan& pl, bool exact, int MT, b
                                     : launch_rows_dt<kDtypeQ4>(pl, p, exact, MT, pdl, st);
 }
 
-int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out);
+int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what);
 
 // FAST row kernel, with the activation limbs built once by limb_prep_kernel (into
 // the stream's scratch) when every CTA would otherwise spend a large share of its
@@ -335,7 +335,7 @@ int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStre
     if (pl.p.nblk >= kPrepMinBlocks && pl.p.rows_base + (pl.p.rows_extra ? 1u : 0u) <= kPrepMaxRows) {
         const size_t bytes = static_cast<size_t>(pl.p.M) * pl.p.nblk * kLimbRec;
         uint8_t* recs = nullptr;
-        const int rc = tc_scratch(st, bytes, &recs);
+        const int rc = stream_scratch(st, bytes, &recs, "the FAST path's activation-limb prep (K >= 8192 with few rows per CTA)");
         if (rc) return rc;
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
@@ -453,14 +453,21 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     return true;
 }
 
+// A stream's scratch area is never freed before qraf_cuda_shutdown: CUDA graphs
+// captured from the stream (the host entry's own, or a caller's) hold its
+// address.  When a call needs more, a larger area (at least twice the old one,
+// so the areas kept add up to less than twice the largest) becomes the stream's
+// current one and the old area is kept, still valid for the graphs that use it.
 struct TcScratch {
     uint8_t* base = nullptr;
     size_t bytes = 0;
+    std::vector<uint8_t*> retired;   // earlier areas of this stream, freed at shutdown
 };
 std::mutex g_scratch_mutex;
 std::map<std::pair<int, cudaStream_t>, TcScratch> g_scratch;
 
-int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out) {
+// `what` names the path that needs the scratch, for the error message.
+int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what) {
     int dev = 0;
     QRAF_CUDA_TRY(cudaGetDevice(&dev));
     std::lock_guard<std::mutex> lk(g_scratch_mutex);
@@ -469,20 +476,18 @@ int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         QRAF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
         if (cs != cudaStreamCaptureStatusNone)
-            return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs %zu bytes of scratch on this stream; make a "
-                                              "first call of this size on the stream before capturing it", bytes);
-        if (s.base) {
-            QRAF_CUDA_TRY(cudaStreamSynchronize(st));
-            cudaFree(s.base);
-            s.base = nullptr;
-            s.bytes = 0;
-        }
-        if (cudaMalloc(&s.base, bytes) != cudaSuccess) {
+            return fail(QRAF_ERR_UNSUPPORTED, "%s needs %zu bytes of per-stream scratch (this stream has %zu); make a "
+                                              "first call of this shape on the stream before capturing it",
+                        what, bytes, s.bytes);
+        const size_t want = std::max(bytes, 2 * s.bytes);
+        uint8_t* fresh = nullptr;
+        if (cudaMalloc(&fresh, want) != cudaSuccess) {
             cudaGetLastError();
-            s.base = nullptr;
-            return fail(QRAF_ERR_NOMEM, "tensor-core scratch of %zu bytes could not be allocated", bytes);
+            return fail(QRAF_ERR_NOMEM, "%s: per-stream scratch of %zu bytes could not be allocated", what, want);
         }
-        s.bytes = bytes;
+        if (s.base) s.retired.push_back(s.base);
+        s.base = fresh;
+        s.bytes = want;
     }
     *out = s.base;
     return QRAF_OK;
@@ -490,14 +495,15 @@ int tc_scratch(cudaStream_t st, size_t bytes, uint8_t** out) {
 
 void tc_scratch_release() {
     std::lock_guard<std::mutex> lk(g_scratch_mutex);
+    int cur = 0;
+    cudaGetDevice(&cur);
     for (auto& kv : g_scratch) {
-        int cur = 0;
-        cudaGetDevice(&cur);
         cudaSetDevice(kv.first.first);
         cudaDeviceSynchronize();
         if (kv.second.base) cudaFree(kv.second.base);
-        cudaSetDevice(cur);
+        for (uint8_t* p : kv.second.retired) cudaFree(p);
     }
+    cudaSetDevice(cur);
     g_scratch.clear();
 }
 
@@ -505,7 +511,8 @@ void tc_scratch_release() {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 std::once_flag g_encode_once;
 
-bool weight_map(const qraf_weight_t& w, CUtensorMap* map) {
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType type, const void* base, const cuuint64_t (&dims)[2],
+                  cuuint64_t stride, const cuuint32_t (&box)[2], CUtensorMapSwizzle swizzle) {
     std::call_once(g_encode_once, [] {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -514,14 +521,17 @@ bool weight_map(const qraf_weight_t& w, CUtensorMap* map) {
             g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
     if (!g_encode_tiled) return false;
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t estr[2] = {1, 1};
+    return g_encode_tiled(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool weight_map(const qraf_weight_t& w, CUtensorMap* map) {
     // the weight as [rows][row_bytes / 4] 32-bit words; a box is 128 rows x 144 bytes
     const cuuint64_t dims[2] = {w.row_bytes / 4u, w.rows};
-    const cuuint64_t strides[1] = {w.row_bytes};
     const cuuint32_t box[2] = {kTcUnitBytes / 4u, kTcRows};
-    const cuuint32_t estr[2] = {1, 1};
-    return g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w.data), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, w.data, dims, w.row_bytes, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 template <uint32_t DT, uint32_t MV>
@@ -567,7 +577,7 @@ int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool
     if (!weight_map(w, &map)) return fail(QRAF_ERR_CUDA, "could not describe the weight to the TMA unit");
     uint8_t* base = scratch;
     if (!base) {
-        const int rc = tc_scratch(st, pl.bytes, &base);
+        const int rc = stream_scratch(st, pl.bytes, &base, "the tensor-core path");
         if (rc) return rc;
     } else if (scratch_cap < pl.bytes) {
         return fail(QRAF_ERR_INVALID, "this call needs %zu bytes of scratch, more than the %zu available", pl.bytes,
@@ -716,6 +726,12 @@ struct HostStaging {
     float* x_dev = nullptr;
     float* y_dev = nullptr;
     size_t x_cap = 0, y_cap = 0;   // in floats
+    // the device status word as the call's last kernel took it (pinned host
+    // memory; status_map: as a device pointer, or null when the device cannot
+    // map host memory, then status_dev is copied into it)
+    uint32_t* status_pinned = nullptr;
+    uint32_t* status_map = nullptr;
+    uint32_t* status_dev = nullptr;
 };
 
 std::mutex g_host_mutex;
@@ -747,6 +763,14 @@ void drop_graphs(int device) {
 
 int grow(HostStaging& s, size_t xn, size_t yn, int device) {
     if (!s.stream) QRAF_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    if (!s.status_pinned) {
+        if (cudaMallocHost(&s.status_pinned, sizeof(uint32_t)) != cudaSuccess ||
+            cudaMalloc(&s.status_dev, sizeof(uint32_t)) != cudaSuccess)
+            return fail(QRAF_ERR_NOMEM, "status word allocation failed");
+        if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&s.status_map), s.status_pinned, 0) != cudaSuccess)
+            s.status_map = nullptr;
+        cudaGetLastError();
+    }
     if (xn > s.x_cap || yn > s.y_cap) drop_graphs(device);   // they hold the old buffers
     if (xn > s.x_cap) {
         if (s.x_pinned) cudaFreeHost(s.x_pinned);
@@ -1269,8 +1293,9 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
         cfg.gridDim = dim3(static_cast<unsigned>(std::min<size_t>((n4 + 255) / 256, 4u * dinfo->sm_count)));
         cfg.blockDim = dim3(256);
         cfg.stream = s.stream;
-        QRAF_CUDA_TRY(from_host ? cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n)
-                                : cudaLaunchKernelEx(&cfg, host_copy_kernel<false>, src, dst, n));
+        uint32_t* status = from_host ? nullptr : s.status_map;
+        QRAF_CUDA_TRY(from_host ? cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n, status)
+                                : cudaLaunchKernelEx(&cfg, host_copy_kernel<false>, src, dst, n, status));
         return QRAF_OK;
     };
     auto enqueue = [&]() -> int {
@@ -1281,11 +1306,18 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
         const int mv_mode = (in_dim && s.x_map) ? (mode | QRAF_MODE_FLAG_OVERLAP) : mode;
         r = matvec_impl(&it->second, s.x_dev, s.y_dev, M, mv_mode, s.stream);
         if (r) return r;
-        if (s.y_map) return sm_copy(false, s.y_dev, s.y_map, yn);
+        if (s.y_map && s.status_map) return sm_copy(false, s.y_dev, s.y_map, yn);
+        // no mapped host memory: the status word through a one-thread copy kernel, then copy engines
+        QRAF_CUDA_TRY(cudaLaunchKernelEx(&(const cudaLaunchConfig_t&)cudaLaunchConfig_t{dim3(1), dim3(1), 0, s.stream,
+                                                                                        nullptr, 0},
+                                         host_copy_kernel<false>, s.y_dev, s.y_dev, size_t{0}, s.status_dev));
+        QRAF_CUDA_TRY(cudaMemcpyAsync(s.status_pinned, s.status_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                      s.stream));
         QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
         return QRAF_OK;
     };
     if (in_dim) std::memcpy(s.x_pinned, x_host, x_bytes);
+    *reinterpret_cast<volatile uint32_t*>(s.status_pinned) = 0u;
     const GraphKey gk{key, M, mode};
     auto g = g_graphs.find(gk);
     if (g != g_graphs.end() && g->second) {
@@ -1296,6 +1328,14 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     }
     QRAF_CUDA_TRY(cudaStreamSynchronize(s.stream));
     std::memcpy(y_host, s.y_pinned, yn * sizeof(float));
+    // the device status word as the copy of y took it: an expired bounded wait in
+    // the call's kernels means y is not complete
+    const uint32_t status = *reinterpret_cast<volatile uint32_t*>(s.status_pinned);
+    if (status & kErrWaitTimeout)
+        return fail(QRAF_ERR_TIMEOUT, "a device-side wait expired during this call (status 0x%x); y is incomplete",
+                    status);
+    if (status & kErrBadLaunch)
+        return fail(QRAF_ERR_INVALID, "a kernel rejected its launch shape during this call (status 0x%x)", status);
     if (g == g_graphs.end()) {
         // capture the same work for the next calls with this weight, M and mode
         cudaGraph_t graph = nullptr;
@@ -1342,6 +1382,8 @@ int qraf_cuda_shutdown(void) {
         if (s.y_pinned) cudaFreeHost(s.y_pinned);
         if (s.x_dev) cudaFree(s.x_dev);
         if (s.y_dev) cudaFree(s.y_dev);
+        if (s.status_pinned) cudaFreeHost(s.status_pinned);
+        if (s.status_dev) cudaFree(s.status_dev);
         if (s.stream) cudaStreamDestroy(s.stream);
         s = HostStaging();
     }

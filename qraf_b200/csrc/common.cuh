@@ -100,6 +100,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// L2 policy for data many CTAs read (activations).
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // L2 policy for data read exactly once (streamed weights).
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
@@ -121,11 +128,18 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 // The device-to-host copy is itself launched as a programmatic dependent of the
 // matvec before it (so it waits here, before reading src); a wait without such
 // a launch returns at once.
+// With `status_out` set (device-to-host only), one thread also takes the
+// device's status word (reading and clearing it) and stores it there, so that
+// the host learns of an expired wait in the kernels before it, with no extra
+// copy.
 template <bool FROM_HOST>
 __global__ void __launch_bounds__(256) host_copy_kernel(const float* __restrict__ src, float* __restrict__ dst,
-                                                        size_t n) {
+                                                        size_t n, uint32_t* status_out) {
     pdl_launch_dependents();
-    if constexpr (!FROM_HOST) pdl_wait();
+    if constexpr (!FROM_HOST) {
+        pdl_wait();
+        if (status_out && blockIdx.x == 0 && threadIdx.x == 0) __stwt(status_out, atomicExch(&g_status, 0u));
+    }
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t n4 = n >> 2;   // src and dst are 16-byte aligned

@@ -256,6 +256,72 @@ def test_host_entry_repeated_calls(cuda, oracle_lib):
     assert qb.device_status() == qb.OK
 
 
+def _host_check(oracle_lib, dt, q, n, k, x, y, mode, label):
+    m = x.shape[0]
+    y_ref = np.stack([oracle_lib.matvec(dt, q, n, k, x[j]) for j in range(m)])
+    if mode == qb.MODE_EXACT:
+        assert y.tobytes() == y_ref.tobytes(), label
+    else:
+        y64 = np.stack([oracle_lib.matvec_f64(dt, q, n, k, x[j]) for j in range(m)])
+        assert_fast_ok(y, y_ref, y64, label)
+
+
+def test_host_entry_shapes_that_grow_the_scratch(cuda, oracle_lib):
+    """The host entry replays a cached CUDA graph per (weight, M, mode), and those
+    graphs hold the stream's scratch address.  A later call that needs more scratch
+    must not free memory an earlier graph still writes: the 70B sequence QKV
+    (10240 x 8192, activation limbs in scratch) -> down (8192 x 28672, more
+    scratch) -> QKV again, then on the tensor cores M = 16 on a small weight ->
+    M = 64 on a large one -> M = 16 on the small one again; every call against the
+    oracle, twice per step so that the second call of a step replays its graph."""
+    seq = [("qkv", qb.Q4_0, 10240, 8192, 1, qb.MODE_FAST), ("down", qb.Q4_0, 8192, 28672, 1, qb.MODE_FAST),
+           ("qkv", qb.Q4_0, 10240, 8192, 1, qb.MODE_FAST),
+           ("small", qb.Q8_0, 640, 2048, 16, qb.MODE_TC), ("large", qb.Q4_0, 4096, 8192, 64, qb.MODE_TC),
+           ("small", qb.Q8_0, 640, 2048, 16, qb.MODE_TC)]
+    weights = {}
+    for step, (name, dt, n, k, m, mode) in enumerate(seq):
+        if name not in weights:
+            w = qb.fill_normal(42, 0.0, 0.02, n * k).reshape(n, k)
+            weights[name] = oracle_lib.quantize_rows(dt, w).reshape(-1)
+        q = weights[name]
+        for call in range(2):
+            x = qb.fill_normal(100 + 10 * step + call, 0.0, 1.0, m * k).reshape(m, k)
+            y = np.zeros((m, n), np.float32)
+            qb.dispatch_matvec_q(q, q.size, dt, 32, n, k, x, y, m=m, mode=mode)
+            _host_check(oracle_lib, dt, q, n, k, x, y, mode, f"step {step} ({name}) call {call}")
+    qb.host_cache_clear()
+    assert qb.device_status() == qb.OK
+
+
+def test_host_entry_reports_an_expired_device_wait(cuda, oracle_lib):
+    """The host entry reads the device's status word with the copy of y: a bounded
+    wait that ran out on the device (here: a 2-rank fused all-gather with no second
+    rank, a flag nothing sets) comes back as QRAF_ERR_TIMEOUT from the next host
+    call instead of a silently incomplete y; the word is taken, so the call after
+    that is clean again."""
+    import torch
+
+    n, k = 256, 1024
+    qd = torch.from_numpy(oracle_lib.quantize_rows(qb.Q8_0, qb.fill_normal(7, 0.0, 0.02, n * k).reshape(n, k)))
+    full = qb.Weight.from_device(qd.to(cuda).reshape(-1), qb.Q8_0, n, k)
+    c0, c1 = qb.Comm(2, 0, n), qb.Comm(2, 1, n)
+    qb.Comm.open_local([c0, c1])
+    c0.matvec_q(full.shard(2, 0), n, 0, torch.ones(k, device=cuda), mode=qb.MODE_EXACT)
+    torch.cuda.synchronize()
+    q = qd.numpy().reshape(-1)
+    x = qb.fill_normal(8, 0.0, 1.0, k).reshape(1, k)
+    y = np.zeros((1, n), np.float32)
+    with pytest.raises(qb.QrafError) as e:
+        qb.dispatch_matvec_q(q, q.size, qb.Q8_0, 32, n, k, x, y, m=1, mode=qb.MODE_EXACT)
+    assert e.value.code == qb.ERR_TIMEOUT
+    qb.dispatch_matvec_q(q, q.size, qb.Q8_0, 32, n, k, x, y, m=1, mode=qb.MODE_EXACT)
+    _host_check(oracle_lib, qb.Q8_0, q, n, k, x, y, qb.MODE_EXACT, "after the reported timeout")
+    assert qb.device_status() == qb.OK
+    qb.host_cache_clear()
+    c0.destroy()
+    c1.destroy()
+
+
 # ── full-size configurations (BASELINE.json configs 1-5) ──────────────────
 _W_CACHE = {}
 _Q_HOST = {}
