@@ -1,27 +1,32 @@
 #!/usr/bin/env python
 """bench.py — QRAF's quantized matvec on B200 (BASELINE.json metric: "Q8/Q4 matvec HBM GB/s").
 
-Default workload: BASELINE.json configs[1], the Q4_0 4096x4096 batch-1 matvec.
-Weight W ~ N(0, 0.02) from std::mt19937(42) (the reference's seeding idiom),
-quantized on the GPU by the byte-exact Q4_0 quantizer; activation x ~ N(0, 1)
-from std::mt19937(43).
+Default workload on one GPU: BASELINE.json configs[1], the Q4_0 4096x4096
+batch-1 matvec.  Weight W ~ N(0, 0.02) from std::mt19937(42) (the reference's
+seeding idiom), quantized on the GPU by the byte-exact Q4_0 quantizer;
+activation x ~ N(0, 1) from std::mt19937(43).
 
 A STEP is one pass over a pool of R distinct copies of the quantized weight
 (R = ceil(4 x L2 / weight bytes)), one matvec launch per copy: every launch
 reads its weight cold from HBM (inputs larger than L2, so no flush is needed).
-The step is captured once as a CUDA graph and replayed.  value = algorithmic
-bytes (N*K/32*block_bytes + 4K + 4N per matvec) of every launch of every rank
-/ max-over-ranks device time of the K timed steps.
+The step is captured once as a CUDA graph and replayed; consecutive launches
+overlap their ramps (programmatic dependent launch), as a decode chain of
+matvecs runs.  value = algorithmic bytes (N*K/32*block_bytes + 4K + 4N per
+matvec) of every launch of every rank / max-over-ranks device time of the K
+timed steps; roofline.achieved is the same bytes per launch over the average
+launch duration in that timed region.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>]|<model>_token[_m<M>]]
+                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>][_shard]|<model>_token[_m<M>]]
                   [--mode fast|exact|tc|auto]
 
-With --gpus N > 1 (launched by torch.distributed.run) every rank runs the same
-workload on its own weights (independent matvec objects, no data-path
-collective): "scaling": "weak".  --impl reference times the reference's own
-CPU code (oracle/_ref: dispatch_matvec_q's per-row dot, fanned out over all host
-threads) on the same workload; under torchrun only rank 0 runs it.
+Under torch.distributed.run (WORLD_SIZE > 1) the default workload is the
+row-sharded 70B gate/up projection (q4_28672x8192_shard
+configs[4]): one weight split by output rows over the ranks, every call
+all-gathering its rows inside the kernel (NVLink peer stores): "scaling":
+"strong".  --impl reference times the reference's own CPU code (oracle/_ref:
+dispatch_matvec_q's per-row dot, fanned out over all host threads) on the same
+workload; under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -40,6 +45,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 Q8, Q4 = 10, 20
+DEFAULT_WORKLOAD = "q4_4096x4096"
+DEFAULT_SHARDED = "q4_28672x8192_shard"    # the 70B gate/up projection, row-sharded
 BLOCK_BYTES = {Q8: 36, Q4: 18}
 METRIC = "Q8/Q4 matvec HBM GB/s"
 
@@ -52,6 +59,14 @@ def parse_workload(name: str):
     n, k = (int(v) for v in parts[1].split("x"))
     m = int(parts[2][1:]) if len(parts) > 2 and parts[2].startswith("m") else 1
     return dt, n, k, m
+
+
+def resolve_workload(name, world: int) -> str:
+    """The workload a run without --workload measures: configs[1] on one GPU, the
+    row-sharded 70B gate/up projection across torchrun ranks."""
+    if name:
+        return name
+    return DEFAULT_SHARDED if world > 1 else DEFAULT_WORKLOAD
 
 
 def is_shard_workload(name: str) -> bool:
@@ -197,17 +212,33 @@ def cpu_reference(dt, n, k, m, q_host, x_host, threads, budget_s, max_ops=None):
     return ops, el, kind
 
 
+def base_config(args, dt, n, k, m):
+    """The workload's identity, the same in both arms' JSON lines."""
+    return {"workload": args.workload, "N": n, "K": k, "M": m, "block": 32,
+            "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode}
+
+
+def host_normal(seed, std, n):
+    """Seeded synthetic values with the reference's idiom (std::mt19937(seed),
+    std::normal_distribution<float>), drawn by the reference library built in
+    oracle/_ref (so the reference arm loads nothing of the product)."""
+    import oracle
+
+    if oracle.reference_available():
+        return oracle.Reference().fill_normal(seed, 0.0, std, n)
+    return np.random.default_rng(seed).normal(0.0, std, n).astype(np.float32)
+
+
 def run_reference_arm(args, dt, n, k, m):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import qraf_b200 as qb
-
-    w = qb.fill_normal(42, 0.0, 0.02, n * k).reshape(n, k)
     import oracle
 
+    w = host_normal(42, 0.02, n * k).reshape(n, k)
     q_host = (oracle.Reference() if oracle.reference_available() else oracle.Oracle()).quantize(dt, w.ravel(), 32)
-    x_host = qb.fill_normal(43, 0.0, 1.0, m * k).reshape(m, k)
+    del w
+    x_host = host_normal(43, 1.0, m * k).reshape(m, k)
     threads = os.cpu_count() or 1
     # Each step is one full matvec of the workload; warm-up is bounded to keep the run short.
     for _ in range(min(args.warmup, 3)):
@@ -219,8 +250,8 @@ def run_reference_arm(args, dt, n, k, m):
               f"(the reference's own row fan-out, backend.cpp:145-151)")
     line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
             "steps": ops, "warmup": args.warmup, "ms_per_step": el / ops * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "N": n, "K": k, "M": m},
+            "scaling": "strong" if is_shard_workload(args.workload) else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": base_config(args, dt, n, k, m),
             "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -255,7 +286,8 @@ def run_ours(args, dt, n, k, m):
     q = qb.quantize_rows(dt, wf, 32).reshape(-1)
     del wf
     wbytes = q.numel()
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    props = torch.cuda.get_device_properties(dev)
+    l2 = props.L2_cache_size
     free, _ = torch.cuda.mem_get_info(dev)
     R = max(2, math.ceil(4 * l2 / wbytes))
     R = max(2, min(R, int(0.5 * free // wbytes)))
@@ -328,7 +360,9 @@ def run_ours(args, dt, n, k, m):
     per_launch = alg_bytes(dt, n, k, m)
     value = world * args.steps * R * per_launch / (elapsed_ms / 1e3) / 1e9
     peak, peak_src = measured_peaks()
-    achieved = per_launch / (kern_ms / 1e3) / 1e9
+    launch_ms = elapsed_ms / (args.steps * R)              # average launch duration in the timed region
+    achieved = per_launch / (launch_ms / 1e3) / 1e9
+    achieved_alone = per_launch / (kern_ms / 1e3) / 1e9
     status = qb.device_status()
 
     # e2e: the reference-facing host entry (host x in, host y out, synchronous), same pool.
@@ -371,24 +405,28 @@ def run_ours(args, dt, n, k, m):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "N": n, "K": k, "M": m, "block": 32,
-                       "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode,
-                       "parallelism": f"independent weights per rank x{world}" if world > 1 else "single GPU",
-                       "pool_copies": R, "pool_bytes": R * wbytes, "l2_bytes": l2,
-                       "l2_policy": "inputs larger than L2: rotating pool of weight copies >= 4x L2",
-                       "step": f"{R} matvec launches, one per L2-cold weight copy (CUDA graph replay)",
-                       "launch_overlap": "programmatic dependent launch (weights prefetched before the previous "
-                                         "launch ends)" if args.overlap else "none",
-                       "weights": "N(0,0.02) std::mt19937(42), quantized on GPU (byte-exact Q*_0)",
-                       "payload_sha_matches_reference": payload_ok, "arith": "fp32 accumulate"},
+            "config": base_config(args, dt, n, k, m),
+            "setup": {"parallelism": f"independent weights per rank x{world}" if world > 1 else "single GPU",
+                      "pool_copies": R, "pool_bytes": R * wbytes, "l2_bytes": l2,
+                      "l2_policy": "inputs larger than L2: rotating pool of weight copies >= 4x L2",
+                      "step": f"{R} matvec launches, one per L2-cold weight copy (CUDA graph replay)",
+                      "launch_overlap": "programmatic dependent launch (weights prefetched before the previous "
+                                        "launch ends)" if args.overlap else "none",
+                      "weights": "N(0,0.02) std::mt19937(42), quantized on GPU (byte-exact Q*_0)",
+                      "payload_sha_matches_reference": payload_ok, "arith": "exact int32 block sums, fp32 accumulate"},
             "e2e": e2e,
-            "gpu_launches": args.steps * R,
+            "gpu_launches": args.steps * R * launches_per_call(n, k, props.multi_processor_count)
+            if kernel == "qmv_rows_kernel" and m <= 2 and args.mode != "exact" else args.steps * R,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(kernel, dt, n, k, m),
                          "peak_source": peak_src, "kernel": kernel,
-                         "kernel_us": kern_ms * 1e3,
-                         "kernel_timing": "average launch duration of back-to-back launches without overlap "
-                                          "(CUDA events around a graph of launches, inter-launch gaps included)",
+                         "kernel_us": launch_ms * 1e3,
+                         "kernel_timing": "average launch duration in the timed region (CUDA events on the "
+                                          "launching stream around the K steps of overlapping launches)",
+                         "kernel_us_alone": kern_ms * 1e3, "achieved_alone": achieved_alone,
+                         "frac_alone": achieved_alone / peak,
+                         "alone_timing": "the same launches strictly one after another, without overlap (CUDA "
+                                         "events around a graph of them, inter-launch gaps included)",
                          "alg_bytes_per_launch": per_launch},
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
@@ -477,9 +515,7 @@ def _sample_rows_timer(spec, threads, budget_s, quantized_rows):
 
 
 def qb_fill(seed, n):
-    import qraf_b200 as qb
-
-    return qb.fill_normal(seed, 0.0, 1.0, n)
+    return host_normal(seed, 1.0, n)
 
 
 def run_shard(args, dt, n, k, m):
@@ -536,6 +572,14 @@ def run_shard(args, dt, n, k, m):
     pool[:] = q
     weights = [qb.Weight.from_device(pool[i], dt, rows, k) for i in range(R)]
     x = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * k)).to(dev).reshape(m, k)
+
+    # The same projection unsharded on rank 0's GPU alone (the 1-GPU point of this
+    # strong-scaling line; the other ranks wait at the barrier).
+    one_gpu = None
+    if world > 1 and not args.no_1gpu_ref:
+        if rank == 0:
+            one_gpu = _unsharded_figure(args, dt, n, k, m, mode, dev)
+        dist.barrier()
 
     comm = None
     ys = [torch.empty((m, n), device=dev) for _ in range(R)] if world == 1 else None
@@ -640,15 +684,16 @@ def run_shard(args, dt, n, k, m):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "N": n, "K": k, "M": m, "block": 32,
-                       "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode,
-                       "parallelism": (f"rows split over {world} GPUs ({rows} per GPU), all-gather "
-                                       f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
-                       if world > 1 else "single GPU (unsharded kernel)",
-                       "pool_copies": R, "l2_policy": "inputs larger than L2: rotating pool of shard copies",
-                       "step": f"{R} calls (CUDA graph replay, overlapping launches)",
-                       "us_per_call_pipelined": elapsed_ms * 1e3 / calls,
-                       "us_per_call_alone": call_ms * 1e3},
+            "config": base_config(args, dt, n, k, m),
+            "setup": {"parallelism": (f"rows split over {world} GPUs ({rows} per GPU), all-gather "
+                                      f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
+                      if world > 1 else "single GPU (unsharded kernel)",
+                      "comm_ranks": world,
+                      "pool_copies": R, "l2_policy": "inputs larger than L2: rotating pool of shard copies",
+                      "step": f"{R} calls (CUDA graph replay, overlapping launches)",
+                      "us_per_call_pipelined": elapsed_ms * 1e3 / calls,
+                      "us_per_call_alone": call_ms * 1e3,
+                      "same_workload_1gpu": one_gpu},
             "e2e": {"value": e2e_steps * R * full / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": m * k * 4,
                     "d2h_bytes_per_step": m * n * 4, "steps": e2e_steps,
                     "path": "H2D x from pinned memory, the step's graph, D2H of the last call's y, stream sync"},
@@ -669,6 +714,54 @@ def run_shard(args, dt, n, k, m):
         comm.destroy()
     if dist:
         dist.destroy_process_group()
+
+
+def _unsharded_figure(args, dt, n, k, m, mode, dev):
+    """Pipelined and single-call time of the whole projection on this GPU alone:
+    a pool of full-weight copies (>= 4 x L2), one CUDA graph of overlapping calls."""
+    import torch
+
+    import qraf_b200 as qb
+
+    gen = torch.Generator(device=dev)
+    wf = torch.empty((n, k), device=dev)
+    for c0 in range(0, n, 1024):
+        gen.manual_seed(42 * 1_000_003 + c0 // 1024)
+        wf[c0:c0 + 1024] = torch.randn((min(1024, n - c0), k), generator=gen, device=dev) * 0.02
+    q = qb.quantize_rows(dt, wf, 32).reshape(-1)
+    del wf
+    wb = q.numel()
+    R = max(2, math.ceil(4 * torch.cuda.get_device_properties(dev).L2_cache_size / wb))
+    pool = torch.empty((R, wb), dtype=torch.uint8, device=dev)
+    pool[:] = q
+    ws = [qb.Weight.from_device(pool[i], dt, n, k) for i in range(R)]
+    x = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * k)).to(dev).reshape(m, k)
+    ys = torch.empty((R, m, n), device=dev)
+    s = torch.cuda.Stream(dev)
+    ov = qb.MODE_FLAG_OVERLAP if args.overlap else 0
+    with torch.cuda.stream(s):
+        for i in range(R):
+            qb.matvec_q(ws[i], x, ys[i], mode=mode | ov)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(R):
+            qb.matvec_q(ws[i], x, ys[i], mode=mode | ov)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, min(20, args.steps))
+    with torch.cuda.stream(s):
+        t0.record()
+        for _ in range(reps):
+            g.replay()
+        t1.record()
+    torch.cuda.synchronize(dev)
+    us = t0.elapsed_time(t1) * 1e3 / (reps * R)
+    del g
+    return {"value": alg_bytes(dt, n, k, m) / (us * 1e-6) / 1e9, "unit": "GB/s", "us_per_call_pipelined": us,
+            "what": "the same projection unsharded on one GPU of this box (rank 0 alone), same pool and graph method"}
 
 
 def run_token(args, model, m):
@@ -929,7 +1022,11 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="q4_4096x4096")
+    ap.add_argument("--workload", default=None,
+                    help="default: q4_4096x4096 on one GPU; q4_28672x8192_shard (the 70B gate/up projection split "
+                         "over the ranks) under torch.distributed.run")
+    ap.add_argument("--no-1gpu-ref", dest="no_1gpu_ref", action="store_true",
+                    help="sharded workloads on N > 1 GPUs: skip the unsharded one-GPU figure of the same projection")
     ap.add_argument("--mode", choices=["fast", "exact", "tc", "auto"], default="fast")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
@@ -937,6 +1034,7 @@ def main():
     ap.add_argument("--allgather", choices=["fused", "nccl"], default="fused",
                     help="token workloads on N > 1 GPUs: all-gather fused into the kernel, or NCCL after it")
     args = ap.parse_args()
+    args.workload = resolve_workload(args.workload, int(os.environ.get("WORLD_SIZE", "1")))
     tok = parse_token_workload(args.workload)
     if tok:
         (run_token_reference if args.impl == "reference" else run_token)(args, *tok)

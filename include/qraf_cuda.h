@@ -46,13 +46,21 @@ extern "C" {
 
 /* ── arithmetic modes ───────────────────────────────────────────────────── */
 #define QRAF_MODE_EXACT 0  /* bit-identical to the reference's Linux scalar path */
-#define QRAF_MODE_FAST  1  /* fused multiply-add, reordered sums; allclose(rtol 1e-5, atol 1e-6) */
+#define QRAF_MODE_FAST  1  /* exact per-block integer sums (activations as 8-bit limbs),
+                              reordered fp32 sums; allclose(rtol 1e-5, atol 1e-6) */
 #define QRAF_MODE_TC    2  /* tcgen05 tensor-core tile (exact per-block integer sums, fp32
                               epilogue); same tolerance as FAST.  Needs block size 32,
                               K % 128 == 0 (Q8_0) or K % 256 == 0 (Q4_0) and 16-byte-aligned
-                              weights.  Uses per-stream scratch memory that the library
-                              allocates at a stream's first call of a given size (make that
-                              call before capturing the stream in a CUDA graph). */
+                              weights. */
+/* Per-stream scratch.  QRAF_MODE_TC, and QRAF_MODE_FAST (also the sharded FAST
+ * path) when a row has at least 256 blocks (K >= 8192) and a CTA gets at most 96
+ * rows (long-K projections, row shards), use scratch memory that the library
+ * allocates per (device, stream) at the stream's first call that needs that much.
+ * Make one call of each such shape on a stream before capturing the stream in a
+ * CUDA graph: a capture that would need more scratch fails with
+ * QRAF_ERR_UNSUPPORTED.  Scratch areas are never freed before qraf_cuda_shutdown
+ * (graphs hold their addresses); a graph captured on a stream uses that stream's
+ * scratch, so it must not run concurrently with other work of that stream. */
 #define QRAF_MODE_AUTO  3  /* FAST for M <= 2, TC from M = 3 where the weight allows (else FAST) */
 /* Or-able flag: the kernel may start while the previous kernel in the stream is
  * still running and fetch the weight before waiting for it (programmatic
@@ -139,8 +147,9 @@ int qraf_cuda_dot_q(uint32_t dtype, const void* q_dev, const float* x_dev, uint6
  * checks against a CPU restatement (verification entry; no counterpart in the
  * reference, whose path has no integer sums).  For one vector x and every (row
  * n, block b): d_dev[n][b][j] = sum_i q_i * L_j,i (int32, j = 0..3; codes with
- * their bias removed; L_j the signed 7-bit digits of X_i = rint(x_i 2^(27-e_b)))
- * and c_dev[b] = 2^(e_b - 27), exactly as the FAST kernels form them.  Block
+ * their bias removed; L_j the balanced signed 8-bit digits, most significant
+ * first, of X_i = rint(x_i 2^(30-e_b)), max |x| (1 + 2^-8) < 2^e_b over the block)
+ * and c_dev[b] = 2^(e_b - 30), exactly as the FAST kernels form them.  Block
  * size 32, K % 32 == 0, 4-byte-aligned rows, K up to the shared memory (176 B per
  * block). */
 int qraf_cuda_limb_partials(const qraf_weight_t* w, const float* x_dev, int32_t* d_dev, float* c_dev, void* stream);
@@ -166,12 +175,16 @@ int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint
 /* ── row-sharded matvec over several GPUs (one process per GPU) ─────────── */
 /* A weight too large for one GPU's bandwidth budget is partitioned by output
  * rows (qraf_cuda_weight_shard); each rank computes its rows and the kernel
- * itself stores every output element into every rank's full-length y buffer
- * over NVLink (CUDA IPC peer mappings, plain stores), then signals the peers and
- * waits (bounded) for them: the all-gather is fused into the matvec.  The
- * library does no networking: the caller exchanges the opaque handles (e.g.
- * with torch.distributed or MPI).  Waits that run out set the device status
- * (qraf_cuda_device_status returns QRAF_ERR_TIMEOUT). */
+ * itself stores every output element into this rank's y and, as one 8-byte
+ * word (call number << 32 | value bits), into every peer's receive array over
+ * NVLink (CUDA IPC peer mappings, plain stores, no fence and no flag: an
+ * aligned 8-byte store is seen whole or not at all).  Before it ends, the
+ * kernel copies the other ranks' rows from its own receive array into y,
+ * polling each word (bounded) until it carries this call's number: the
+ * all-gather is fused into the matvec.  The library does no networking: the
+ * caller exchanges the opaque handles (e.g. with torch.distributed or MPI).
+ * Waits that run out set the device status (qraf_cuda_device_status returns
+ * QRAF_ERR_TIMEOUT). */
 #define QRAF_COMM_HANDLE_BYTES 512
 #define QRAF_COMM_BUFFERS 4
 #define QRAF_COMM_MAX_WORLD 8

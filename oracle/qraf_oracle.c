@@ -329,9 +329,11 @@ void qo_matvec_q_f64(const void* w, uint32_t dtype, int bs, uint32_t N, uint32_t
 
 /* Integer limb partials (the FAST kernels' integer path; see qraf_oracle.h).
  * Not a restatement of reference code: the reference has no integer path.  The
- * dot it reconstructs, sum_b scale_b * c_b * sum_j 2^(7(3-j)) D_j, approximates
- * dot_q*_0_f32 (quantize.cpp:187-239) with X_i carrying 27 bits of each block's
- * scale. */
+ * dot it reconstructs, sum_b scale_b * c_b * sum_j 2^(8(3-j)) D_j, approximates
+ * dot_q*_0_f32 (quantize.cpp:187-239) with X_i carrying 30 bits of each block's
+ * range.  Per block: t = fl(max|x| * (1 + 2^-8)), e with t < 2^e (frexpf; 128 when
+ * t overflows), c = 2^(e-30), X_i = rint(x_i 2^(30-e)) (half to even), and the
+ * balanced base-256 digits of X_i, -128 <= L_j <= 127, most significant first. */
 void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, const float* x, int32_t* D,
                       float* c) {
     const size_t nb = (size_t)K / 32;
@@ -349,17 +351,21 @@ void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, con
         }
         int e = 0;
         int live = amax > 0.0f && !bad;
-        if (live) frexpf(amax, &e);   /* amax = m * 2^e, m in [0.5, 1) */
-        c[b] = bad ? NAN : (live ? ldexpf(1.0f, e - 27) : 0.0f);
+        if (live) {
+            const float t = amax * 1.00390625f;
+            if (isinf(t)) e = 128;
+            else frexpf(t, &e);   /* t = m * 2^e, m in [0.5, 1) */
+        }
+        c[b] = bad ? NAN : (live ? ldexpf(1.0f, e - 30) : 0.0f);
         for (int i = 0; i < 32; i++) {
-            long X = live ? lrintf(ldexpf(xb[i], 27 - e)) : 0;   /* exact scaling, round half to even */
-            unsigned long ua = (unsigned long)(X < 0 ? -X : X);
-            int sg = X < 0 ? -1 : 1;
+            long X = live ? lrintf(ldexpf(xb[i], 30 - e)) : 0;   /* exact scaling, round half to even */
             int32_t* l = L + (b * 32 + (size_t)i) * 4;
-            l[0] = sg * (int)(ua >> 21);
-            l[1] = sg * (int)((ua >> 14) & 127u);
-            l[2] = sg * (int)((ua >> 7) & 127u);
-            l[3] = sg * (int)(ua & 127u);
+            for (int j = 3; j >= 0; j--) {   /* balanced digits, least significant first */
+                long d = X & 0xFF;
+                if (d >= 128) d -= 256;
+                l[j] = (int32_t)d;
+                X = (X - d) / 256;
+            }
         }
     }
     for (uint32_t r = 0; r < N; r++) {

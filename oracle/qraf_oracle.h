@@ -78,12 +78,12 @@ void qo_matvec_q_f64(const void* w, uint32_t dtype, int block_size, uint32_t N, 
 
 /* Per-block integer partial sums of the batch-1 FAST arithmetic (a restatement
  * of the GPU kernels' integer path, for bit-exact checks; block size 32, K a
- * multiple of 32).  For every 32-element block b of x: e_b with max|x| in
- * [2^(e_b-1), 2^e_b); X_i = rint(x_i * 2^(27 - e_b)) (round half to even);
- * X_i = L0*2^21 + L1*2^14 + L2*2^7 + L3 with |L_j| <= 127, every digit with the
- * sign of X_i; D[n][b][j] = sum_i q_i * L_j,i with the true codes q (Q8: int8,
- * Q4: nibble - 8); c[b] = 2^(e_b - 27) (0 for an all-zero block).  A block that
- * holds a NaN or an infinity gets zero digits and c = NaN. */
+ * multiple of 32).  For every 32-element block b of x: t = fl(max|x| * (1 + 2^-8))
+ * and e_b with t < 2^e_b (t in [2^(e_b-1), 2^e_b)); X_i = rint(x_i * 2^(30 - e_b))
+ * (round half to even); X_i = L0*2^24 + L1*2^16 + L2*2^8 + L3 with balanced
+ * digits -128 <= L_j <= 127; D[n][b][j] = sum_i q_i * L_j,i with the true codes q
+ * (Q8: int8, Q4: nibble - 8); c[b] = 2^(e_b - 30) (0 for an all-zero block).  A
+ * block that holds a NaN or an infinity gets zero digits and c = NaN. */
 void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, const float* x, int32_t* D,
                       float* c);
 

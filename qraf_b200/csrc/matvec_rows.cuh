@@ -178,15 +178,20 @@ __device__ __forceinline__ void lds_x_block(const float* xs, uint32_t b, float4 
 }
 
 // ── FAST: activations as integer limbs, codes used as they are ───────────
-// Per 32-element block b of an activation vector, with e_b the exponent of
-// max |x| (max |x| < 2^e_b):  X_i = rint(x_i * 2^(27 - e_b)), |X_i| < 2^27, and
-// X_i = L0*2^21 + L1*2^14 + L2*2^7 + L3 with signed digits |L_j| <= 127.
-// Then sum_i q_i x_i ~= 2^(e_b - 27) * sum_j 2^(7(3-j)) * D_j,  D_j = sum_i q_i L_ji,
+// Per 32-element block b of an activation vector, with e_b such that
+// max |x| (1 + 2^-8) < 2^e_b:  X_i = rint(x_i * 2^(30 - e_b)), |X_i| < 2^30, and
+// X_i = L0*2^24 + L1*2^16 + L2*2^8 + L3 with balanced signed digits -128 <= L_j <= 127.
+// Then sum_i q_i x_i ~= 2^(e_b - 30) * sum_j 2^(8(3-j)) * D_j,  D_j = sum_i q_i L_ji,
 // where every D_j is an exact int32 (dp4a), so the per-block partial sums are
-// integers independent of summation order; the only roundings are X_i (a
-// relative error below 2^-27 of the block maximum) and the fp32 combination.
+// integers independent of summation order; the only roundings are X_i (half a
+// unit of 2^(e_b - 30), i.e. 2^-31 of the block maximum) and the fp32 combination.
+// The digits are not extracted one by one: for |X| < 2^30 the bytes of
+// U = X + 0x80808080 are the digits plus 128 (the added 128s absorb every
+// borrow), so U ^ 0x80808080 holds the four signed digits, least significant in
+// byte 0, and a 4 x 4 byte transpose (PRMT) turns four elements' U into one word
+// per digit plane.
 // Record of one block in shared memory (kLimbRec bytes): limb plane j at
-// bytes [32j, 32j+32), c_b = 2^(e_b - 27) at 128, the plane sums S_j (int32) at
+// bytes [32j, 32j+32), c_b = 2^(e_b - 30) at 128, the plane sums S_j (int32) at
 // 144..159 (Q4 only), padding to an odd number of 16-byte units so that lanes
 // reading consecutive blocks hit distinct banks.
 // Q4 stores the elements of each group of 8 in the order 0,2,4,6,1,3,5,7 so
@@ -207,9 +212,9 @@ __device__ __forceinline__ void lds_limbs(const uint8_t* rec, LimbBlock& lb) {
     }
 }
 
-// sum_j 2^(7(3-j)) D_j as fp32 (D0*128 + D1 and D2*128 + D3 are exact int32).
+// sum_j 2^(8(3-j)) D_j as fp32 (|D_j| < 2^20, so D0*256 + D1 and D2*256 + D3 are exact int32).
 __device__ __forceinline__ float combine_limbs(int d0, int d1, int d2, int d3) {
-    return fmaf(__int2float_rn(d0 * 128 + d1), 16384.0f, __int2float_rn(d2 * 128 + d3));
+    return fmaf(__int2float_rn(d0 * 256 + d1), 65536.0f, __int2float_rn(d2 * 256 + d3));
 }
 
 // D_j = sum_i q_i L_j,i for one block: exact int32 dot products (dp4a).
@@ -282,40 +287,47 @@ __device__ __forceinline__ void limb_record_part(const float4 a, const float4 b,
         amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
         bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, o);
     }
-    // e with amax in [2^(e-1), 2^e); x * 2^(27-e) and 2^(e-27) built from exponent
-    // bits when both are normal floats, else by ldexpf.
-    const uint32_t ebits = (__float_as_uint(amax) >> 23) & 0xFFu;
+    // e with max |x| (1 + 2^-8) < 2^e, from the exponent bits of t = max |x| * (1 + 2^-8):
+    // t in [2^(tb-127), 2^(tb-126)), e = tb - 126.  2^(30-e) and 2^(e-30) come from
+    // exponent bits where both are normal floats; otherwise (blocks near the ends of
+    // the range) each x is scaled by ldexpf.
     const bool live = amax > 0.0f && !bad;
+    const float t = amax * 1.00390625f;
+    const uint32_t tb = __float_as_uint(t) >> 23;
     int e = 0;
     float up = 0.0f, cb = 0.0f;
     bool slow = false;
     if (live) {
-        if (ebits >= 29u) {
-            e = static_cast<int>(ebits) - 126;
-            up = __uint_as_float(static_cast<uint32_t>(127 + 27 - e) << 23);
-            cb = __uint_as_float(static_cast<uint32_t>(127 + e - 27) << 23);
+        if (tb >= 30u && tb <= 254u) {
+            up = __uint_as_float((283u - tb) << 23);   // 2^(30 - e)
+            cb = __uint_as_float((tb - 29u) << 23);    // 2^(e - 30)
         } else {
-            frexpf(amax, &e);
+            if (tb > 254u) e = 128;   // t overflowed: max |x| < 2^128
+            else frexpf(t, &e);       // t < 2^e
             slow = true;
-            cb = ldexpf(1.0f, e - 27);
+            cb = ldexpf(1.0f, e - 30);
         }
     }
-    uint32_t w[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
-    int S[4] = {0, 0, 0, 0};
+    // U = X + 0x80808080 per element, in record order (Q4: 0,2,4,6 then 1,3,5,7)
+    uint32_t u[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int X = live ? __float2int_rn(slow ? ldexpf(xv[i], 27 - e) : xv[i] * up) : 0;
-        const uint32_t ua = static_cast<uint32_t>(X < 0 ? -X : X);
-        const int sg = X < 0 ? -1 : 1;
-        const int L[4] = {sg * static_cast<int>(ua >> 21), sg * static_cast<int>((ua >> 14) & 127u),
-                          sg * static_cast<int>((ua >> 7) & 127u), sg * static_cast<int>(ua & 127u)};
-        // byte position of element i inside this thread's 8 bytes of each plane
-        const int pos = (DT == kDtypeQ4) ? ((i & 1) * 4 + (i >> 1)) : i;
+        const int src = (DT == kDtypeQ4) ? ((i & 3) * 2 + (i >> 2)) : i;
+        const int X = live ? __float2int_rn(slow ? ldexpf(xv[src], 30 - e) : xv[src] * up) : 0;
+        u[i] = static_cast<uint32_t>(X) + 0x80808080u;
+    }
+    uint32_t w[4][2];
+    int S[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            w[j][pos >> 2] |= (static_cast<uint32_t>(L[j]) & 0xFFu) << (8 * (pos & 3));
-            S[j] += L[j];
-        }
+    for (int h = 0; h < 2; ++h) {   // 4 x 4 byte transpose: byte k of element word i -> byte i of plane word 3-k
+        const uint32_t t0 = __byte_perm(u[4 * h + 0], u[4 * h + 1], 0x5140u), t1 = __byte_perm(u[4 * h + 0], u[4 * h + 1], 0x7362u);
+        const uint32_t t2 = __byte_perm(u[4 * h + 2], u[4 * h + 3], 0x5140u), t3 = __byte_perm(u[4 * h + 2], u[4 * h + 3], 0x7362u);
+        w[3][h] = __byte_perm(t0, t2, 0x5410u) ^ 0x80808080u;
+        w[2][h] = __byte_perm(t0, t2, 0x7632u) ^ 0x80808080u;
+        w[1][h] = __byte_perm(t1, t3, 0x5410u) ^ 0x80808080u;
+        w[0][h] = __byte_perm(t1, t3, 0x7632u) ^ 0x80808080u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) S[j] = __dp4a(static_cast<int>(w[j][h]), 0x01010101, S[j]);
     }
 #pragma unroll
     for (int o = 1; o <= 2; o <<= 1)

@@ -24,6 +24,9 @@ def test_workload_names():
     assert bench.parse_token_workload("llama70b_token") == ("llama70b", 1)
     assert bench.parse_token_workload("qwen3b_token_m16") == ("qwen3b", 16)
     assert bench.parse_token_workload("q4_4096x4096") is None
+    assert bench.resolve_workload(None, 1) == "q4_4096x4096"
+    assert bench.resolve_workload(None, 8) == "q4_28672x8192_shard"       # the sharded 70B projection
+    assert bench.resolve_workload("q8_4096x4096", 8) == "q8_4096x4096"
 
 
 def test_algorithmic_bytes_match_the_measurement_plan():
@@ -44,10 +47,14 @@ def test_launch_count_rule():
 
 
 def test_reference_arm_prints_the_contract_line():
+    """The reference arm's line has every contract key and the same config as our
+    arm, and the process never maps the product library (its inputs come from the
+    reference library's own std::mt19937 draws)."""
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
-    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
-                          "q8_256x512", "--steps", "2", "--warmup", "1"], capture_output=True, text=True, env=env,
-                         timeout=300, cwd=ROOT)
+    code = ("import sys, runpy; sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'q8_256x512', "
+            "'--steps', '2', '--warmup', '1']; runpy.run_path('bench.py', run_name='__main__'); "
+            "maps = open('/proc/self/maps').read(); print('PRODUCT_SO_MAPPED', 'libqraf_cuda' in maps)")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1, out.stdout
@@ -59,3 +66,6 @@ def test_reference_arm_prints_the_contract_line():
     assert d["value"] > 0 and d["higher_is_better"] is True
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"] == {"workload": "q8_256x512", "N": 256, "K": 512, "M": 1, "block": 32, "quant": "Q8_0",
+                           "mode": "fast"}
+    assert "PRODUCT_SO_MAPPED False" in out.stdout

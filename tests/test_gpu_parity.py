@@ -20,7 +20,6 @@ from conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 
 RTOL, ATOL = 1e-5, 1e-6
-FULL = os.environ.get("QRAF_TEST_FULL", "0") == "1"
 
 
 def assert_fast_ok(y, y_ref, y64, label):
@@ -347,8 +346,38 @@ def weight_for(name, d, torch, dev):
 
 
 def config_names(digests):
-    small = [n for n, d in digests.items() if d["n"] * d["k"] <= 300_000_000]
-    return sorted(digests) if FULL else sorted(small)
+    """Every BASELINE configuration shape, the two LM heads (151936 x 2048 Q8_0,
+    128256 x 8192 Q4_0) included."""
+    return sorted(digests)
+
+
+# Outputs outside strict allclose(RTOL, ATOL) of the reference, per (config, M,
+# mode): printed at the end of the session, written as JSON where
+# QRAF_PARITY_REPORT names a file.  Configurations 1 and 2 (4096 x 4096) must
+# have none.
+STRICT_MISSES = {}
+STRICT_REQUIRED = ("cfg1_q8_4096x4096", "cfg2_q4_4096x4096")
+
+
+def strict_misses(y, y_ref):
+    y, y_ref = np.asarray(y, np.float64), np.asarray(y_ref, np.float64)
+    return int((np.abs(y - y_ref) > ATOL + RTOL * np.abs(y_ref)).sum())
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _strict_report():
+    yield
+    if not STRICT_MISSES:
+        return
+    import json
+
+    print("\nstrict allclose(1e-5, 1e-6) misses per config, M and mode (outputs):")
+    for key, v in sorted(STRICT_MISSES.items()):
+        print(f"  {key}: {v['misses']} of {v['outputs']}")
+    path = os.environ.get("QRAF_PARITY_REPORT")
+    if path:
+        with open(path, "w") as f:
+            json.dump(STRICT_MISSES, f, indent=1, sort_keys=True)
 
 
 def pytest_generate_tests(metafunc):
@@ -375,9 +404,13 @@ def test_config_exact_and_fast(cuda, digests, config_name, oracle_lib):
         xh = xall[:m].cpu().numpy()
         y64 = np.stack([oracle_lib.matvec_f64(d["dtype"], q_host, d["n"], d["k"], xh[j]) for j in range(m)])
         assert_fast_ok(y_fast, y_exact, y64, f"{config_name} M={m}")
+        STRICT_MISSES[f"{config_name} M={m} FAST"] = {"misses": strict_misses(y_fast, y_exact), "outputs": y_fast.size}
+        if config_name in STRICT_REQUIRED:
+            assert STRICT_MISSES[f"{config_name} M={m} FAST"]["misses"] == 0, f"{config_name}: FAST not strictly close"
         if d["k"] % (256 if d["dtype"] == qb.Q4_0 else 128) == 0:
             y_tc = qb.matvec_q(w, xall[:m].contiguous(), mode=qb.MODE_TC).cpu().numpy()
             assert_fast_ok(y_tc, y_exact, y64, f"{config_name} M={m} tensor cores")
+            STRICT_MISSES[f"{config_name} M={m} TC"] = {"misses": strict_misses(y_tc, y_exact), "outputs": y_tc.size}
         if m == 1 and config_name in ys.files:
             assert y_exact[0].tobytes() == ys[config_name].tobytes()
     assert qb.device_status() == qb.OK

@@ -118,7 +118,7 @@ def _block_scales(dt, q, n, k):
 
 @pytest.mark.parametrize("dt", [10, 20])
 def test_limb_partials_reconstruct_the_dot(oracle_lib, dt):
-    """The integer restatement of the FAST path: sum_b scale_b c_b sum_j 2^(7(3-j)) D_j
+    """The integer restatement of the FAST path: sum_b scale_b c_b sum_j 2^(8(3-j)) D_j
     matches the fp64 dot up to the rounding of X_i (half a unit of c_b per element),
     including blocks of zeros, of tiny (subnormal-range) and of huge values."""
     n, k = 16, 512
@@ -132,7 +132,7 @@ def test_limb_partials_reconstruct_the_dot(oracle_lib, dt):
     q = oracle_lib.quantize_rows(dt, w)
     d, c = oracle_lib.limb_partials(dt, q, n, k, x)
     assert c[1] == 0.0 and not d[:, 1].any()
-    ints = (d.astype(np.int64) * np.array([1 << 21, 1 << 14, 1 << 7, 1], np.int64)).sum(-1)
+    ints = (d.astype(np.int64) * np.array([1 << 24, 1 << 16, 1 << 8, 1], np.int64)).sum(-1)
     sc = _block_scales(dt, q, n, k)
     rec = (sc * c.astype(np.float64)[None, :] * ints).sum(1)
     y64 = oracle_lib.matvec_f64(dt, q, n, k, x)
@@ -142,7 +142,8 @@ def test_limb_partials_reconstruct_the_dot(oracle_lib, dt):
 
 
 def test_limb_partials_known_block(oracle_lib):
-    """Block max 0.75 (so e = 0, c = 2^-27 and X_i = rint(x_i 2^27)) against codes all 1."""
+    """Block max 0.75 (t = 0.75 (1 + 2^-8) < 1, so e = 0, c = 2^-30 and X_i = rint(x_i 2^30))
+    against codes all 1; every digit within [-128, 127]."""
     k = 32
     raw = np.zeros(36, np.uint8)
     raw[:4] = np.frombuffer(np.float32(1.0).tobytes(), np.uint8)
@@ -150,6 +151,6 @@ def test_limb_partials_known_block(oracle_lib):
     x = (np.arange(1, 33, dtype=np.float32) / np.float32(64.0)) * np.float32(0.98)
     x[-1] = np.float32(0.75)
     d, c = oracle_lib.limb_partials(10, raw, 1, k, x)
-    assert c[0] == np.float32(2.0 ** -27)
-    ints = int((d[0, 0].astype(np.int64) * np.array([1 << 21, 1 << 14, 1 << 7, 1])).sum())
-    assert ints == int(sum(int(np.rint(float(v) * 2.0 ** 27)) for v in x))
+    assert c[0] == np.float32(2.0 ** -30)
+    ints = int((d[0, 0].astype(np.int64) * np.array([1 << 24, 1 << 16, 1 << 8, 1])).sum())
+    assert ints == int(sum(int(np.rint(float(v) * 2.0 ** 30)) for v in x))
