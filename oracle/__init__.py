@@ -22,7 +22,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "libqraf_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libqraf_ref.so")
-REF_TREE = os.environ.get("QRAF_REFERENCE_TREE", "/root/reference")
+# The reference checkout: QRAF_REFERENCE_TREE, else the directory `reference`
+# beside this repository (oracle/Makefile uses the same default).
+REF_TREE = os.environ.get("QRAF_REFERENCE_TREE",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 Q8_0 = 10
 Q4_0 = 20

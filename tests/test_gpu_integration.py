@@ -1,7 +1,7 @@
 """The drop-in, end to end: the reference's own code calling the CUDA path.
 
-oracle/_ref/libqraf_ref_cuda.so is the reference's sources linked exactly as
-INTEGRATION.md describes (backend.cpp's scalar dispatch_matvec_q renamed, the
+oracle/_ref/libqraf_ref_cuda.so is the reference's sources linked the way a QRAF
+maintainer links the library (backend.cpp's scalar dispatch_matvec_q renamed, the
 shim qraf_b200/shim/dispatch_matvec_q_cuda.cpp in its place).  The reference's
 unmodified SwiGLU MLP (src/nn/attention.cpp:159-186: gate, up and down
 projections through do_matvec -> dispatch_matvec_q) must give bit-identical
