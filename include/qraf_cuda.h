@@ -119,6 +119,19 @@ int qraf_cuda_weight_shard(const qraf_weight_t* full, uint32_t world, uint32_t r
 int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev, uint32_t M, int mode,
                        void* stream);
 
+/* Several projections of the same activations in one launch: ys_dev[i] =
+ * W_i X for the `count` weights ws[0..count) (1 to QRAF_MULTI_MAX_WEIGHTS, same
+ * dtype, block size, cols and device; each ys_dev[i] is [M][ws[i].rows]).  The
+ * reference makes one dispatch_matvec_q call per projection on one input
+ * (src/nn/attention.cpp:92-97: Q, K and V of the normalised hidden state;
+ * :172-174: gate and up); here the weights are one row range of one launch, so
+ * the activations are staged once and there is one launch instead of `count`.
+ * EXACT (any M) and FAST (M <= 2) run fused and give the same bits as separate
+ * qraf_cuda_matvec_q calls; other modes and shapes run one call per weight. */
+#define QRAF_MULTI_MAX_WEIGHTS 4
+int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
+                             uint32_t M, int mode, void* stream);
+
 /* The tensor-core path of qraf_cuda_matvec_q (QRAF_MODE_TC, same kernels and
  * results) for callers that may not allocate device memory: its scratch (the
  * prepared activation tiles, the stream-K partial sums and tile counters) lives
@@ -210,10 +223,11 @@ int qraf_cuda_comm_destroy(qraf_comm_t comm);
  * peer's receive array over NVLink; before it ends it copies the other ranks'
  * rows into this rank's buffer, so Y[m][n] for all n is in *y_out (this rank's
  * buffer for this call, valid for the next QRAF_COMM_BUFFERS - 1 calls) when
- * the launch completes.  Same arguments and modes as qraf_cuda_matvec_q; needs
- * block size 32, 16-byte-aligned rows, and M small enough for one launch
- * (M <= 2 in FAST mode).  The calls of one comm go to one stream, in the same
- * order on every rank.  Calls are numbered on the device, so a sequence of
+ * the launch completes.  Same arguments as qraf_cuda_matvec_q, modes EXACT
+ * and FAST (AUTO runs FAST); needs block size 32, K a multiple of 32 and
+ * 16-byte-aligned rows and pointers.  Any M: the vectors go in groups of one
+ * launch each (FAST: two), every launch one numbered call of the protocol.
+ * The calls of one comm go to one stream, in the same order on every rank.  Calls are numbered on the device, so a sequence of
  * calls may be captured in a CUDA graph and replayed; capture a multiple of
  * QRAF_COMM_BUFFERS calls per comm so that replays keep the buffer rotation
  * (the buffers are chosen at capture).  A peer that does not deliver its rows

@@ -80,6 +80,7 @@ def _load() -> C.CDLL:
         "qraf_cuda_weight_free": (i32, [W]),
         "qraf_cuda_weight_shard": (i32, [W, u32, u32, W]),
         "qraf_cuda_matvec_q": (i32, [W, vp, vp, u32, i32, vp]),
+        "qraf_cuda_matvec_q_multi": (i32, [W, u32, vp, C.POINTER(vp), u32, i32, vp]),
         "qraf_cuda_matmul_tc_noalloc": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
         "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
@@ -236,6 +237,30 @@ def matvec_q(w: Weight, x, y=None, mode: int = MODE_AUTO, stream=None):
     check(_get_lib().qraf_cuda_matvec_q(C.byref(w.desc), C.c_void_p(x2.data_ptr()), C.c_void_p(y.data_ptr()), m, mode,
                                  _stream(stream)))
     return y.reshape(w.rows) if squeeze else y
+
+
+MULTI_MAX_WEIGHTS = 4
+
+
+def matvec_q_multi(weights, x, ys=None, mode: int = MODE_AUTO, stream=None):
+    """[W_i X for each weight] in one launch (qraf_cuda_matvec_q_multi): projections of
+    the same activations, e.g. a layer's Q, K and V, or gate and up.  Returns the list
+    of outputs ([M, rows_i] each, or [rows_i] for a 1-D x)."""
+    torch = _torch()
+    if not 1 <= len(weights) <= MULTI_MAX_WEIGHTS:
+        raise ValueError(f"1 to {MULTI_MAX_WEIGHTS} weights")
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.dtype != torch.float32 or not x2.is_cuda or not x2.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA float32 tensor")
+    m = x2.shape[0]
+    if ys is None:
+        ys = [torch.empty((m, w.rows), dtype=torch.float32, device=x.device) for w in weights]
+    descs = (qraf_weight_t * len(weights))(*[w.desc for w in weights])
+    outs = (C.c_void_p * len(weights))(*[y.data_ptr() for y in ys])
+    check(_get_lib().qraf_cuda_matvec_q_multi(descs, len(weights), C.c_void_p(x2.data_ptr()), outs, m, mode,
+                                              _stream(stream)))
+    return [y.reshape(w.rows) for y, w in zip(ys, weights)] if squeeze else ys
 
 
 def dot_q(dtype: int, q, x, count: int, block_size: int = 32, mode: int = MODE_EXACT, stream=None):

@@ -275,12 +275,20 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.rows_extra = rows_extra;
     p.pdl = 0;
     p.xrec = nullptr;
+    p.nseg = 0;
+    for (int i = 0; i < kMaxSeg; ++i) {
+        p.seg_w[i] = nullptr;
+        p.seg_y[i] = nullptr;
+        p.seg_row0[i] = 0;
+    }
+    p.seg_row0[kMaxSeg] = 0;
     p.world = 0;
     p.rank = 0;
     p.seq = nullptr;
     p.y_ld = w.rows;
     p.row_off = 0;
     p.y_full = nullptr;
+    p.v_off = 0;
     p.local_ll = nullptr;
     p.ll_cap = 0;
     p.cta_counter = nullptr;
@@ -920,6 +928,77 @@ int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev,
     return matvec_impl(w, x_dev, y_dev, M, mode, static_cast<cudaStream_t>(stream));
 }
 
+static_assert(QRAF_MULTI_MAX_WEIGHTS == kMaxSeg, "the header's weight limit is the kernel's segment count");
+
+int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
+                             uint32_t M, int mode_in, void* stream) {
+    if (!ws || !ys_dev || count == 0 || count > static_cast<uint32_t>(kMaxSeg))
+        return fail(QRAF_ERR_INVALID, "multi call needs 1 to %d weights and their outputs", kMaxSeg);
+    for (uint32_t i = 0; i < count; ++i) {
+        const int rc = check_weight(&ws[i]);
+        if (rc) return rc;
+        if (ws[i].dtype != ws[0].dtype || ws[i].block_size != ws[0].block_size || ws[i].cols != ws[0].cols ||
+            ws[i].device != ws[0].device)
+            return fail(QRAF_ERR_INVALID, "weight %u differs from weight 0 in dtype, block size, cols or device", i);
+        if (ws[i].rows && !ys_dev[i]) return fail(QRAF_ERR_INVALID, "output %u is NULL", i);
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
+    int mode = mode_in & 0xFF;
+    if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(ws[0])) ? QRAF_MODE_TC : QRAF_MODE_FAST;
+    const bool exact = mode == QRAF_MODE_EXACT;
+    uint64_t total = 0;
+    bool eligible = (exact || (mode == QRAF_MODE_FAST && M <= 2)) && count > 1 && M > 0 && ws[0].cols > 0 && x_dev;
+    for (uint32_t i = 0; i < count && eligible; ++i) {
+        eligible = ws[i].rows > 0 && rows_eligible(ws[i], x_dev);
+        total += ws[i].rows;
+    }
+    DeviceInfo* dev = nullptr;
+    if (eligible && total <= 0xFFFFFFFFull) {
+        int rc = ensure_device(nullptr, &dev);
+        if (rc) return rc;
+        qraf_weight_t v = ws[0];   // the weights as one virtual row range
+        v.rows = static_cast<uint32_t>(total);
+        v.bytes = total * v.row_bytes;
+        uint32_t per = M;
+        RowPlan pl;
+        while (per > 1 && !plan_rows(v, x_dev, nullptr, per, exact, *dev, &pl)) per = (per + 1) / 2;
+        if (plan_rows(v, x_dev, nullptr, per, exact, *dev, &pl)) {
+            for (uint32_t m0 = 0; m0 < M; m0 += per) {
+                RowPlan one = pl;
+                RowParams& p = one.p;
+                const uint32_t cnt = std::min(per, M - m0);
+                p.x = x_dev + static_cast<size_t>(m0) * v.cols;
+                p.M = cnt;
+                p.nseg = count;
+                uint32_t row0 = 0;
+                for (uint32_t i = 0; i < count; ++i) {
+                    p.seg_w[i] = static_cast<const uint8_t*>(ws[i].data);
+                    p.seg_y[i] = ys_dev[i] + static_cast<size_t>(m0) * ws[i].rows;
+                    p.seg_row0[i] = row0;
+                    row0 += ws[i].rows;
+                }
+                for (uint32_t i = count; i <= static_cast<uint32_t>(kMaxSeg); ++i) p.seg_row0[i] = row0;
+                const bool ov = overlap || m0 > 0;
+                if (exact) {
+                    const cudaError_t e = launch_rows(v.dtype, one, true, 1, ov, st);
+                    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "row kernel launch: %s", cudaGetErrorString(e));
+                } else {
+                    rc = launch_rows_fast(v.dtype, one, static_cast<int>(cnt), ov, st);
+                    if (rc) return rc;
+                }
+            }
+            return QRAF_OK;
+        }
+    }
+    // otherwise: one call per weight (same results as the fused launch would give)
+    for (uint32_t i = 0; i < count; ++i) {
+        const int rc = matvec_impl(&ws[i], x_dev, ys_dev[i], M, mode | (overlap ? QRAF_MODE_FLAG_OVERLAP : 0), st);
+        if (rc) return rc;
+    }
+    return QRAF_OK;
+}
+
 // ── the tensor-core path without allocation ───────────────────────────────
 // Its scratch: one fixed array per device, shared by every call on that device.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[QRAF_NOALLOC_SCRATCH_BYTES];
@@ -1214,33 +1293,48 @@ int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32
     if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
     if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_UNSUPPORTED, "mode %d", mode_in);
     const bool exact = mode == QRAF_MODE_EXACT;
-    if (!rows_eligible(*shard, x_dev) || (!exact && M > 2))
-        return fail(QRAF_ERR_UNSUPPORTED, "the sharded path needs block size 32, 16-byte-aligned rows and pointers, "
-                                          "and M <= 2 in FAST mode");
+    if (!rows_eligible(*shard, x_dev))
+        return fail(QRAF_ERR_UNSUPPORTED, "the sharded path needs block size 32, K a multiple of 32, and 16-byte-aligned "
+                                          "rows and pointers");
     DeviceInfo* dev = nullptr;
     rc = ensure_device(nullptr, &dev);
     if (rc) return rc;
+    // Vectors in groups of one launch each (FAST: two, the row kernel's widest pass;
+    // EXACT: as many as the shared memory takes).  Every launch is one numbered
+    // call of the comm's protocol; all of them write into this host call's buffer,
+    // each at its own vector offset.
+    uint32_t per = exact ? M : std::min<uint32_t>(M, 2u);
     RowPlan pl;
-    if (!plan_rows(*shard, x_dev, nullptr, M, exact, *dev, &pl))
-        return fail(QRAF_ERR_UNSUPPORTED, "%u activation vectors do not fit one launch", M);
+    while (per > 1 && !plan_rows(*shard, x_dev, nullptr, per, exact, *dev, &pl)) per = (per + 1) / 2;
+    if (!plan_rows(*shard, x_dev, nullptr, per, exact, *dev, &pl))
+        return fail(QRAF_ERR_UNSUPPORTED, "one activation vector of K = %u does not fit one launch", shard->cols);
     const int buf = static_cast<int>(++c->calls % QRAF_COMM_BUFFERS);
-    RowParams& p = pl.p;
-    p.world = static_cast<uint32_t>(c->world);
-    p.rank = static_cast<uint32_t>(c->rank);
-    p.seq = c->counter + 32;
-    p.y_ld = total_rows;
-    p.row_off = row_offset;
-    p.y_full = c->y[buf];
-    p.local_ll = c->ll;
-    p.ll_cap = c->cap;
-    p.cta_counter = c->counter;
-    for (int r = 0; r < c->world; ++r) p.peer_ll[r] = c->peer_ll[r];
-    if (exact) {
-        const cudaError_t e = launch_rows(shard->dtype, pl, true, 1, overlap, static_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));
-    } else {
-        rc = launch_rows_fast(shard->dtype, pl, static_cast<int>(M), overlap, static_cast<cudaStream_t>(stream));
-        if (rc) return rc;
+    for (uint32_t m0 = 0; m0 < M; m0 += per) {
+        RowPlan one = pl;
+        RowParams& p = one.p;
+        const uint32_t cnt = std::min(per, M - m0);
+        p.x = x_dev + static_cast<size_t>(m0) * shard->cols;
+        p.M = cnt;
+        p.world = static_cast<uint32_t>(c->world);
+        p.rank = static_cast<uint32_t>(c->rank);
+        p.seq = c->counter + 32;
+        p.y_ld = total_rows;
+        p.row_off = row_offset;
+        p.y_full = c->y[buf];
+        p.v_off = m0;
+        p.local_ll = c->ll;
+        p.ll_cap = c->cap;
+        p.cta_counter = c->counter;
+        for (int r = 0; r < c->world; ++r) p.peer_ll[r] = c->peer_ll[r];
+        // a later group waits for the one before it (it reuses the CTA counter and call number)
+        const bool ov = overlap || m0 > 0;
+        if (exact) {
+            const cudaError_t e = launch_rows(shard->dtype, one, true, 1, ov, static_cast<cudaStream_t>(stream));
+            if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "sharded kernel launch: %s", cudaGetErrorString(e));
+        } else {
+            rc = launch_rows_fast(shard->dtype, one, static_cast<int>(cnt), ov, static_cast<cudaStream_t>(stream));
+            if (rc) return rc;
+        }
     }
     *y_out = c->y[buf];
     return QRAF_OK;

@@ -53,6 +53,7 @@ constexpr int kRowWarps = 16;                      // warps per CTA (4 per SM su
 constexpr int kRowThreads = kRowWarps * 32;
 constexpr int kRowGMax = 4;                        // rows per stage, at most
 constexpr int kMaxWorld = 8;                       // GPUs in a row-sharded group, at most
+constexpr int kMaxSeg = 4;                         // weights of one multi-weight launch, at most
 
 struct RowParams {
     const uint8_t* w;        // [N][row_bytes], 16-byte aligned, row_bytes % 16 == 0
@@ -75,6 +76,14 @@ struct RowParams {
     uint32_t rows_base, rows_extra;
     uint32_t pdl;            // 1: programmatic dependent launch protocol
     const uint8_t* xrec;     // FAST: limb records built by limb_prep_kernel ([M][nblk] x kLimbRec), or null
+    // Several weights of one input in one launch (nseg >= 2): virtual rows
+    // [seg_row0[i], seg_row0[i+1]) are the rows of weight i (seg_w[i]), whose
+    // outputs go to seg_y[i] ([M][rows of weight i]); same cols, dtype and
+    // row_bytes for all.  nseg <= 1: the one weight w and output y.
+    uint32_t nseg;
+    const uint8_t* seg_w[kMaxSeg];
+    float* seg_y[kMaxSeg];
+    uint32_t seg_row0[kMaxSeg + 1];
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
     // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
     // output element goes into this rank's y and, as one 8-byte word (call number
@@ -84,7 +93,8 @@ struct RowParams {
     // ranks' rows from this rank's receive array into y, polling (bounded) until
     // each word carries this call's number.  Calls are numbered on the device
     // (*seq), so a captured and replayed sequence of calls stays in step.
-    float* y_full;                                // this rank's y, [M][y_ld]
+    float* y_full;                                // this rank's y, [M_call][y_ld] (all vectors of the host call)
+    uint32_t v_off;                               // this launch's first vector within the host call
     unsigned long long* peer_ll[kMaxWorld];       // rank r's receive array: two halves of ll_cap words (call parity)
     unsigned long long* local_ll;                 // this rank's receive array
     uint64_t ll_cap;
@@ -103,14 +113,35 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
     return v;
 }
 
-// One output element: into y, or (row-sharded) into this rank's y and every
-// peer's receive array.
+// The segment (weight) that virtual row `row` belongs to (multi-weight launches).
+__device__ __forceinline__ uint32_t seg_of(const RowParams& p, uint32_t row) {
+    uint32_t i = 0;
+#pragma unroll
+    for (int j = 1; j < kMaxSeg; ++j)
+        if (static_cast<uint32_t>(j) < p.nseg && row >= p.seg_row0[j]) i = static_cast<uint32_t>(j);
+    return i;
+}
+
+// First byte of virtual row `row` in global memory.
+__device__ __forceinline__ const uint8_t* row_src(const RowParams& p, uint32_t row) {
+    if (p.nseg <= 1) return p.w + static_cast<size_t>(row) * p.row_bytes;
+    const uint32_t i = seg_of(p, row);
+    return p.seg_w[i] + static_cast<size_t>(row - p.seg_row0[i]) * p.row_bytes;
+}
+
+// One output element: into y (or its weight's y), or (row-sharded) into this
+// rank's y and every peer's receive array.
 __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uint32_t v, uint32_t row, float t) {
     if (p.world == 0) {
-        p.y[static_cast<size_t>(v) * p.N + row] = t;
+        if (p.nseg <= 1) {
+            p.y[static_cast<size_t>(v) * p.N + row] = t;
+        } else {
+            const uint32_t i = seg_of(p, row);
+            p.seg_y[i][static_cast<size_t>(v) * (p.seg_row0[i + 1] - p.seg_row0[i]) + (row - p.seg_row0[i])] = t;
+        }
         return;
     }
-    const size_t idx = static_cast<size_t>(v) * p.y_ld + p.row_off + row;
+    const size_t idx = static_cast<size_t>(v + p.v_off) * p.y_ld + p.row_off + row;
     p.y_full[idx] = t;
     const unsigned long long word = (static_cast<unsigned long long>(call) << 32) | __float_as_uint(t);
     const size_t off = static_cast<size_t>(call & 1u) * p.ll_cap + idx;
@@ -127,8 +158,11 @@ __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uin
 // rows of c + 1, which this rank computes only after this launch (call c)
 // has completed.
 __device__ __forceinline__ void sharded_gather(const RowParams& p, uint32_t call) {
+    // this launch's vectors [v_off, v_off + M) of the host call
+    const size_t base = static_cast<size_t>(p.v_off) * p.y_ld;
     const size_t total = static_cast<size_t>(p.M) * p.y_ld;
-    const unsigned long long* ll = p.local_ll + static_cast<size_t>(call & 1u) * p.ll_cap;
+    const unsigned long long* ll = p.local_ll + static_cast<size_t>(call & 1u) * p.ll_cap + base;
+    float* yf = p.y_full + base;
     const uint64_t t0 = globaltimer_ns();
     bool ok = true;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; ok && i < total;
@@ -144,7 +178,7 @@ __device__ __forceinline__ void sharded_gather(const RowParams& p, uint32_t call
             }
             w = ld_relaxed_sys_u64(ll + i);
         }
-        if (ok) p.y_full[i] = __uint_as_float(static_cast<uint32_t>(w));
+        if (ok) yf[i] = __uint_as_float(static_cast<uint32_t>(w));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -504,17 +538,27 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     auto issue = [&](uint32_t s, uint32_t slot) {
         const uint32_t g = p.npieces == 1 ? s : s / p.npieces, pc = s - g * p.npieces;
         const uint32_t rows = min(p.G, nrows - g * p.G);
-        const uint8_t* src = p.w + static_cast<size_t>(r0 + g * p.G) * p.row_bytes + static_cast<size_t>(pc) * p.piece_bytes;
+        const uint32_t a = r0 + g * p.G;   // first (virtual) row of the stage
         uint8_t* dst = slots + static_cast<size_t>(slot) * p.slot_stride;
-        if (p.npieces == 1) {   // whole rows: one copy
+        if (p.npieces == 1) {   // whole rows: one copy (one per weight where the rows span several)
             const uint32_t bytes = rows * static_cast<uint32_t>(p.row_bytes);
             mbar_arrive_expect_tx(&full[slot], bytes);
-            bulk_g2s(dst, src, bytes, &full[slot], pol);
+            if (p.nseg <= 1) {
+                bulk_g2s(dst, p.w + static_cast<size_t>(a) * p.row_bytes, bytes, &full[slot], pol);
+            } else {
+                for (uint32_t i = 0; i < p.nseg; ++i) {
+                    const uint32_t lo = max(a, p.seg_row0[i]), hi = min(a + rows, p.seg_row0[i + 1]);
+                    if (lo < hi)
+                        bulk_g2s(dst + static_cast<size_t>(lo - a) * p.row_bytes, row_src(p, lo),
+                                 (hi - lo) * static_cast<uint32_t>(p.row_bytes), &full[slot], pol);
+                }
+            }
         } else {                // one copy per row of this piece
             const uint32_t pb = min(p.piece_blocks, p.nblk - pc * p.piece_blocks) * kBlockBytes;
             mbar_arrive_expect_tx(&full[slot], rows * pb);
             for (uint32_t i = 0; i < rows; ++i)
-                bulk_g2s(dst + i * p.piece_bytes, src + static_cast<size_t>(i) * p.row_bytes, pb, &full[slot], pol);
+                bulk_g2s(dst + i * p.piece_bytes, row_src(p, a + i) + static_cast<size_t>(pc) * p.piece_bytes, pb,
+                         &full[slot], pol);
         }
         slot_stage[slot] = s;   // the slot's barrier is now in stage s's phase
     };

@@ -414,3 +414,29 @@ def test_config_exact_and_fast(cuda, digests, config_name, oracle_lib):
         if m == 1 and config_name in ys.files:
             assert y_exact[0].tobytes() == ys[config_name].tobytes()
     assert qb.device_status() == qb.OK
+
+
+# ── several projections of one input in one launch ───────────────────────
+@pytest.mark.parametrize("dt,rows,k", [
+    (qb.Q8_0, (2048, 256, 256), 2048),      # Qwen2-3B Q, K, V (config 3)
+    (qb.Q4_0, (3000, 3000), 4096),          # gate and up
+    (qb.Q4_0, (5, 3, 7, 1), 8192),          # tiny weights: stages span several of them
+    (qb.Q4_0, (640, 700), 28672),           # long rows: pieces of K, limb prep
+])
+def test_multi_weight_launch_equals_separate_calls(cuda, dt, rows, k):
+    """qraf_cuda_matvec_q_multi gives the bits of one qraf_cuda_matvec_q call per
+    weight, in EXACT (1 and 3 vectors) and FAST (1 and 2)."""
+    import torch
+
+    ws = []
+    for i, n in enumerate(rows):
+        wf = torch.from_numpy(qb.fill_normal(42 + i, 0.0, 0.02, n * k)).to(cuda).reshape(n, k)
+        ws.append(qb.Weight.from_device(qb.quantize_rows(dt, wf).reshape(-1), dt, n, k))
+    for mode, ms in ((qb.MODE_EXACT, (1, 3)), (qb.MODE_FAST, (1, 2))):
+        for m in ms:
+            x = torch.from_numpy(qb.fill_normal(50 + m, 0.0, 1.0, m * k)).to(cuda).reshape(m, k)
+            got = qb.matvec_q_multi(ws, x, mode=mode)
+            for i, w in enumerate(ws):
+                want = qb.matvec_q(w, x, mode=mode)
+                assert got[i].cpu().numpy().tobytes() == want.cpu().numpy().tobytes(), f"mode {mode} M={m} weight {i}"
+    assert qb.device_status() == qb.OK

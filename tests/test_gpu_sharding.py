@@ -27,14 +27,18 @@ def test_single_rank_group_equals_plain_matvec(cuda, dt, mode):
     n, k = 1024, 2048
     q = _weight(torch, cuda, dt, n, k)
     w = qb.Weight.from_device(q, dt, n, k)
-    comm = qb.Comm(1, 0, 3 * n)
+    comm = qb.Comm(1, 0, 7 * n)
     qb.Comm.open_local([comm])
-    for m in (1, 2) if mode == qb.MODE_FAST else (1, 3):
+    for m in (1, 2, 5) if mode == qb.MODE_FAST else (1, 3, 7):
         x = torch.from_numpy(qb.fill_normal(43 + m, 0.0, 1.0, m * k)).to(cuda).reshape(m, k)
-        want = qb.matvec_q(w, x, mode=mode).cpu().numpy()
+        if mode == qb.MODE_FAST:   # sharded FAST runs the row kernel on pairs of vectors
+            want = np.concatenate([qb.matvec_q(w, x[m0:m0 + 2].contiguous(), mode=mode).cpu().numpy()
+                                   for m0 in range(0, m, 2)])
+        else:
+            want = qb.matvec_q(w, x, mode=mode).cpu().numpy()
         for _ in range(3):   # the output buffer alternates call by call
             got = comm.matvec_q(w, n, 0, x, mode=mode).cpu().numpy()
-            assert got.tobytes() == want.tobytes()
+            assert got.tobytes() == want.tobytes(), f"M={m}"
     assert qb.device_status() == qb.OK
     comm.destroy()
 
@@ -94,8 +98,11 @@ def test_single_process_multi_gpu_group(cuda, dt, n, k):
     world = min(ngpu, 8)
     q_full = _weight(torch, cuda, dt, n, k)
     full = qb.Weight.from_device(q_full, dt, n, k)
-    x0 = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, k))
-    want = {md: qb.matvec_q(full, x0.to(cuda), mode=md).cpu().numpy() for md in (qb.MODE_EXACT, qb.MODE_FAST)}
+    m = 3   # three vectors: two launches per sharded FAST call (pairs), one in EXACT
+    x0 = torch.from_numpy(qb.fill_normal(43, 0.0, 1.0, m * k)).reshape(m, k)
+    want = {qb.MODE_EXACT: qb.matvec_q(full, x0.to(cuda), mode=qb.MODE_EXACT).cpu().numpy(),
+            qb.MODE_FAST: np.concatenate([qb.matvec_q(full, x0[m0:m0 + 2].contiguous().to(cuda),
+                                                      mode=qb.MODE_FAST).cpu().numpy() for m0 in (0, 2)])}
     comms, shards, xs, offs = [], [], [], []
     rb = q_full.numel() // n
     for r in range(world):
@@ -107,7 +114,7 @@ def test_single_process_multi_gpu_group(cuda, dt, n, k):
         shards.append(qb.Weight.from_device(qs, dt, r1 - r0, k))
         xs.append(x0.to(dev))
         offs.append(r0)
-        comms.append(qb.Comm(world, r, n))
+        comms.append(qb.Comm(world, r, m * n))
     qb.Comm.open_local(comms)
     for md in (qb.MODE_EXACT, qb.MODE_FAST):
         outs = []
@@ -116,7 +123,7 @@ def test_single_process_multi_gpu_group(cuda, dt, n, k):
             outs.append(comms[r].matvec_q(shards[r], n, offs[r], xs[r], mode=md))
         for r in range(world):
             torch.cuda.set_device(r)
-            assert outs[r].cpu().numpy()[0].tobytes() == want[md].tobytes(), f"rank {r} mode {md}"
+            assert outs[r].cpu().numpy().tobytes() == want[md].tobytes(), f"rank {r} mode {md}"
             assert qb.device_status() == qb.OK
     for r in range(world):
         torch.cuda.set_device(r)
