@@ -247,6 +247,42 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
                             int mode);
 /* Drop every cached device copy made by qraf_cuda_matvec_q_host. */
 int qraf_cuda_host_cache_clear(void);
+/* Upload one weight into that cache now, under the key a later
+ * qraf_cuda_matvec_q_host call with the same arguments looks up, so the first
+ * decode step pays no upload.  The call a host integration adds where the
+ * reference's Transformer::init takes each weight's mapped bytes
+ * (setup_layer_llama's set_w / set_mlp, src/nn/transformer.cpp:96-126, and the
+ * lm_head, :374-389): out_dim = shape[0], in_dim = shape[1], block_size from the
+ * tensor's QuantScheme (0 = 32).  w_size, when non-zero, must cover the rows. */
+int qraf_cuda_host_cache_add(const void* w_host, uint64_t w_size, uint32_t dtype, uint32_t block_size,
+                             uint32_t out_dim, uint32_t in_dim);
+/* Number of cached weights and their device bytes (either pointer may be NULL). */
+int qraf_cuda_host_cache_info(uint32_t* entries, uint64_t* device_bytes);
+
+/* ── .qraf model files on the device ────────────────────────────────────── */
+/* A .qraf file (the reference's format, include/qraf/format.h) with its Q8_0 /
+ * Q4_0 tensors resident on one device.  qraf_cuda_model_open maps the file,
+ * checks it as the reference's loader does (validate_header,
+ * src/qraf/header.cpp:8-55; tensor bounds, src/qraf/loader.cpp:178-211; plus
+ * every section and string this reader touches) and copies every quantized
+ * tensor into one device allocation on the current device (256-byte aligned
+ * tensors); rows = the product of the leading dimensions, cols = the last,
+ * block size from the tensor's QuantScheme (32 without one).  F32 tensors are
+ * not uploaded.  A malformed file returns QRAF_ERR_INVALID before any device
+ * work.  Weights handed out are views (owned = 0), valid until
+ * qraf_cuda_model_close. */
+typedef struct qraf_model* qraf_model_t;
+int qraf_cuda_model_open(const char* path, qraf_model_t* out);
+/* The descriptor of the quantized tensor `name` (QRAF_ERR_INVALID if absent). */
+int qraf_cuda_model_weight(qraf_model_t m, const char* name, qraf_weight_t* out);
+/* Number of quantized tensors, bytes of the device allocation, device (each may be NULL). */
+int qraf_cuda_model_info(qraf_model_t m, uint32_t* num_weights, uint64_t* device_bytes, int* device);
+/* Name of quantized tensor `index` in directory order; NULL past the end. */
+const char* qraf_cuda_model_weight_name(qraf_model_t m, uint32_t index);
+/* Raw 32-bit value of a u32 or f32 config entry (ConfigEntry, format.h:61-65). */
+int qraf_cuda_model_config_u32(qraf_model_t m, const char* key, uint32_t* value);
+/* Free the device copy. */
+int qraf_cuda_model_close(qraf_model_t m);
 
 /* ── host utility ───────────────────────────────────────────────────────── */
 /* Seeded synthetic data with the reference's idiom: std::mt19937(seed) and

@@ -185,6 +185,26 @@ class Reference:
         lib.qref_fp16_to_fp32.argtypes = [C.c_uint16]
         lib.qref_fill_normal.restype = None
         lib.qref_fill_normal.argtypes = [C.c_uint32, C.c_float, C.c_float, _f32p, C.c_size_t]
+        vp, cp = C.c_void_p, C.c_char_p
+        for name, res, args in (
+                ("qref_writer_new", vp, []), ("qref_writer_free", None, [vp]),
+                ("qref_writer_config_u32", None, [vp, cp, C.c_uint32]),
+                ("qref_writer_config_f32", None, [vp, cp, C.c_float]),
+                ("qref_writer_config_string", None, [vp, cp, cp]),
+                ("qref_writer_quant_scheme", C.c_uint32, [vp, C.c_uint32, C.c_uint32, C.c_uint32]),
+                ("qref_writer_tensor", None, [vp, cp, C.c_uint32, C.POINTER(C.c_uint32), C.c_uint32, vp,
+                                              C.c_uint64, C.c_uint32]),
+                ("qref_writer_vocab", None, [vp, C.POINTER(cp), _f32p, C.c_uint32]),
+                ("qref_writer_merges", None, [vp, C.POINTER(C.c_uint32), _f32p, C.c_uint32]),
+                ("qref_writer_special", None, [vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+                ("qref_writer_write", C.c_int, [vp, cp]),
+                ("qref_model_open", vp, [cp]), ("qref_model_close", None, [vp]),
+                ("qref_model_tensor", C.c_int, [vp, cp, C.POINTER(vp), C.POINTER(C.c_uint64),
+                                                C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                                C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+                ("qref_model_hidden_size", C.c_uint32, [vp])):
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, args
         self.lib = lib
 
     def fill_normal(self, seed: int, mean: float, std: float, n: int) -> np.ndarray:
@@ -233,6 +253,65 @@ class Reference:
         self.lib.qref_ops_matvec_quantized(wb, wb.size, dtype, bs, n, k,
                                            np.ascontiguousarray(x, dtype=np.float32).ravel(), y)
         return y
+
+
+    def write_qraf(self, path: str, config=(), tensors=(), schemes=(), vocab=None, merges=(), special=None) -> None:
+        """The reference's QrafWriter (src/qraf/writer.cpp): config = [(key, value)]
+        with int -> u32, float -> f32, str -> string; schemes = [(dtype, block_size,
+        group_size)] added in order; tensors = [(name, shape, dtype, bytes, quant_id)];
+        vocab = (tokens, scores); merges = [(a, b, result, priority)];
+        special = (bos, eos, pad, unk)."""
+        lib = self.lib
+        h = lib.qref_writer_new()
+        try:
+            for key, v in config:
+                if isinstance(v, str):
+                    lib.qref_writer_config_string(h, key.encode(), v.encode())
+                elif isinstance(v, (int, np.integer)):
+                    lib.qref_writer_config_u32(h, key.encode(), int(v))
+                else:
+                    lib.qref_writer_config_f32(h, key.encode(), float(v))
+            for dt, bs, gs in schemes:
+                lib.qref_writer_quant_scheme(h, dt, bs, gs)
+            for name, shape, dt, data, qid in tensors:
+                raw = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8))
+                sh = (C.c_uint32 * len(shape))(*shape)
+                lib.qref_writer_tensor(h, name.encode(), len(shape), sh, dt, raw.ctypes.data, raw.size, qid)
+            if vocab is not None:
+                toks, scores = vocab
+                arr = (C.c_char_p * len(toks))(*[t.encode() for t in toks])
+                sc = np.ascontiguousarray(scores, dtype=np.float32)
+                lib.qref_writer_vocab(h, arr, sc, len(toks))
+            if merges:
+                abr = np.ascontiguousarray([m[:3] for m in merges], dtype=np.uint32).ravel()
+                pr = np.ascontiguousarray([m[3] for m in merges], dtype=np.float32)
+                lib.qref_writer_merges(h, abr.ctypes.data_as(C.POINTER(C.c_uint32)), pr, len(merges))
+            if special is not None:
+                lib.qref_writer_special(h, *special)
+            if lib.qref_writer_write(h, path.encode()) != 0:
+                raise OSError(f"reference writer failed on {path}")
+        finally:
+            lib.qref_writer_free(h)
+
+    def read_qraf(self, path: str, names) -> dict:
+        """Tensors read back by the reference's QrafModel (src/qraf/loader.cpp):
+        name -> (dtype, shape, block_size, bytes); plus hidden_size from its config."""
+        lib = self.lib
+        h = lib.qref_model_open(path.encode())
+        if not h:
+            raise ValueError(f"reference loader rejected {path}")
+        try:
+            out = {"hidden_size": lib.qref_model_hidden_size(h)}
+            for name in names:
+                data, size, dt, nd, bs = C.c_void_p(), C.c_uint64(), C.c_uint32(), C.c_uint32(), C.c_uint32()
+                shape = (C.c_uint32 * 8)()
+                if lib.qref_model_tensor(h, name.encode(), C.byref(data), C.byref(size), C.byref(dt), C.byref(nd),
+                                         shape, C.byref(bs)) != 0:
+                    raise KeyError(name)
+                out[name] = (dt.value, tuple(shape[:nd.value]), bs.value, C.string_at(data.value, size.value))
+            return out
+        finally:
+            lib.qref_model_close(h)
 
 
 def reference_available() -> bool:

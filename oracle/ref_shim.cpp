@@ -11,6 +11,8 @@
 #include "nn/backend.h"
 #include "nn/ops.h"
 #include "qraf/format.h"
+#include "qraf/loader.h"
+#include "qraf/writer.h"
 #include "tensor/quantize.h"
 
 #include <cstring>
@@ -127,6 +129,65 @@ void qref_mlp_forward(float* out, const float* x, const void* w_gate, const void
 // fp32_to_fp16 / fp16_to_fp32 (src/tensor/dtype.cpp:9-59).
 uint16_t qref_fp32_to_fp16(float f) { return fp32_to_fp16(f); }
 float qref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
+
+// The reference's own .qraf writer (src/qraf/writer.cpp, QrafWriter) and loader
+// (src/qraf/loader.cpp, QrafModel) behind plain C handles, to pin the product's
+// writer byte for byte and to read its files back with the reference's code.
+void* qref_writer_new() { return new QrafWriter(); }
+void qref_writer_free(void* h) { delete static_cast<QrafWriter*>(h); }
+void qref_writer_config_u32(void* h, const char* key, uint32_t v) { static_cast<QrafWriter*>(h)->set_config(key, v); }
+void qref_writer_config_f32(void* h, const char* key, float v) { static_cast<QrafWriter*>(h)->set_config(key, v); }
+void qref_writer_config_string(void* h, const char* key, const char* v) {
+    static_cast<QrafWriter*>(h)->set_config_string(key, v);
+}
+uint32_t qref_writer_quant_scheme(void* h, uint32_t dtype, uint32_t block_size, uint32_t group_size) {
+    return static_cast<QrafWriter*>(h)->add_quant_scheme(static_cast<DType>(dtype), block_size, group_size);
+}
+void qref_writer_tensor(void* h, const char* name, uint32_t ndim, const uint32_t* shape, uint32_t dtype,
+                        const void* data, uint64_t size, uint32_t quant_id) {
+    std::vector<u32> sh(shape, shape + ndim);
+    static_cast<QrafWriter*>(h)->add_tensor(name, sh, static_cast<DType>(dtype), data, size, quant_id);
+}
+void qref_writer_vocab(void* h, const char* const* tokens, const float* scores, uint32_t n) {
+    std::vector<std::string> t(tokens, tokens + n);
+    std::vector<f32> sc(scores, scores + n);
+    static_cast<QrafWriter*>(h)->set_vocab(t, sc);
+}
+void qref_writer_merges(void* h, const uint32_t* abr, const float* priority, uint32_t n) {
+    std::vector<std::tuple<u32, u32, u32, f32>> m;
+    for (uint32_t i = 0; i < n; ++i) m.emplace_back(abr[3 * i], abr[3 * i + 1], abr[3 * i + 2], priority[i]);
+    static_cast<QrafWriter*>(h)->set_merges(m);
+}
+void qref_writer_special(void* h, uint32_t bos, uint32_t eos, uint32_t pad, uint32_t unk) {
+    static_cast<QrafWriter*>(h)->set_special_tokens(bos, eos, pad, unk);
+}
+int qref_writer_write(void* h, const char* path) { return static_cast<QrafWriter*>(h)->write(path) ? 0 : 1; }
+
+void* qref_model_open(const char* path) {
+    QrafModel* m = new QrafModel();
+    if (!m->load(path)) {
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+void qref_model_close(void* h) { delete static_cast<QrafModel*>(h); }
+// One tensor: its bytes (a view into the reference's mapping), dtype, shape and
+// the block size of its quantization scheme (0 if none).  Returns 0 if found.
+int qref_model_tensor(void* h, const char* name, const void** data, uint64_t* size, uint32_t* dtype,
+                      uint32_t* ndim, uint32_t* shape, uint32_t* block_size) {
+    QrafModel* m = static_cast<QrafModel*>(h);
+    if (!m->has_tensor(name)) return 1;
+    TensorView tv = m->get_tensor(name);
+    *data = tv.data;
+    *size = tv.data_size;
+    *dtype = static_cast<uint32_t>(tv.dtype);
+    *ndim = tv.ndim();
+    for (uint32_t i = 0; i < tv.ndim() && i < 8; i++) shape[i] = tv.shape[i];
+    *block_size = tv.quant ? tv.quant->block_size : 0;
+    return 0;
+}
+uint32_t qref_model_hidden_size(void* h) { return static_cast<QrafModel*>(h)->config().hidden_size; }
 
 // Seeded synthetic data with the reference's idiom (std::mt19937 +
 // std::normal_distribution<float>, tools/dummy_model.cpp:12-16,

@@ -90,6 +90,14 @@ def _load() -> C.CDLL:
         "qraf_cuda_dequantize": (i32, [u32, vp, u64, u32, vp, vp]),
         "qraf_cuda_matvec_q_host": (i32, [vp, u64, u32, u32, u32, u32, vp, vp, u32, i32]),
         "qraf_cuda_host_cache_clear": (i32, []),
+        "qraf_cuda_host_cache_add": (i32, [vp, u64, u32, u32, u32, u32]),
+        "qraf_cuda_host_cache_info": (i32, [C.POINTER(u32), C.POINTER(u64)]),
+        "qraf_cuda_model_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+        "qraf_cuda_model_weight": (i32, [vp, C.c_char_p, W]),
+        "qraf_cuda_model_info": (i32, [vp, C.POINTER(u32), C.POINTER(u64), C.POINTER(i32)]),
+        "qraf_cuda_model_weight_name": (C.c_char_p, [vp, u32]),
+        "qraf_cuda_model_config_u32": (i32, [vp, C.c_char_p, C.POINTER(u32)]),
+        "qraf_cuda_model_close": (i32, [vp]),
         "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
         "qraf_cuda_comm_create": (i32, [i32, i32, u64, C.POINTER(vp)]),
         "qraf_cuda_comm_handle": (i32, [vp, vp]),
@@ -220,6 +228,66 @@ class Weight:
                 _get_lib().qraf_cuda_weight_free(C.byref(self.desc))
         except Exception:
             pass
+
+
+class DeviceModel:
+    """A .qraf file with its Q8_0 / Q4_0 tensors resident on the current device
+    (qraf_cuda_model_open: one allocation, the file's bytes unchanged)."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        check(_get_lib().qraf_cuda_model_open(os.fsencode(path), C.byref(h)))
+        self._h = h
+
+    @property
+    def names(self) -> list:
+        """Quantized tensors in directory order."""
+        lib, out = _get_lib(), []
+        while True:
+            n = lib.qraf_cuda_model_weight_name(self._h, len(out))
+            if n is None:
+                return out
+            out.append(n.decode())
+
+    def info(self) -> dict:
+        n, b, d = C.c_uint32(), C.c_uint64(), C.c_int()
+        check(_get_lib().qraf_cuda_model_info(self._h, C.byref(n), C.byref(b), C.byref(d)))
+        return {"num_weights": n.value, "device_bytes": b.value, "device": d.value}
+
+    def weight(self, name: str) -> Weight:
+        d = qraf_weight_t()
+        check(_get_lib().qraf_cuda_model_weight(self._h, name.encode(), C.byref(d)))
+        return Weight(d, keepalive=self)
+
+    def config_u32(self, key: str) -> int:
+        """Raw bits of a u32 / f32 config entry."""
+        v = C.c_uint32()
+        check(_get_lib().qraf_cuda_model_config_u32(self._h, key.encode(), C.byref(v)))
+        return v.value
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, C.c_void_p()
+            check(_get_lib().qraf_cuda_model_close(h))
+
+    def __del__(self):
+        try:
+            if self._h:
+                _get_lib().qraf_cuda_model_close(self._h)
+        except Exception:
+            pass
+
+
+def host_cache_add(w_host: np.ndarray, dtype: int, rows: int, cols: int, block_size: int = 32) -> None:
+    """Preload a host weight into the cache qraf_cuda_matvec_q_host (dispatch_matvec_q) looks up."""
+    check(_get_lib().qraf_cuda_host_cache_add(w_host.ctypes.data, w_host.nbytes, dtype, block_size, rows, cols))
+
+
+def host_cache_info() -> tuple:
+    """(entries, device bytes) of that cache."""
+    n, b = C.c_uint32(), C.c_uint64()
+    check(_get_lib().qraf_cuda_host_cache_info(C.byref(n), C.byref(b)))
+    return n.value, b.value
 
 
 def matvec_q(w: Weight, x, y=None, mode: int = MODE_AUTO, stream=None):

@@ -1,12 +1,14 @@
 // capi.cu — the C ABI of libqraf_cuda.so (declared in include/qraf_cuda.h):
 // argument checking, kernel selection and launch planning, the host-pointer
-// drop-in entry with its device weight cache, and small host utilities.
+// drop-in entry with its device weight cache, and small host utilities; the
+// .qraf model store (model_store.cuh) is included at the end.
 #include <algorithm>
 #include <cudaTypedefs.h>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <random>
 #include <string>
@@ -744,6 +746,23 @@ struct HostStaging {
 
 std::mutex g_host_mutex;
 std::map<CacheKey, qraf_weight_t> g_cache;
+
+// The cached device copy of the host weight (w_host, dtype, bs, rows, cols) on
+// `dev`, uploaded on first use.  Called with g_host_mutex held.
+int cache_entry(const void* w_host, uint32_t dtype, uint32_t block_size, uint32_t rows, uint32_t cols, int dev,
+                std::map<CacheKey, qraf_weight_t>::iterator* out) {
+    const uint64_t need = qraf_row_bytes(dtype, block_size, cols) * rows;
+    const CacheKey key{w_host, need, dtype, block_size, rows, cols, dev};
+    auto it = g_cache.find(key);
+    if (it == g_cache.end()) {
+        qraf_weight_t w;
+        const int rc = qraf_cuda_weight_upload(w_host, need, dtype, block_size, rows, cols, &w);
+        if (rc) return rc;
+        it = g_cache.emplace(key, w).first;
+    }
+    *out = it;
+    return QRAF_OK;
+}
 HostStaging g_staging[64];
 
 // Per cached weight, M and mode: a CUDA graph of the call's device work (x in,
@@ -1340,6 +1359,34 @@ int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32
     return QRAF_OK;
 }
 
+int qraf_cuda_host_cache_add(const void* w_host, uint64_t w_size, uint32_t dtype, uint32_t block_size,
+                             uint32_t out_dim, uint32_t in_dim) {
+    if (!known_dtype(dtype)) return fail(QRAF_ERR_UNSUPPORTED, "dtype %u is not Q8_0 (10) or Q4_0 (20)", dtype);
+    if (block_size == 0) block_size = 32;   // a null QuantScheme means 32 (backend.cpp:135)
+    if (!w_host) return fail(QRAF_ERR_INVALID, "w is NULL");
+    if (out_dim == 0) return QRAF_OK;
+    const uint64_t need = qraf_row_bytes(dtype, block_size, in_dim) * out_dim;
+    if (w_size && w_size < need)
+        return fail(QRAF_ERR_INVALID, "weight holds %llu bytes, %u rows need %llu",
+                    static_cast<unsigned long long>(w_size), out_dim, static_cast<unsigned long long>(need));
+    int dev = 0;
+    DeviceInfo* dinfo = nullptr;
+    int rc = ensure_device(&dev, &dinfo);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(g_host_mutex);
+    std::map<CacheKey, qraf_weight_t>::iterator it;
+    return cache_entry(w_host, dtype, block_size, out_dim, in_dim, dev, &it);
+}
+
+int qraf_cuda_host_cache_info(uint32_t* entries, uint64_t* device_bytes) {
+    std::lock_guard<std::mutex> lk(g_host_mutex);
+    uint64_t b = 0;
+    for (const auto& kv : g_cache) b += kv.second.bytes;
+    if (entries) *entries = static_cast<uint32_t>(g_cache.size());
+    if (device_bytes) *device_bytes = b;
+    return QRAF_OK;
+}
+
 int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype, uint32_t block_size, uint32_t out_dim,
                             uint32_t in_dim, const float* x_host, float* y_host, uint32_t M, int mode) {
     if (M == 0 || out_dim == 0) return QRAF_OK;
@@ -1355,17 +1402,12 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
     DeviceInfo* dinfo = nullptr;
     int rc = ensure_device(&dev, &dinfo);
     if (rc) return rc;
-    const uint64_t need = qraf_row_bytes(dtype, block_size, in_dim) * out_dim;
-    (void)w_size;   // the reference never reads it either; it reads exactly `need` bytes
+    (void)w_size;   // the reference never reads it either; it reads exactly rows * row_bytes
     std::lock_guard<std::mutex> lk(g_host_mutex);
-    CacheKey key{w_host, need, dtype, block_size, out_dim, in_dim, dev};
-    auto it = g_cache.find(key);
-    if (it == g_cache.end()) {
-        qraf_weight_t w;
-        rc = qraf_cuda_weight_upload(w_host, need, dtype, block_size, out_dim, in_dim, &w);
-        if (rc) return rc;
-        it = g_cache.emplace(key, w).first;
-    }
+    std::map<CacheKey, qraf_weight_t>::iterator it;
+    rc = cache_entry(w_host, dtype, block_size, out_dim, in_dim, dev, &it);
+    if (rc) return rc;
+    const CacheKey key = it->first;
     HostStaging& s = g_staging[dev];
     const size_t xn = std::max<size_t>(static_cast<size_t>(M) * in_dim, 4);
     const size_t yn = static_cast<size_t>(M) * out_dim;
@@ -1492,3 +1534,5 @@ void qraf_fill_normal(uint32_t seed, float mean, float stddev, float* out_host, 
 }
 
 }  // extern "C"
+
+#include "model_store.cuh"
