@@ -73,6 +73,13 @@ def is_shard_workload(name: str) -> bool:
     return name.endswith("_shard")
 
 
+def uses_tc1(mode_name, n, k, m, sm_count):
+    """Whether one matvec runs the batch-1 tensor-core kernel (qmv_tc1_kernel): one
+    vector under TC, K a multiple of 1024 up to 4096, and every 32-row CTA
+    resident in one wave (capi.cu plan_tc1)."""
+    return m == 1 and mode_name == "tc" and k % 1024 == 0 and k <= 4096 and -(-n // 32) <= sm_count
+
+
 def launches_per_call(n_rows, k, sm_count):
     """Kernels one FAST M <= 2 matvec launches: the activation-limb prep kernel runs
     when a row has at least 256 blocks and a CTA gets at most 96 rows (capi.cu)."""
@@ -94,7 +101,7 @@ def measured_peaks():
 
 def profiled_traffic(kernel, dt, n, k, m=1):
     """DRAM bytes per launch from the committed ncu summary of the same kernel and shape, if present."""
-    stem = "matmul_tc" if kernel == "qmm_tc_kernel" else "matvec_rows"
+    stem = {"qmm_tc_kernel": "matmul_tc", "qmv_tc1_kernel": "matvec_tc1"}.get(kernel, "matvec_rows")
     name = f"{stem}_{'q4' if dt == Q4 else 'q8'}_{n}x{k}{f'_m{m}' if m > 1 else ''}.md"
     path = os.path.join(ROOT, "profiles", name)
     if not os.path.exists(path):
@@ -278,8 +285,12 @@ def run_ours(args, dt, n, k, m):
     qb.init(local)
     mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
     use_tc = args.mode == "tc" or (args.mode == "auto" and m >= 3)   # AUTO's switch (every bench shape qualifies)
-    kernel = "qmm_tc_kernel" if use_tc else ("qmv_rows_kernel" if m <= 2 or args.mode == "exact"
-                                             else "qmv_stream_kernel")
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    if uses_tc1(args.mode, n, k, m, sm_count):
+        kernel = "qmv_tc1_kernel"
+    else:
+        kernel = "qmm_tc_kernel" if use_tc else ("qmv_rows_kernel" if m <= 2 or args.mode == "exact"
+                                                 else "qmv_stream_kernel")
 
     # Seeded weight, quantized on the GPU (byte-exact with the reference quantizer).
     wf = torch.from_numpy(qb.fill_normal(42, 0.0, 0.02, n * k)).to(dev).reshape(n, k)

@@ -51,7 +51,10 @@ extern "C" {
 #define QRAF_MODE_TC    2  /* tcgen05 tensor-core tile (exact per-block integer sums, fp32
                               epilogue); same tolerance as FAST.  Needs block size 32,
                               K % 128 == 0 (Q8_0) or K % 256 == 0 (Q4_0) and 16-byte-aligned
-                              weights. */
+                              weights.  One vector with K a multiple of 1024 up to 4096, a
+                              16-byte-aligned x and at most 32 x (SM count) rows runs a
+                              batch-1 tensor-core kernel instead (int8 MMAs on the FAST
+                              path's activation limbs). */
 /* Per-stream scratch.  QRAF_MODE_TC, and QRAF_MODE_FAST (also the sharded FAST
  * path) when a row has at least 256 blocks (K >= 8192) and a CTA gets at most 96
  * rows (long-K projections, row shards), use scratch memory that the library

@@ -20,6 +20,7 @@
 #include "matvec_generic.cuh"
 #include "matvec_rows.cuh"
 #include "matvec_stream.cuh"
+#include "matvec_tc1.cuh"
 #include "quantize.cuh"
 
 using namespace qraf_dev;
@@ -102,6 +103,8 @@ int ensure_device(int* dev_out, DeviceInfo** info_out) {
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 2>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 1, 4>, lim));
         QRAF_CUDA_TRY(allow_smem(qmv_rows_kernel<kDtypeQ4, false, 2, 2>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_tc1_kernel<kDtypeQ8>, lim));
+        QRAF_CUDA_TRY(allow_smem(qmv_tc1_kernel<kDtypeQ4>, lim));
         QRAF_CUDA_TRY(allow_smem(limb_partials_kernel<kDtypeQ8>, lim));
         QRAF_CUDA_TRY(allow_smem(limb_partials_kernel<kDtypeQ4>, lim));
         QRAF_CUDA_TRY(allow_smem(qmm_tc_kernel<kDtypeQ8, 16>, lim));
@@ -625,13 +628,89 @@ int check_weight(const qraf_weight_t* w) {
 
 constexpr uint32_t kAutoTcMinVectors = 3;
 
+// ── batch-1 tensor-core kernel (qmv_tc1_kernel) ───────────────────────────
+// One vector, block size 32, K a multiple of 1024 up to 4096, 16-byte-aligned
+// rows and x, and every 32-row CTA of the (virtual) weight resident in one wave.
+struct Tc1Plan {
+    Tc1Params p;
+    int grid = 0;
+    size_t smem = 0;
+};
+
+bool tc1_shape_ok(const qraf_weight_t& w) {
+    return w.block_size == 32 && w.cols > 0 && (w.cols % 1024u) == 0 && w.cols <= 32u * kT1MaxBlocks &&
+           (w.row_bytes % 16) == 0 && aligned16(w.data) && w.rows > 0;
+}
+
+// ws[0..count): weights of one dtype and K, as one row range.
+bool plan_tc1(const qraf_weight_t* ws, uint32_t count, const float* x, float* const* ys, const DeviceInfo& dev,
+              Tc1Plan* out) {
+    if (count == 0 || count > static_cast<uint32_t>(kMaxSeg) || !aligned16(x)) return false;
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        if (!tc1_shape_ok(ws[i]) || ws[i].dtype != ws[0].dtype || ws[i].cols != ws[0].cols) return false;
+        total += ws[i].rows;
+    }
+    const uint64_t grid = (total + kT1Rows - 1) / kT1Rows;
+    if (grid == 0 || grid > static_cast<uint64_t>(dev.sm_count)) return false;   // one wave, one CTA per SM
+    Tc1Params& p = out->p;
+    p = Tc1Params{};
+    const uint32_t nblk = ws[0].cols / 32u;
+    const uint32_t bb = ws[0].dtype == QRAF_DTYPE_Q8_0 ? 36u : 18u;
+    uint32_t npc = (nblk * bb + kT1MaxPieceBytes - 1) / kT1MaxPieceBytes;
+    while ((nblk / 32u) % npc) ++npc;   // pieces of a whole number of 32-block groups
+    p.nseg = count;
+    uint32_t row0 = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        p.seg_w[i] = static_cast<const uint8_t*>(ws[i].data);
+        p.seg_y[i] = ys ? ys[i] : nullptr;
+        p.seg_row0[i] = row0;
+        row0 += ws[i].rows;
+    }
+    for (uint32_t i = count; i <= static_cast<uint32_t>(kMaxSeg); ++i) p.seg_row0[i] = row0;
+    p.x = x;
+    p.row_bytes = ws[0].row_bytes;
+    p.N = static_cast<uint32_t>(total);
+    p.nblk = nblk;
+    p.npc = npc;
+    p.pblk = nblk / npc;
+    p.piece_bytes = p.pblk * bb;
+    const Tc1Layout L = ws[0].dtype == QRAF_DTYPE_Q8_0 ? tc1_layout<kDtypeQ8>(nblk, p.piece_bytes, kT1Rows * npc)
+                                                       : tc1_layout<kDtypeQ4>(nblk, p.piece_bytes, kT1Rows * npc);
+    out->smem = L.bytes + 1024u;   // slack for the 1024-byte alignment
+    if (out->smem > static_cast<size_t>(dev.smem_optin) || L.slots < kT1Warps) return false;
+    out->grid = static_cast<int>(grid);
+    return true;
+}
+
+int launch_tc1(uint32_t dtype, Tc1Plan& pl, bool overlap, cudaStream_t st) {
+    pl.p.pdl = overlap ? 1u : 0u;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+    cfg.blockDim = dim3(kT1Threads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = overlap ? 1 : 0;
+    const cudaError_t e = dtype == QRAF_DTYPE_Q8_0 ? cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ8>, pl.p)
+                                                   : cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ4>, pl.p);
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "batch-1 tensor-core kernel launch: %s", cudaGetErrorString(e));
+    return QRAF_OK;
+}
+
 int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode_in, cudaStream_t st) {
     int rc = check_weight(w);
     if (rc) return rc;
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
     int mode = mode_in & 0xFF;
-    // AUTO: the row kernel for one or two vectors, the tensor-core tile from three (measured on B200: at M = 3 the
-    // tile matches or beats the CUDA-core kernels on every BASELINE shape, at M = 2 it is slower on all of them)
+    // AUTO: the row kernel for one or two vectors, the tensor-core tile from three
+    // (measured on B200: at M = 3 the tile matches or beats the CUDA-core kernels on
+    // every BASELINE shape, at M = 2 it is slower on all of them; for one vector the
+    // row kernel also beats the batch-1 tensor-core kernel, 5.7 against 7.1 us on
+    // Q4_0 4096 x 4096 in a dependent chain)
     if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(*w)) ? QRAF_MODE_TC : QRAF_MODE_FAST;
     if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC)
         return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
@@ -645,6 +724,10 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
     DeviceInfo* dev = nullptr;
     rc = ensure_device(nullptr, &dev);
     if (rc) return rc;
+    if (M == 1 && mode == QRAF_MODE_TC) {   // tensor cores for one vector: the batch-1 kernel where it applies
+        Tc1Plan t1;
+        if (plan_tc1(w, 1, x, &y, *dev, &t1)) return launch_tc1(w->dtype, t1, overlap, st);
+    }
     if (mode == QRAF_MODE_TC) {
         if (!tc_eligible(*w))
             return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs block size 32, K a multiple of %u and "
@@ -964,15 +1047,27 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
     int mode = mode_in & 0xFF;
+    const bool auto_mode = mode == QRAF_MODE_AUTO;
     if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(ws[0])) ? QRAF_MODE_TC : QRAF_MODE_FAST;
     const bool exact = mode == QRAF_MODE_EXACT;
+    DeviceInfo* dev = nullptr;
+    bool tc1_any = false;   // a weight that a call of its own would run on the batch-1 tensor-core kernel
+    if (M == 1 && mode == QRAF_MODE_TC && x_dev) {
+        int rc = ensure_device(nullptr, &dev);
+        if (rc) return rc;
+        Tc1Plan t1;
+        if (plan_tc1(ws, count, x_dev, ys_dev, *dev, &t1)) return launch_tc1(ws[0].dtype, t1, overlap, st);
+        for (uint32_t i = 0; i < count && !tc1_any; ++i) tc1_any = ws[i].rows > 0 && plan_tc1(&ws[i], 1, x_dev, &ys_dev[i], *dev, &t1);
+    }
     uint64_t total = 0;
-    bool eligible = (exact || (mode == QRAF_MODE_FAST && M <= 2)) && count > 1 && M > 0 && ws[0].cols > 0 && x_dev;
+    // fused on the row kernel only where each weight alone would run there too, so
+    // that the fused launch gives the separate calls' bits
+    bool eligible = (exact || (mode == QRAF_MODE_FAST && M <= 2)) && !tc1_any && count > 1 && M > 0 &&
+                    ws[0].cols > 0 && x_dev;
     for (uint32_t i = 0; i < count && eligible; ++i) {
         eligible = ws[i].rows > 0 && rows_eligible(ws[i], x_dev);
         total += ws[i].rows;
     }
-    DeviceInfo* dev = nullptr;
     if (eligible && total <= 0xFFFFFFFFull) {
         int rc = ensure_device(nullptr, &dev);
         if (rc) return rc;
@@ -1011,8 +1106,9 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
         }
     }
     // otherwise: one call per weight (same results as the fused launch would give)
+    const int each = (auto_mode ? QRAF_MODE_AUTO : mode) | (overlap ? QRAF_MODE_FLAG_OVERLAP : 0);
     for (uint32_t i = 0; i < count; ++i) {
-        const int rc = matvec_impl(&ws[i], x_dev, ys_dev[i], M, mode | (overlap ? QRAF_MODE_FLAG_OVERLAP : 0), st);
+        const int rc = matvec_impl(&ws[i], x_dev, ys_dev[i], M, each, st);
         if (rc) return rc;
     }
     return QRAF_OK;

@@ -298,12 +298,16 @@ __device__ __forceinline__ float q4_block_limb(const uint32_t (&qw)[4], const Li
     return combine_limbs(d[0], d[1], d[2], d[3]);
 }
 
-// One thread's share of a limb record: elements 8*sub .. 8*sub+7 of a block
+// One thread's share of a block's limbs: elements 8*sub .. 8*sub+7 of the block
 // (for Q4 exactly one group of 8 in the 0,2,4,6,1,3,5,7 order).  The four
 // threads of a block are lanes 4k..4k+3 of one warp, all active (`act` false
 // for padding threads): the group's maximum and plane sums take two shuffles.
+// Results: the digit-plane word pairs w[j][0..1] of the 8 elements, the block
+// factor cb = 2^(e - 30) (NaN when the block holds a non-finite value) and the
+// block's plane sums S_j.
 template <uint32_t DT>
-__device__ __forceinline__ void limb_record_part(const float4 a, const float4 b, bool act, uint8_t* rec, uint32_t sub) {
+__device__ __forceinline__ void limb_part_digits(const float4 a, const float4 b, bool act, uint32_t (&w)[4][2],
+                                                 float& cb_out, int (&S)[4]) {
     const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     float amax = 0.0f;
     uint32_t bad = 0;
@@ -350,8 +354,8 @@ __device__ __forceinline__ void limb_record_part(const float4 a, const float4 b,
         const int X = live ? __float2int_rn(slow ? ldexpf(xv[src], 30 - e) : xv[src] * up) : 0;
         u[i] = static_cast<uint32_t>(X) + 0x80808080u;
     }
-    uint32_t w[4][2];
-    int S[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) S[j] = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {   // 4 x 4 byte transpose: byte k of element word i -> byte i of plane word 3-k
         const uint32_t t0 = __byte_perm(u[4 * h + 0], u[4 * h + 1], 0x5140u), t1 = __byte_perm(u[4 * h + 0], u[4 * h + 1], 0x7362u);
@@ -367,11 +371,21 @@ __device__ __forceinline__ void limb_record_part(const float4 a, const float4 b,
     for (int o = 1; o <= 2; o <<= 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) S[j] += __shfl_xor_sync(0xFFFFFFFFu, S[j], o);
+    cb_out = bad ? __int_as_float(0x7FC00000) : cb;
+}
+
+// The same share stored into a limb record (kLimbRec bytes per block).
+template <uint32_t DT>
+__device__ __forceinline__ void limb_record_part(const float4 a, const float4 b, bool act, uint8_t* rec, uint32_t sub) {
+    uint32_t w[4][2];
+    int S[4];
+    float cb;
+    limb_part_digits<DT>(a, b, act, w, cb, S);
     if (act) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) *reinterpret_cast<uint2*>(rec + 32u * j + 8u * sub) = make_uint2(w[j][0], w[j][1]);
         if (sub == 0) {
-            *reinterpret_cast<float*>(rec + 128) = bad ? __int_as_float(0x7FC00000) : cb;
+            *reinterpret_cast<float*>(rec + 128) = cb;
             *reinterpret_cast<int4*>(rec + 144) = make_int4(S[0], S[1], S[2], S[3]);
         }
     }

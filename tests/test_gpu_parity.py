@@ -425,14 +425,15 @@ def test_config_exact_and_fast(cuda, digests, config_name, oracle_lib):
 ])
 def test_multi_weight_launch_equals_separate_calls(cuda, dt, rows, k):
     """qraf_cuda_matvec_q_multi gives the bits of one qraf_cuda_matvec_q call per
-    weight, in EXACT (1 and 3 vectors) and FAST (1 and 2)."""
+    weight, in EXACT (1 and 3 vectors), FAST (1 and 2) and TC (1: the batch-1
+    tensor-core kernel, fused where all rows fit one wave, else weight by weight)."""
     import torch
 
     ws = []
     for i, n in enumerate(rows):
         wf = torch.from_numpy(qb.fill_normal(42 + i, 0.0, 0.02, n * k)).to(cuda).reshape(n, k)
         ws.append(qb.Weight.from_device(qb.quantize_rows(dt, wf).reshape(-1), dt, n, k))
-    for mode, ms in ((qb.MODE_EXACT, (1, 3)), (qb.MODE_FAST, (1, 2))):
+    for mode, ms in ((qb.MODE_EXACT, (1, 3)), (qb.MODE_FAST, (1, 2)), (qb.MODE_TC, (1,))):
         for m in ms:
             x = torch.from_numpy(qb.fill_normal(50 + m, 0.0, 1.0, m * k)).to(cuda).reshape(m, k)
             got = qb.matvec_q_multi(ws, x, mode=mode)
