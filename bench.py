@@ -898,10 +898,12 @@ def run_token(args, model, m):
         g = gbuf[name]
         return g.view(1, n) if m == 1 else g.view(world, m, rows).permute(1, 0, 2).reshape(m, n)
 
-    # projections of one input go in one launch (qraf_cuda_matvec_q_multi) on one GPU
+    # projections of one input go in one launch (qraf_cuda_matvec_q_multi) on one GPU;
+    # gate and up as one SwiGLU launch (qraf_cuda_matvec_q_swiglu: down reads silu(gate) * up)
     multi = world == 1 and args.multi
     first_of = {g[0]: g for g in spec.get("groups", [])} if multi else {}
     in_group = {name for g in first_of.values() for name in g}
+    swiglu = multi and args.swiglu
 
     def token():
         vals = {"h": h0}
@@ -910,6 +912,10 @@ def run_token(args, model, m):
             for name, n, k, src in projs:
                 if name in first_of:
                     g = first_of[name]
+                    if swiglu and g == ("gate", "up"):
+                        vals["gate"] = qb.matvec_q_swiglu(ws["gate"], ws["up"], vals[src], ybuf["gate"],
+                                                          mode=launch_mode)
+                        continue
                     outs = qb.matvec_q_multi([ws[x] for x in g], vals[src], [ybuf[x] for x in g], mode=launch_mode)
                     vals.update(zip(g, outs))
                 elif name not in in_group:
@@ -992,6 +998,8 @@ def run_token(args, model, m):
             "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "model_shapes": model, "M": m, "layers": spec["layers"],
                        "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode, "calls_per_token": calls,
+                       "mlp": "silu(gate) * up fused into the gate/up launch; down reads it" if swiglu
+                       else "down reads gate (no activation on the path)",
                        "weight_bytes_per_token": total_weight_bytes,
                        "parallelism": (f"rows split over {world} GPUs, all-gather "
                                        f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
@@ -1076,6 +1084,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
+    ap.add_argument("--no-swiglu", dest="swiglu", action="store_false",
+                    help="token workloads on one GPU: gate and up as a plain two-weight launch, down reading gate "
+                         "(default: one SwiGLU launch, down reading silu(gate) * up)")
     ap.add_argument("--no-multi", dest="multi", action="store_false",
                     help="token workloads: one launch per projection even where several share an input")
     ap.add_argument("--allgather", choices=["fused", "nccl"], default="fused",

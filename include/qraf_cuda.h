@@ -135,6 +135,19 @@ int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev,
 int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
                              uint32_t M, int mode, void* stream);
 
+/* SwiGLU of one input: h[m][i] = silu((W_gate X[m])[i]) * (W_up X[m])[i], with
+ * silu(g) = g / (1 + exp(-g)) - the reference's gate and up projections, silu and
+ * product (mlp_forward, src/nn/attention.cpp:172-179; silu_inplace,
+ * src/nn/ops.cpp:218-221).  gate and up have one dtype, block size and shape; h is
+ * [M][rows].  FAST (and AUTO for one or two vectors) runs one launch: the row
+ * kernel streams each gate row beside its up row and writes the product, so
+ * gate and up never reach memory.  Other modes run the two projections in that
+ * mode and an elementwise pass (through a per-stream buffer that, like the
+ * scratch above, is sized at a stream's first call of the shape).  exp is CUDA's
+ * expf (within 2 ulp of the C library's). */
+int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, float* h_dev,
+                              uint32_t M, int mode, void* stream);
+
 /* The tensor-core path of qraf_cuda_matvec_q (QRAF_MODE_TC, same kernels and
  * results) for callers that may not allocate device memory: its scratch (the
  * prepared activation tiles, the stream-K partial sums and tile counters) lives

@@ -81,6 +81,7 @@ def _load() -> C.CDLL:
         "qraf_cuda_weight_shard": (i32, [W, u32, u32, W]),
         "qraf_cuda_matvec_q": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_matvec_q_multi": (i32, [W, u32, vp, C.POINTER(vp), u32, i32, vp]),
+        "qraf_cuda_matvec_q_swiglu": (i32, [W, W, vp, vp, u32, i32, vp]),
         "qraf_cuda_matmul_tc_noalloc": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
         "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
@@ -329,6 +330,22 @@ def matvec_q_multi(weights, x, ys=None, mode: int = MODE_AUTO, stream=None):
     check(_get_lib().qraf_cuda_matvec_q_multi(descs, len(weights), C.c_void_p(x2.data_ptr()), outs, m, mode,
                                               _stream(stream)))
     return [y.reshape(w.rows) for y, w in zip(ys, weights)] if squeeze else ys
+
+
+def matvec_q_swiglu(gate: Weight, up: Weight, x, h=None, mode: int = MODE_AUTO, stream=None):
+    """silu(W_gate X) * (W_up X) (qraf_cuda_matvec_q_swiglu): one launch in FAST / AUTO
+    for one or two vectors.  Returns [M, rows] (or [rows] for a 1-D x)."""
+    torch = _torch()
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.dtype != torch.float32 or not x2.is_cuda or not x2.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA float32 tensor")
+    m = x2.shape[0]
+    if h is None:
+        h = torch.empty((m, gate.rows), dtype=torch.float32, device=x.device)
+    check(_get_lib().qraf_cuda_matvec_q_swiglu(C.byref(gate.desc), C.byref(up.desc), C.c_void_p(x2.data_ptr()),
+                                               C.c_void_p(h.data_ptr()), m, mode, _stream(stream)))
+    return h.reshape(gate.rows) if squeeze else h
 
 
 def dot_q(dtype: int, q, x, count: int, block_size: int = 32, mode: int = MODE_EXACT, stream=None):

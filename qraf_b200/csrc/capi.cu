@@ -209,20 +209,23 @@ bool rows_eligible(const qraf_weight_t& w, const float* x) {
 }
 
 // Plan one launch over `mcount` activation vectors.  Returns false when the
-// staged activations do not fit in shared memory.
+// staged activations do not fit in shared memory.  pairs: SwiGLU launch (the
+// rows are (gate, up) pairs; CTAs take whole pairs, stages hold one pair).
 bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount, bool exact, const DeviceInfo& dev,
-               RowPlan* out) {
+               RowPlan* out, bool pairs = false) {
     const uint32_t nblk = w.cols / 32;
     const uint64_t rb = w.row_bytes;
-    const uint32_t grid = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), w.rows);
-    const uint32_t rows_base = w.rows / grid, rows_extra = w.rows % grid;
-    const uint32_t max_rows = rows_base + (rows_extra ? 1u : 0u);
+    const uint32_t unit = pairs ? 2u : 1u, units = w.rows / unit;
+    const uint32_t grid = std::min<uint32_t>(static_cast<uint32_t>(dev.sm_count), units);
+    const uint32_t rows_base = units / grid, rows_extra = units % grid;   // in units of `unit` rows
+    const uint32_t max_rows = (rows_base + (rows_extra ? 1u : 0u)) * unit;
     const uint32_t bb = w.dtype == QRAF_DTYPE_Q8_0 ? 36u : 18u;
     uint32_t G = 1, piece = nblk, npieces = 1;
     // Rows per stage: enough stages to keep all warps busy, then as many rows as
     // fit ~18 KB (more rows share each staged activation block).  Whole rows.
     while (G < kRowGMax && (2 * G) * rb <= 18432 && 5 * ((max_rows + 2 * G - 1) / (2 * G)) >= 4 * kRowWarps) G *= 2;
     if (!exact && mcount == 2) G = 2;
+    if (pairs) G = 2;
     const bool long_rows = 2 * rb > 18432;   // not even 2 whole rows per stage
     if (!exact && long_rows) {
         // FAST, long rows: stages of 4 rows (2 for two vectors) x one piece of K, so
@@ -231,8 +234,8 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
         // order, at the end.  The pieces depend on K and the dtype only, so a row's
         // arithmetic is the same however the rows are spread over CTAs or GPUs
         // (row shards give the unsharded bits).
-        G = mcount == 2 ? 2u : 4u;
-        while (G > 1 && G > max_rows) G >>= 1;
+        G = (mcount == 2 || pairs) ? 2u : 4u;
+        while (!pairs && G > 1 && G > max_rows) G >>= 1;
         const uint32_t cap = 18432u / (4u * bb) / 8u * 8u;   // blocks per piece at 4 rows per ~18 KB stage
         npieces = (nblk + cap - 1) / cap;
         piece = ((nblk + npieces - 1) / npieces + 7u) / 8u * 8u;
@@ -278,6 +281,8 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.pb_row = pb_row;
     p.rows_base = rows_base;
     p.rows_extra = rows_extra;
+    p.row_unit = unit;
+    p.swiglu = 0;
     p.pdl = 0;
     p.xrec = nullptr;
     p.nseg = 0;
@@ -334,7 +339,9 @@ cudaError_t launch_rows(uint32_t dtype, const RowPlan& pl, bool exact, int MT, b
                                     : launch_rows_dt<kDtypeQ4>(pl, p, exact, MT, pdl, st);
 }
 
-int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what);
+// kind 0: the kernels' own scratch (one call at a time); kind 1: a buffer that
+// lives across the several launches of one call (the SwiGLU entry's up projection).
+int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what, int kind = 0);
 
 // FAST row kernel, with the activation limbs built once by limb_prep_kernel (into
 // the stream's scratch) when every CTA would otherwise spend a large share of its
@@ -477,14 +484,14 @@ struct TcScratch {
     std::vector<uint8_t*> retired;   // earlier areas of this stream, freed at shutdown
 };
 std::mutex g_scratch_mutex;
-std::map<std::pair<int, cudaStream_t>, TcScratch> g_scratch;
+std::map<std::tuple<int, cudaStream_t, int>, TcScratch> g_scratch;   // (device, stream, kind)
 
 // `what` names the path that needs the scratch, for the error message.
-int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what) {
+int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* what, int kind) {
     int dev = 0;
     QRAF_CUDA_TRY(cudaGetDevice(&dev));
     std::lock_guard<std::mutex> lk(g_scratch_mutex);
-    TcScratch& s = g_scratch[{dev, st}];
+    TcScratch& s = g_scratch[std::make_tuple(dev, st, kind)];
     if (s.bytes < bytes) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         QRAF_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
@@ -511,7 +518,7 @@ void tc_scratch_release() {
     int cur = 0;
     cudaGetDevice(&cur);
     for (auto& kv : g_scratch) {
-        cudaSetDevice(kv.first.first);
+        cudaSetDevice(std::get<0>(kv.first));
         cudaDeviceSynchronize();
         if (kv.second.base) cudaFree(kv.second.base);
         for (uint8_t* p : kv.second.retired) cudaFree(p);
@@ -1111,6 +1118,59 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
         const int rc = matvec_impl(&ws[i], x_dev, ys_dev[i], M, each, st);
         if (rc) return rc;
     }
+    return QRAF_OK;
+}
+
+int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, float* h_dev,
+                              uint32_t M, int mode_in, void* stream) {
+    int rc = check_weight(gate);
+    if (rc) return rc;
+    rc = check_weight(up);
+    if (rc) return rc;
+    if (gate->dtype != up->dtype || gate->block_size != up->block_size || gate->cols != up->cols ||
+        gate->rows != up->rows || gate->device != up->device)
+        return fail(QRAF_ERR_INVALID, "gate and up differ in dtype, block size, shape or device");
+    if (M == 0 || gate->rows == 0) return QRAF_OK;
+    if (!h_dev) return fail(QRAF_ERR_INVALID, "h is NULL");
+    if (gate->cols && !x_dev) return fail(QRAF_ERR_INVALID, "x is NULL");
+    const int mode = mode_in & 0xFF;
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC && mode != QRAF_MODE_AUTO)
+        return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
+    const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    DeviceInfo* dev = nullptr;
+    rc = ensure_device(nullptr, &dev);
+    if (rc) return rc;
+    // fused: FAST (AUTO) for one or two vectors on the row kernel, rows paired
+    const bool fast = mode == QRAF_MODE_FAST || (mode == QRAF_MODE_AUTO && M < kAutoTcMinVectors);
+    if (fast && M <= 2 && gate->cols > 0 && rows_eligible(*gate, x_dev) && rows_eligible(*up, x_dev) &&
+        gate->rows <= 0x7FFFFFFFu) {
+        qraf_weight_t v = *gate;   // the pairs as one virtual weight of 2 x rows
+        v.rows = 2u * gate->rows;
+        v.bytes = static_cast<uint64_t>(v.rows) * v.row_bytes;
+        RowPlan pl;
+        if (plan_rows(v, x_dev, nullptr, M, false, *dev, &pl, true)) {
+            RowParams& p = pl.p;
+            p.swiglu = 1;
+            p.nseg = 2;
+            p.seg_w[0] = static_cast<const uint8_t*>(gate->data);
+            p.seg_w[1] = static_cast<const uint8_t*>(up->data);
+            p.seg_y[0] = h_dev;
+            return launch_rows_fast(v.dtype, pl, static_cast<int>(M), overlap, st);
+        }
+    }
+    // otherwise the reference's steps: gate into h, up into a buffer, h = silu(h) * up
+    const size_t n = static_cast<size_t>(M) * gate->rows;
+    uint8_t* ubuf = nullptr;
+    rc = stream_scratch(st, n * sizeof(float), &ubuf, "the SwiGLU entry's up-projection buffer", 1);
+    if (rc) return rc;
+    rc = matvec_impl(gate, x_dev, h_dev, M, mode_in, st);
+    if (rc) return rc;
+    rc = matvec_impl(up, x_dev, reinterpret_cast<float*>(ubuf), M, mode_in, st);
+    if (rc) return rc;
+    const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev->sm_count));
+    swiglu_apply_kernel<<<grid, 256, 0, st>>>(h_dev, reinterpret_cast<const float*>(ubuf), n);
+    QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
 

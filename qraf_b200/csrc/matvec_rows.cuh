@@ -73,7 +73,8 @@ struct RowParams {
     uint32_t slot_stride;    // bytes per slot (multiple of 128)
     uint32_t xs_stride;      // bytes per staged activation vector: nblk * 144 (EXACT), nblk * kLimbRec (FAST)
     uint32_t pb_row;         // EXACT: floats per row of the per-warp partial buffer
-    uint32_t rows_base, rows_extra;
+    uint32_t rows_base, rows_extra;   // rows per CTA in units of row_unit rows: the first rows_extra CTAs take one more
+    uint32_t row_unit;       // 1, or 2 for paired (SwiGLU) rows
     uint32_t pdl;            // 1: programmatic dependent launch protocol
     const uint8_t* xrec;     // FAST: limb records built by limb_prep_kernel ([M][nblk] x kLimbRec), or null
     // Several weights of one input in one launch (nseg >= 2): virtual rows
@@ -84,6 +85,12 @@ struct RowParams {
     const uint8_t* seg_w[kMaxSeg];
     float* seg_y[kMaxSeg];
     uint32_t seg_row0[kMaxSeg + 1];
+    // SwiGLU pairs (swiglu = 1, FAST, two rows per stage): virtual row 2i is row i
+    // of the gate weight seg_w[0], 2i + 1 row i of the up weight seg_w[1]; the
+    // stage that holds both writes silu(gate) * up (the reference's
+    // x / (1 + exp(-x)), then the product: src/nn/ops.cpp:218-221,
+    // src/nn/attention.cpp:172-179) to seg_y[0][v][i] ([M][N / 2]).
+    uint32_t swiglu;
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
     // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
     // output element goes into this rank's y and, as one 8-byte word (call number
@@ -124,6 +131,7 @@ __device__ __forceinline__ uint32_t seg_of(const RowParams& p, uint32_t row) {
 
 // First byte of virtual row `row` in global memory.
 __device__ __forceinline__ const uint8_t* row_src(const RowParams& p, uint32_t row) {
+    if (p.swiglu) return p.seg_w[row & 1u] + static_cast<size_t>(row >> 1) * p.row_bytes;
     if (p.nseg <= 1) return p.w + static_cast<size_t>(row) * p.row_bytes;
     const uint32_t i = seg_of(p, row);
     return p.seg_w[i] + static_cast<size_t>(row - p.seg_row0[i]) * p.row_bytes;
@@ -148,6 +156,22 @@ __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uin
 #pragma unroll
     for (int r = 0; r < kMaxWorld; ++r)
         if (r < static_cast<int>(p.world) && r != static_cast<int>(p.rank)) st_relaxed_sys_u64(p.peer_ll[r] + off, word);
+}
+
+// SwiGLU output of the pair (gate, up) = virtual rows (2i, 2i + 1).
+__device__ __forceinline__ void store_swiglu(const RowParams& p, uint32_t v, uint32_t pair, float g, float u) {
+    const float act = g / (1.0f + expf(-g));
+    p.seg_y[0][static_cast<size_t>(v) * (p.N >> 1) + pair] = act * u;
+}
+
+// h = silu(h) * u, element by element (the SwiGLU entry's unfused path).
+__global__ void __launch_bounds__(256) swiglu_apply_kernel(float* __restrict__ h, const float* __restrict__ u,
+                                                           size_t n) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const float g = h[i];
+        h[i] = (g / (1.0f + expf(-g))) * u[i];
+    }
 }
 
 // Row-sharded completion, by every thread of every CTA: copy the other ranks'
@@ -533,8 +557,8 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         return;
     }
     const uint32_t c = blockIdx.x;
-    const uint32_t r0 = c * p.rows_base + min(c, p.rows_extra);
-    const uint32_t nrows = p.rows_base + (c < p.rows_extra ? 1u : 0u);
+    const uint32_t r0 = (c * p.rows_base + min(c, p.rows_extra)) * p.row_unit;
+    const uint32_t nrows = (p.rows_base + (c < p.rows_extra ? 1u : 0u)) * p.row_unit;
     const uint32_t nstages = (nrows + p.G - 1) / p.G * p.npieces;
     constexpr uint32_t kBlockBytes = DT == kDtypeQ8 ? 36u : 18u;
 
@@ -557,7 +581,11 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         if (p.npieces == 1) {   // whole rows: one copy (one per weight where the rows span several)
             const uint32_t bytes = rows * static_cast<uint32_t>(p.row_bytes);
             mbar_arrive_expect_tx(&full[slot], bytes);
-            if (p.nseg <= 1) {
+            if (p.swiglu) {         // a gate row and an up row: two copies
+                for (uint32_t i = 0; i < rows; ++i)
+                    bulk_g2s(dst + static_cast<size_t>(i) * p.row_bytes, row_src(p, a + i),
+                             static_cast<uint32_t>(p.row_bytes), &full[slot], pol);
+            } else if (p.nseg <= 1) {
                 bulk_g2s(dst, p.w + static_cast<size_t>(a) * p.row_bytes, bytes, &full[slot], pol);
             } else {
                 for (uint32_t i = 0; i < p.nseg; ++i) {
@@ -666,16 +694,23 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
             }
             __syncwarp();
             if (lane == 0 && s + nst < nstages) issue(s + nst, slot);   // the slot's bytes are no longer read
+            float tsum[GT][MT];
 #pragma unroll
-            for (int g = 0; g < GT; ++g) {
+            for (int g = 0; g < GT; ++g)
 #pragma unroll
-                for (int v = 0; v < MT; ++v) {
-                    const float t = warp_sum(racc[g][v]);
-                    if (lane == 0 && g < static_cast<int>(rows_s)) {
-                        if (p.npieces == 1)
-                            store_out(p, call, v, row0 + g, t);
+                for (int v = 0; v < MT; ++v) tsum[g][v] = warp_sum(racc[g][v]);
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g < GT; ++g) {
+#pragma unroll
+                    for (int v = 0; v < MT; ++v) {
+                        if (g >= static_cast<int>(rows_s)) continue;
+                        if (p.npieces > 1)
+                            part[(static_cast<size_t>(v) * p.part_rows + (row0 - r0 + g)) * p.npieces + pc] = tsum[g][v];
+                        else if (p.swiglu)
+                            { if (GT == 2 && g == 1) store_swiglu(p, v, row0 >> 1, tsum[0][v], tsum[GT - 1][v]); }
                         else
-                            part[(static_cast<size_t>(v) * p.part_rows + (row0 - r0 + g)) * p.npieces + pc] = t;
+                            store_out(p, call, v, row0 + g, tsum[g][v]);
                     }
                 }
             }
@@ -731,13 +766,21 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     if constexpr (!EXACT) {
         if (p.npieces > 1) {   // rows summed piece by piece, in order
             __syncthreads();
-            const uint32_t total = p.M * nrows;
+            const uint32_t per = p.swiglu ? nrows >> 1 : nrows;   // outputs per vector: rows, or pairs
+            const uint32_t total = p.M * per;
             for (uint32_t i = threadIdx.x; i < total; i += kRowThreads) {
-                const uint32_t v = i / nrows, rl = i - v * nrows;
+                const uint32_t v = i / per, k = i - v * per;
+                const uint32_t rl = p.swiglu ? 2u * k : k;
                 const float* pr = part + (static_cast<size_t>(v) * p.part_rows + rl) * p.npieces;
                 float t = 0.0f;
                 for (uint32_t q = 0; q < p.npieces; ++q) t += pr[q];
-                store_out(p, call, v, r0 + rl, t);
+                if (!p.swiglu) {
+                    store_out(p, call, v, r0 + rl, t);
+                    continue;
+                }
+                float u = 0.0f;
+                for (uint32_t q = 0; q < p.npieces; ++q) u += pr[p.npieces + q];
+                store_swiglu(p, v, (r0 + rl) >> 1, t, u);
             }
         }
     }
