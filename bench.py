@@ -462,12 +462,16 @@ TOKEN_MODELS = {
                          ("o", 2048, 2048, "q"), ("gate", 11008, 2048, "o"), ("up", 11008, 2048, "o"),
                          ("down", 2048, 11008, "gate")],
                # projections of one input in the model (attention.cpp:92-97, :172-174): one launch each
-               "groups": [("q", "k", "v"), ("gate", "up")]},
+               "groups": [("q", "k", "v"), ("gate", "up")],
+               # RMSNorm before the attention and MLP inputs (transformer.cpp:588-590, :596-597);
+               # Qwen2's Q, K and V biases (attention.cpp:100-102)
+               "norm_before": ("q", "gate"), "biased": ("q", "k", "v")},
     # 70B shapes (config 5), Q4_0: fused QKV 10240, gate/up 28672, down, LM head 128256.
     "llama70b": {"dtype": Q4, "layers": 80, "hidden": 8192, "vocab": 128256,
                  "projs": [("qkv", 10240, 8192, "h"), ("gate", 28672, 8192, "h"), ("up", 28672, 8192, "h"),
                            ("down", 8192, 28672, "gate")],
-                 "groups": [("gate", "up")]},
+                 "groups": [("gate", "up")],
+                 "norm_before": ("qkv", "gate"), "biased": ()},
 }
 # The payload digests of the reference quantizer (tests/golden/config_digests.json)
 # for each projection shape of the token workloads.
@@ -899,27 +903,45 @@ def run_token(args, model, m):
         return g.view(1, n) if m == 1 else g.view(world, m, rows).permute(1, 0, 2).reshape(m, n)
 
     # projections of one input go in one launch (qraf_cuda_matvec_q_multi) on one GPU;
-    # gate and up as one SwiGLU launch (qraf_cuda_matvec_q_swiglu: down reads silu(gate) * up)
+    # gate and up as one SwiGLU launch (qraf_cuda_matvec_q_swiglu: down reads silu(gate) * up);
+    # the RMSNorms before them and Qwen2's Q/K/V biases folded into those launches
     multi = world == 1 and args.multi
     first_of = {g[0]: g for g in spec.get("groups", [])} if multi else {}
     in_group = {name for g in first_of.values() for name in g}
     swiglu = multi and args.swiglu
+    fuse = swiglu and args.norms
+    norms, bias = {}, {}
+    if fuse:
+        gen = torch.Generator().manual_seed(45)
+        for l in range(spec["layers"]):
+            for name in spec["norm_before"]:
+                norms[(l, name)] = (1.0 + 0.1 * torch.randn(hidden, generator=gen)).to(dev)
+            for name, n, k, _ in projs:
+                if name in spec["biased"]:
+                    bias[(l, name)] = (0.1 * torch.randn(n, generator=gen)).to(dev)
 
     def token():
         vals = {"h": h0}
         for l in range(spec["layers"]):
             ws = {name: w for (name, _, _, _), w in zip(projs, weights[l])}
             for name, n, k, src in projs:
+                nw = norms.get((l, name))
                 if name in first_of:
                     g = first_of[name]
                     if swiglu and g == ("gate", "up"):
                         vals["gate"] = qb.matvec_q_swiglu(ws["gate"], ws["up"], vals[src], ybuf["gate"],
-                                                          mode=launch_mode)
+                                                          mode=launch_mode, norm_w=nw)
                         continue
-                    outs = qb.matvec_q_multi([ws[x] for x in g], vals[src], [ybuf[x] for x in g], mode=launch_mode)
+                    bs = [bias.get((l, x)) for x in g] if any((l, x) in bias for x in g) else None
+                    outs = qb.matvec_q_multi([ws[x] for x in g], vals[src], [ybuf[x] for x in g], mode=launch_mode,
+                                             norm_w=nw, biases=bs)
                     vals.update(zip(g, outs))
                 elif name not in in_group:
-                    vals[name] = project(name, n, k, ws[name], vals[src])
+                    if nw is not None or (l, name) in bias:
+                        vals[name] = qb.matvec_q_multi([ws[name]], vals[src], [ybuf[name]], mode=launch_mode,
+                                                       norm_w=nw, biases=[bias.get((l, name))])[0]
+                    else:
+                        vals[name] = project(name, n, k, ws[name], vals[src])
             vals["h"] = vals["down"]
         return project("lm_head", vocab, hidden, w_lm, vals["h"])
 
@@ -1000,6 +1022,9 @@ def run_token(args, model, m):
                        "quant": "Q4_0" if dt == Q4 else "Q8_0", "mode": args.mode, "calls_per_token": calls,
                        "mlp": "silu(gate) * up fused into the gate/up launch; down reads it" if swiglu
                        else "down reads gate (no activation on the path)",
+                       "norms": "RMSNorm folded into the QKV and gate/up launches" + (", Q/K/V biases folded in"
+                                                                                     if spec["biased"] else "")
+                       if fuse else "none on the path",
                        "weight_bytes_per_token": total_weight_bytes,
                        "parallelism": (f"rows split over {world} GPUs, all-gather "
                                        f"{'fused into the kernel (NVLink peer stores)' if fused else 'by NCCL'}")
@@ -1084,6 +1109,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
+    ap.add_argument("--no-norms", dest="norms", action="store_false",
+                    help="token workloads on one GPU: no RMSNorm / bias folded into the projections")
     ap.add_argument("--no-swiglu", dest="swiglu", action="store_false",
                     help="token workloads on one GPU: gate and up as a plain two-weight launch, down reading gate "
                          "(default: one SwiGLU launch, down reading silu(gate) * up)")

@@ -135,6 +135,21 @@ int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev,
 int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
                              uint32_t M, int mode, void* stream);
 
+/* qraf_cuda_matvec_q_multi with the steps the reference runs around those
+ * projections folded in: norm_w (non-NULL) replaces X[m] by
+ * RMSNorm(X[m]) = X[m] * (1 / sqrt(mean(X[m]^2) + norm_eps)) * norm_w first
+ * (dispatch_rms_norm, src/nn/backend.cpp:203-223 / src/nn/ops.cpp:107-118, as
+ * src/nn/transformer.cpp:588-590 runs it before Q, K and V); biases[i]
+ * (non-NULL array, entries may be NULL) is added to weight i's outputs,
+ * fl(y + b) (src/nn/attention.cpp:100-102).  FAST (M <= 2) folds both into the
+ * one launch (RMSNorm's sum of squares in fp64 by every CTA); EXACT folds the
+ * biases and runs RMSNorm first in the reference's order, so its results are
+ * the reference's bits; other modes run the steps around the projections.  x is
+ * not modified. */
+int qraf_cuda_matvec_q_multi_ex(const qraf_weight_t* ws, uint32_t count, const float* x_dev, const float* norm_w,
+                                float norm_eps, const float* const* biases, float* const* ys_dev, uint32_t M, int mode,
+                                void* stream);
+
 /* SwiGLU of one input: h[m][i] = silu((W_gate X[m])[i]) * (W_up X[m])[i], with
  * silu(g) = g / (1 + exp(-g)) - the reference's gate and up projections, silu and
  * product (mlp_forward, src/nn/attention.cpp:172-179; silu_inplace,
@@ -147,6 +162,11 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
  * expf (within 2 ulp of the C library's). */
 int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, float* h_dev,
                               uint32_t M, int mode, void* stream);
+/* The same after an RMSNorm of x (norm_w, norm_eps as in qraf_cuda_matvec_q_multi_ex;
+ * src/nn/transformer.cpp:597-600 normalises before the MLP): one launch in FAST. */
+int qraf_cuda_matvec_q_swiglu_ex(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev,
+                                 const float* norm_w, float norm_eps, float* h_dev, uint32_t M, int mode,
+                                 void* stream);
 
 /* The tensor-core path of qraf_cuda_matvec_q (QRAF_MODE_TC, same kernels and
  * results) for callers that may not allocate device memory: its scratch (the

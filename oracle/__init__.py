@@ -82,6 +82,8 @@ class Oracle:
         lib.qo_matvec_q_f64.restype = None
         lib.qo_matvec_q_f64.argtypes = [_u8p, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, _f32p, _f64p]
         lib.qo_limb_partials.restype = None
+        lib.qo_rms_norm.restype = None
+        lib.qo_rms_norm.argtypes = [_f32p, _f32p, C.c_int, C.c_float]
         lib.qo_limb_partials.argtypes = [_u8p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p,
                                          np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"), _f32p]
         self.lib = lib
@@ -151,6 +153,11 @@ class Oracle:
                                   np.ascontiguousarray(x, dtype=np.float32).ravel(), d.reshape(-1), c)
         return d, c
 
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        out = np.array(x, dtype=np.float32, copy=True).ravel()
+        self.lib.qo_rms_norm(out, np.ascontiguousarray(w, dtype=np.float32).ravel(), out.size, eps)
+        return out
+
     def matvec_f64(self, dtype: int, w: np.ndarray, n: int, k: int, x: np.ndarray, bs: int = 32):
         y = np.zeros(n, dtype=np.float64)
         self.lib.qo_matvec_q_f64(np.ascontiguousarray(w, dtype=np.uint8).ravel(), dtype, bs, n, k,
@@ -185,6 +192,8 @@ class Reference:
         lib.qref_fp16_to_fp32.argtypes = [C.c_uint16]
         lib.qref_fill_normal.restype = None
         lib.qref_fill_normal.argtypes = [C.c_uint32, C.c_float, C.c_float, _f32p, C.c_size_t]
+        lib.qref_rms_norm.restype = None
+        lib.qref_rms_norm.argtypes = [_f32p, _f32p, C.c_int, C.c_float]
         vp, cp = C.c_void_p, C.c_char_p
         for name, res, args in (
                 ("qref_writer_new", vp, []), ("qref_writer_free", None, [vp]),
@@ -254,6 +263,11 @@ class Reference:
                                            np.ascontiguousarray(x, dtype=np.float32).ravel(), y)
         return y
 
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        out = np.array(x, dtype=np.float32, copy=True).ravel()
+        self.lib.qref_rms_norm(out, np.ascontiguousarray(w, dtype=np.float32).ravel(), out.size, eps)
+        return out
 
     def write_qraf(self, path: str, config=(), tensors=(), schemes=(), vocab=None, merges=(), special=None) -> None:
         """The reference's QrafWriter (src/qraf/writer.cpp): config = [(key, value)]

@@ -385,3 +385,21 @@ void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, con
     }
     free(L);
 }
+
+/* RMSNorm in place, src/nn/ops.cpp:107-118 (rms_norm_inplace, the Linux path of
+ * dispatch_rms_norm): a running fp32 sum of fl(x*x), fl(fl(ss / size) + eps),
+ * r = fl(1 / sqrt), then x = fl(fl(x * r) * w). */
+void qo_rms_norm(float* x, const float* w, int size, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < size; i++) {
+        const float sq = x[i] * x[i];
+        ss = ss + sq;
+    }
+    ss = ss / (float)size + eps;
+    const float r = 1.0f / sqrtf(ss);
+    for (int i = 0; i < size; i++) {
+        const float t = x[i] * r;
+        x[i] = t * w[i];
+    }
+}
+

@@ -84,6 +84,9 @@ void qo_matvec_q_f64(const void* w, uint32_t dtype, int block_size, uint32_t N, 
  * digits -128 <= L_j <= 127; D[n][b][j] = sum_i q_i * L_j,i with the true codes q
  * (Q8: int8, Q4: nibble - 8); c[b] = 2^(e_b - 30) (0 for an all-zero block).  A
  * block that holds a NaN or an infinity gets zero digits and c = NaN. */
+/* RMSNorm in place (src/nn/ops.cpp:107-118). */
+void qo_rms_norm(float* x, const float* w, int size, float eps);
+
 void qo_limb_partials(const void* w, uint32_t dtype, uint32_t N, uint32_t K, const float* x, int32_t* D,
                       float* c);
 

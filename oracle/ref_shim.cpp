@@ -128,6 +128,8 @@ void qref_mlp_forward(float* out, const float* x, const void* w_gate, const void
 
 // fp32_to_fp16 / fp16_to_fp32 (src/tensor/dtype.cpp:9-59).
 uint16_t qref_fp32_to_fp16(float f) { return fp32_to_fp16(f); }
+// ops::rms_norm_inplace (src/nn/ops.cpp:107-118), in place.
+void qref_rms_norm(float* x, const float* w, int size, float eps) { ops::rms_norm_inplace(x, w, size, eps); }
 float qref_fp16_to_fp32(uint16_t h) { return fp16_to_fp32(h); }
 
 // The reference's own .qraf writer (src/qraf/writer.cpp, QrafWriter) and loader

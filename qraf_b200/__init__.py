@@ -82,6 +82,8 @@ def _load() -> C.CDLL:
         "qraf_cuda_matvec_q": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_matvec_q_multi": (i32, [W, u32, vp, C.POINTER(vp), u32, i32, vp]),
         "qraf_cuda_matvec_q_swiglu": (i32, [W, W, vp, vp, u32, i32, vp]),
+        "qraf_cuda_matvec_q_multi_ex": (i32, [W, u32, vp, vp, C.c_float, C.POINTER(vp), C.POINTER(vp), u32, i32, vp]),
+        "qraf_cuda_matvec_q_swiglu_ex": (i32, [W, W, vp, vp, C.c_float, vp, u32, i32, vp]),
         "qraf_cuda_matmul_tc_noalloc": (i32, [W, vp, vp, u32, i32, vp]),
         "qraf_cuda_dot_q": (i32, [u32, vp, vp, u64, u32, vp, i32, vp]),
         "qraf_cuda_block_partials": (i32, [W, vp, vp, vp]),
@@ -311,10 +313,13 @@ def matvec_q(w: Weight, x, y=None, mode: int = MODE_AUTO, stream=None):
 MULTI_MAX_WEIGHTS = 4
 
 
-def matvec_q_multi(weights, x, ys=None, mode: int = MODE_AUTO, stream=None):
+def matvec_q_multi(weights, x, ys=None, mode: int = MODE_AUTO, stream=None, norm_w=None, norm_eps: float = 1e-6,
+                   biases=None):
     """[W_i X for each weight] in one launch (qraf_cuda_matvec_q_multi): projections of
     the same activations, e.g. a layer's Q, K and V, or gate and up.  Returns the list
-    of outputs ([M, rows_i] each, or [rows_i] for a 1-D x)."""
+    of outputs ([M, rows_i] each, or [rows_i] for a 1-D x).  norm_w: RMSNorm of x
+    first; biases: per-weight bias tensors (or None entries) added to the outputs
+    (qraf_cuda_matvec_q_multi_ex)."""
     torch = _torch()
     if not 1 <= len(weights) <= MULTI_MAX_WEIGHTS:
         raise ValueError(f"1 to {MULTI_MAX_WEIGHTS} weights")
@@ -327,12 +332,21 @@ def matvec_q_multi(weights, x, ys=None, mode: int = MODE_AUTO, stream=None):
         ys = [torch.empty((m, w.rows), dtype=torch.float32, device=x.device) for w in weights]
     descs = (qraf_weight_t * len(weights))(*[w.desc for w in weights])
     outs = (C.c_void_p * len(weights))(*[y.data_ptr() for y in ys])
-    check(_get_lib().qraf_cuda_matvec_q_multi(descs, len(weights), C.c_void_p(x2.data_ptr()), outs, m, mode,
-                                              _stream(stream)))
+    if norm_w is None and biases is None:
+        check(_get_lib().qraf_cuda_matvec_q_multi(descs, len(weights), C.c_void_p(x2.data_ptr()), outs, m, mode,
+                                                  _stream(stream)))
+    else:
+        bs = None
+        if biases is not None:
+            bs = (C.c_void_p * len(weights))(*[b.data_ptr() if b is not None else None for b in biases])
+        check(_get_lib().qraf_cuda_matvec_q_multi_ex(
+            descs, len(weights), C.c_void_p(x2.data_ptr()), C.c_void_p(norm_w.data_ptr() if norm_w is not None else 0),
+            norm_eps, bs, outs, m, mode, _stream(stream)))
     return [y.reshape(w.rows) for y, w in zip(ys, weights)] if squeeze else ys
 
 
-def matvec_q_swiglu(gate: Weight, up: Weight, x, h=None, mode: int = MODE_AUTO, stream=None):
+def matvec_q_swiglu(gate: Weight, up: Weight, x, h=None, mode: int = MODE_AUTO, stream=None, norm_w=None,
+                    norm_eps: float = 1e-6):
     """silu(W_gate X) * (W_up X) (qraf_cuda_matvec_q_swiglu): one launch in FAST / AUTO
     for one or two vectors.  Returns [M, rows] (or [rows] for a 1-D x)."""
     torch = _torch()
@@ -343,8 +357,13 @@ def matvec_q_swiglu(gate: Weight, up: Weight, x, h=None, mode: int = MODE_AUTO, 
     m = x2.shape[0]
     if h is None:
         h = torch.empty((m, gate.rows), dtype=torch.float32, device=x.device)
-    check(_get_lib().qraf_cuda_matvec_q_swiglu(C.byref(gate.desc), C.byref(up.desc), C.c_void_p(x2.data_ptr()),
-                                               C.c_void_p(h.data_ptr()), m, mode, _stream(stream)))
+    if norm_w is None:
+        check(_get_lib().qraf_cuda_matvec_q_swiglu(C.byref(gate.desc), C.byref(up.desc), C.c_void_p(x2.data_ptr()),
+                                                   C.c_void_p(h.data_ptr()), m, mode, _stream(stream)))
+    else:
+        check(_get_lib().qraf_cuda_matvec_q_swiglu_ex(C.byref(gate.desc), C.byref(up.desc),
+                                                      C.c_void_p(x2.data_ptr()), C.c_void_p(norm_w.data_ptr()),
+                                                      norm_eps, C.c_void_p(h.data_ptr()), m, mode, _stream(stream)))
     return h.reshape(gate.rows) if squeeze else h
 
 

@@ -255,7 +255,7 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
         slot_stride = static_cast<uint32_t>(((npieces == 1 ? G * rb : static_cast<uint64_t>(G) * piece_bytes) + 127) / 128 * 128);
         const uint64_t part_bytes = npieces > 1 ? ((static_cast<uint64_t>(mcount) * max_rows * npieces + 1) & ~1ull) * 4u : 0;
         const uint32_t stages = (max_rows + G - 1) / G * npieces;
-        fixed = x_bytes + pb_bytes + part_bytes + 64;
+        fixed = x_bytes + pb_bytes + part_bytes + 64 + 272;   // + the RMSNorm reduction buffer
         nst = budget <= fixed ? 0u
                               : static_cast<uint32_t>(std::min<uint64_t>({32u, stages, (budget - fixed) / (slot_stride + 12u)}));
     };
@@ -283,6 +283,9 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.rows_extra = rows_extra;
     p.row_unit = unit;
     p.swiglu = 0;
+    p.norm_w = nullptr;
+    p.norm_eps = 0.0f;
+    for (int i = 0; i < kMaxSeg; ++i) p.seg_b[i] = nullptr;
     p.pdl = 0;
     p.xrec = nullptr;
     p.nseg = 0;
@@ -367,7 +370,8 @@ int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStre
         cfg.blockDim = dim3(256);
         cfg.stream = st;
         const cudaError_t e = cudaLaunchKernelEx(&cfg, dtype == QRAF_DTYPE_Q8_0 ? limb_prep_kernel<kDtypeQ8> : limb_prep_kernel<kDtypeQ4>,
-                                                 pl.p.x, pl.p.K, pl.p.M, pl.p.nblk, recs, overlap ? 1u : 0u);
+                                                 pl.p.x, pl.p.K, pl.p.M, pl.p.nblk, recs, overlap ? 1u : 0u,
+                                                 pl.p.norm_w, pl.p.norm_eps);
         if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "limb prep launch: %s", cudaGetErrorString(e));
         pl.p.xrec = recs;
         overlap = true;   // the row kernel waits for the prep kernel, not for the one before it
@@ -1039,8 +1043,61 @@ int qraf_cuda_matvec_q(const qraf_weight_t* w, const float* x_dev, float* y_dev,
 
 static_assert(QRAF_MULTI_MAX_WEIGHTS == kMaxSeg, "the header's weight limit is the kernel's segment count");
 
-int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
-                             uint32_t M, int mode_in, void* stream) {
+// x_out[m] = RMSNorm(x[m]) for the unfused paths (one CTA per vector): with
+// `exact` one thread sums the squares in the reference's order, so the result
+// is the reference's bits (src/nn/ops.cpp:107-118); otherwise the CTA's fp64 sum.
+static __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps,
+                                                      uint32_t K, float* __restrict__ out, int exact) {
+    __shared__ double red[33];
+    const float* xm = x + static_cast<size_t>(blockIdx.x) * K;
+    float* om = out + static_cast<size_t>(blockIdx.x) * K;
+    float r;
+    if (exact) {
+        if (threadIdx.x == 0) {
+            float ss = 0.0f;
+            for (uint32_t i = 0; i < K; ++i) ss = __fadd_rn(ss, __fmul_rn(xm[i], xm[i]));
+            const float m = __fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps);
+            red[32] = static_cast<double>(__fdiv_rn(1.0f, __fsqrt_rn(m)));
+        }
+        __syncthreads();
+        r = static_cast<float>(red[32]);
+    } else {
+        r = rms_factor(xm, K, eps, red);
+    }
+    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) om[i] = __fmul_rn(__fmul_rn(xm[i], r), w[i]);
+}
+
+// y[m][r] = fl(y[m][r] + b[r]) for the unfused paths.
+static __global__ void __launch_bounds__(256) bias_add_kernel(float* __restrict__ y, const float* __restrict__ b, uint32_t rows,
+                                                       size_t n) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        y[i] = __fadd_rn(y[i], b[i % rows]);
+}
+
+// RMSNorm of x into a per-stream buffer (lives across the launches of one call).
+static int normalize_into_scratch(const float* x, const float* norm_w, float eps, uint32_t K, uint32_t M, bool exact,
+                           cudaStream_t st, const float** out) {
+    uint8_t* buf = nullptr;
+    const int rc = stream_scratch(st, static_cast<size_t>(M) * K * sizeof(float), &buf,
+                                  "the normalised activations of a fused call", 2);
+    if (rc) return rc;
+    rmsnorm_kernel<<<M, 256, 0, st>>>(x, norm_w, eps, K, reinterpret_cast<float*>(buf), exact ? 1 : 0);
+    QRAF_CUDA_TRY(cudaGetLastError());
+    *out = reinterpret_cast<const float*>(buf);
+    return QRAF_OK;
+}
+
+static int add_bias(float* y, const float* b, uint32_t rows, uint32_t M, const DeviceInfo& dev, cudaStream_t st) {
+    const size_t n = static_cast<size_t>(M) * rows;
+    const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev.sm_count));
+    if (n) bias_add_kernel<<<grid, 256, 0, st>>>(y, b, rows, n);
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+static int multi_impl(const qraf_weight_t* ws, uint32_t count, const float* x_dev, const float* norm_w, float eps,
+                      const float* const* biases, float* const* ys_dev, uint32_t M, int mode_in, void* stream) {
     if (!ws || !ys_dev || count == 0 || count > static_cast<uint32_t>(kMaxSeg))
         return fail(QRAF_ERR_INVALID, "multi call needs 1 to %d weights and their outputs", kMaxSeg);
     for (uint32_t i = 0; i < count; ++i) {
@@ -1057,49 +1114,70 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
     const bool auto_mode = mode == QRAF_MODE_AUTO;
     if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(ws[0])) ? QRAF_MODE_TC : QRAF_MODE_FAST;
     const bool exact = mode == QRAF_MODE_EXACT;
+    bool any_bias = false;
+    for (uint32_t i = 0; biases && i < count; ++i) any_bias = any_bias || biases[i] != nullptr;
+    const bool fusion = norm_w != nullptr || any_bias;
+    if (M == 0) return QRAF_OK;
+    if (norm_w && (ws[0].cols % 8u) != 0) return fail(QRAF_ERR_INVALID, "RMSNorm needs K a multiple of 8");
     DeviceInfo* dev = nullptr;
+    int rc = ensure_device(nullptr, &dev);
+    if (rc) return rc;
     bool tc1_any = false;   // a weight that a call of its own would run on the batch-1 tensor-core kernel
     if (M == 1 && mode == QRAF_MODE_TC && x_dev) {
-        int rc = ensure_device(nullptr, &dev);
-        if (rc) return rc;
         Tc1Plan t1;
-        if (plan_tc1(ws, count, x_dev, ys_dev, *dev, &t1)) return launch_tc1(ws[0].dtype, t1, overlap, st);
-        for (uint32_t i = 0; i < count && !tc1_any; ++i) tc1_any = ws[i].rows > 0 && plan_tc1(&ws[i], 1, x_dev, &ys_dev[i], *dev, &t1);
+        if (!fusion && plan_tc1(ws, count, x_dev, ys_dev, *dev, &t1)) return launch_tc1(ws[0].dtype, t1, overlap, st);
+        for (uint32_t i = 0; i < count && !tc1_any; ++i)
+            tc1_any = ws[i].rows > 0 && plan_tc1(&ws[i], 1, x_dev, &ys_dev[i], *dev, &t1);
     }
     uint64_t total = 0;
     // fused on the row kernel only where each weight alone would run there too, so
     // that the fused launch gives the separate calls' bits
-    bool eligible = (exact || (mode == QRAF_MODE_FAST && M <= 2)) && !tc1_any && count > 1 && M > 0 &&
+    bool eligible = (exact || (mode == QRAF_MODE_FAST && M <= 2)) && !tc1_any && (count > 1 || fusion) && M > 0 &&
                     ws[0].cols > 0 && x_dev;
     for (uint32_t i = 0; i < count && eligible; ++i) {
         eligible = ws[i].rows > 0 && rows_eligible(ws[i], x_dev);
         total += ws[i].rows;
     }
     if (eligible && total <= 0xFFFFFFFFull) {
-        int rc = ensure_device(nullptr, &dev);
-        if (rc) return rc;
+        const float* x_in = x_dev;
+        const float* fused_norm = norm_w;
+        if (norm_w && exact) {   // EXACT normalises first, in the reference's order
+            rc = normalize_into_scratch(x_dev, norm_w, eps, ws[0].cols, M, true, st, &x_in);
+            if (rc) return rc;
+            fused_norm = nullptr;
+        }
         qraf_weight_t v = ws[0];   // the weights as one virtual row range
         v.rows = static_cast<uint32_t>(total);
         v.bytes = total * v.row_bytes;
         uint32_t per = M;
         RowPlan pl;
-        while (per > 1 && !plan_rows(v, x_dev, nullptr, per, exact, *dev, &pl)) per = (per + 1) / 2;
-        if (plan_rows(v, x_dev, nullptr, per, exact, *dev, &pl)) {
+        while (per > 1 && !plan_rows(v, x_in, nullptr, per, exact, *dev, &pl)) per = (per + 1) / 2;
+        if (plan_rows(v, x_in, nullptr, per, exact, *dev, &pl)) {
             for (uint32_t m0 = 0; m0 < M; m0 += per) {
                 RowPlan one = pl;
                 RowParams& p = one.p;
                 const uint32_t cnt = std::min(per, M - m0);
-                p.x = x_dev + static_cast<size_t>(m0) * v.cols;
+                p.x = x_in + static_cast<size_t>(m0) * v.cols;
                 p.M = cnt;
-                p.nseg = count;
-                uint32_t row0 = 0;
-                for (uint32_t i = 0; i < count; ++i) {
-                    p.seg_w[i] = static_cast<const uint8_t*>(ws[i].data);
-                    p.seg_y[i] = ys_dev[i] + static_cast<size_t>(m0) * ws[i].rows;
-                    p.seg_row0[i] = row0;
-                    row0 += ws[i].rows;
+                p.norm_w = fused_norm;
+                p.norm_eps = eps;
+                if (count == 1) {
+                    p.nseg = 1;
+                    p.w = static_cast<const uint8_t*>(ws[0].data);
+                    p.y = ys_dev[0] + static_cast<size_t>(m0) * ws[0].rows;
+                    p.seg_b[0] = biases ? biases[0] : nullptr;
+                } else {
+                    p.nseg = count;
+                    uint32_t row0 = 0;
+                    for (uint32_t i = 0; i < count; ++i) {
+                        p.seg_w[i] = static_cast<const uint8_t*>(ws[i].data);
+                        p.seg_y[i] = ys_dev[i] + static_cast<size_t>(m0) * ws[i].rows;
+                        p.seg_b[i] = biases ? biases[i] : nullptr;
+                        p.seg_row0[i] = row0;
+                        row0 += ws[i].rows;
+                    }
+                    for (uint32_t i = count; i <= static_cast<uint32_t>(kMaxSeg); ++i) p.seg_row0[i] = row0;
                 }
-                for (uint32_t i = count; i <= static_cast<uint32_t>(kMaxSeg); ++i) p.seg_row0[i] = row0;
                 const bool ov = overlap || m0 > 0;
                 if (exact) {
                     const cudaError_t e = launch_rows(v.dtype, one, true, 1, ov, st);
@@ -1112,17 +1190,38 @@ int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const floa
             return QRAF_OK;
         }
     }
-    // otherwise: one call per weight (same results as the fused launch would give)
+    // otherwise: one call per weight (same results as the fused launch would give),
+    // around an RMSNorm pass and bias passes where the call asks for them
+    const float* x_in = x_dev;
+    if (norm_w) {
+        rc = normalize_into_scratch(x_dev, norm_w, eps, ws[0].cols, M, exact, st, &x_in);
+        if (rc) return rc;
+    }
     const int each = (auto_mode ? QRAF_MODE_AUTO : mode) | (overlap ? QRAF_MODE_FLAG_OVERLAP : 0);
     for (uint32_t i = 0; i < count; ++i) {
-        const int rc = matvec_impl(&ws[i], x_dev, ys_dev[i], M, each, st);
+        rc = matvec_impl(&ws[i], x_in, ys_dev[i], M, each, st);
         if (rc) return rc;
+        if (biases && biases[i]) {
+            rc = add_bias(ys_dev[i], biases[i], ws[i].rows, M, *dev, st);
+            if (rc) return rc;
+        }
     }
     return QRAF_OK;
 }
 
-int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, float* h_dev,
-                              uint32_t M, int mode_in, void* stream) {
+int qraf_cuda_matvec_q_multi(const qraf_weight_t* ws, uint32_t count, const float* x_dev, float* const* ys_dev,
+                             uint32_t M, int mode, void* stream) {
+    return multi_impl(ws, count, x_dev, nullptr, 0.0f, nullptr, ys_dev, M, mode, stream);
+}
+
+int qraf_cuda_matvec_q_multi_ex(const qraf_weight_t* ws, uint32_t count, const float* x_dev, const float* norm_w,
+                                float norm_eps, const float* const* biases, float* const* ys_dev, uint32_t M, int mode,
+                                void* stream) {
+    return multi_impl(ws, count, x_dev, norm_w, norm_eps, biases, ys_dev, M, mode, stream);
+}
+
+static int swiglu_impl(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, const float* norm_w,
+                       float eps, float* h_dev, uint32_t M, int mode_in, void* stream) {
     int rc = check_weight(gate);
     if (rc) return rc;
     rc = check_weight(up);
@@ -1133,6 +1232,7 @@ int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up
     if (M == 0 || gate->rows == 0) return QRAF_OK;
     if (!h_dev) return fail(QRAF_ERR_INVALID, "h is NULL");
     if (gate->cols && !x_dev) return fail(QRAF_ERR_INVALID, "x is NULL");
+    if (norm_w && (gate->cols % 8u) != 0) return fail(QRAF_ERR_INVALID, "RMSNorm needs K a multiple of 8");
     const int mode = mode_in & 0xFF;
     if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC && mode != QRAF_MODE_AUTO)
         return fail(QRAF_ERR_INVALID, "unknown mode %d", mode_in);
@@ -1156,22 +1256,40 @@ int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up
             p.seg_w[0] = static_cast<const uint8_t*>(gate->data);
             p.seg_w[1] = static_cast<const uint8_t*>(up->data);
             p.seg_y[0] = h_dev;
+            p.norm_w = norm_w;
+            p.norm_eps = eps;
             return launch_rows_fast(v.dtype, pl, static_cast<int>(M), overlap, st);
         }
     }
-    // otherwise the reference's steps: gate into h, up into a buffer, h = silu(h) * up
+    // otherwise the reference's steps: [RMSNorm,] gate into h, up into a buffer, h = silu(h) * up
+    const float* x_in = x_dev;
+    if (norm_w) {
+        rc = normalize_into_scratch(x_dev, norm_w, eps, gate->cols, M, mode == QRAF_MODE_EXACT, st, &x_in);
+        if (rc) return rc;
+    }
     const size_t n = static_cast<size_t>(M) * gate->rows;
     uint8_t* ubuf = nullptr;
     rc = stream_scratch(st, n * sizeof(float), &ubuf, "the SwiGLU entry's up-projection buffer", 1);
     if (rc) return rc;
-    rc = matvec_impl(gate, x_dev, h_dev, M, mode_in, st);
+    rc = matvec_impl(gate, x_in, h_dev, M, mode_in, st);
     if (rc) return rc;
-    rc = matvec_impl(up, x_dev, reinterpret_cast<float*>(ubuf), M, mode_in, st);
+    rc = matvec_impl(up, x_in, reinterpret_cast<float*>(ubuf), M, mode_in, st);
     if (rc) return rc;
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev->sm_count));
     swiglu_apply_kernel<<<grid, 256, 0, st>>>(h_dev, reinterpret_cast<const float*>(ubuf), n);
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
+}
+
+int qraf_cuda_matvec_q_swiglu(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev, float* h_dev,
+                              uint32_t M, int mode, void* stream) {
+    return swiglu_impl(gate, up, x_dev, nullptr, 0.0f, h_dev, M, mode, stream);
+}
+
+int qraf_cuda_matvec_q_swiglu_ex(const qraf_weight_t* gate, const qraf_weight_t* up, const float* x_dev,
+                                 const float* norm_w, float norm_eps, float* h_dev, uint32_t M, int mode,
+                                 void* stream) {
+    return swiglu_impl(gate, up, x_dev, norm_w, norm_eps, h_dev, M, mode, stream);
 }
 
 // ── the tensor-core path without allocation ───────────────────────────────

@@ -91,6 +91,14 @@ struct RowParams {
     // x / (1 + exp(-x)), then the product: src/nn/ops.cpp:218-221,
     // src/nn/attention.cpp:172-179) to seg_y[0][v][i] ([M][N / 2]).
     uint32_t swiglu;
+    // Fusions around the projection (null: none).  norm_w: x is replaced by
+    // RMSNorm(x) = x * (1 / sqrt(mean(x^2) + norm_eps)) * norm_w per vector
+    // (src/nn/ops.cpp:107-118; FAST only: the sum of squares is taken in fp64 by
+    // the whole CTA).  seg_b[i]: a bias added to weight i's outputs, fl(y + b)
+    // (src/nn/attention.cpp:100-102).
+    const float* norm_w;
+    float norm_eps;
+    const float* seg_b[kMaxSeg];
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
     // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
     // output element goes into this rank's y and, as one 8-byte word (call number
@@ -142,10 +150,13 @@ __device__ __forceinline__ const uint8_t* row_src(const RowParams& p, uint32_t r
 __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uint32_t v, uint32_t row, float t) {
     if (p.world == 0) {
         if (p.nseg <= 1) {
+            if (p.seg_b[0]) t = __fadd_rn(t, p.seg_b[0][row]);
             p.y[static_cast<size_t>(v) * p.N + row] = t;
         } else {
             const uint32_t i = seg_of(p, row);
-            p.seg_y[i][static_cast<size_t>(v) * (p.seg_row0[i + 1] - p.seg_row0[i]) + (row - p.seg_row0[i])] = t;
+            const uint32_t r = row - p.seg_row0[i];
+            if (p.seg_b[i]) t = __fadd_rn(t, p.seg_b[i][r]);
+            p.seg_y[i][static_cast<size_t>(v) * (p.seg_row0[i + 1] - p.seg_row0[i]) + r] = t;
         }
         return;
     }
@@ -160,6 +171,8 @@ __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uin
 
 // SwiGLU output of the pair (gate, up) = virtual rows (2i, 2i + 1).
 __device__ __forceinline__ void store_swiglu(const RowParams& p, uint32_t v, uint32_t pair, float g, float u) {
+    if (p.seg_b[0]) g = __fadd_rn(g, p.seg_b[0][pair]);
+    if (p.seg_b[1]) u = __fadd_rn(u, p.seg_b[1][pair]);
     const float act = g / (1.0f + expf(-g));
     p.seg_y[0][static_cast<size_t>(v) * (p.N >> 1) + pair] = act * u;
 }
@@ -415,17 +428,60 @@ __device__ __forceinline__ void limb_record_part(const float4 a, const float4 b,
     }
 }
 
+// RMSNorm factor 1 / sqrt(mean(x^2) + eps) of one vector (K floats, K % 4 == 0),
+// by all threads of the CTA: the sum of squares in fp64 (so it differs from the
+// reference's fp32 running sum by at most that sum's own rounding), then the
+// reference's fp32 steps fl(fl(ss / K) + eps), 1 / sqrt (src/nn/ops.cpp:108-113).
+// red: 33 doubles of shared memory.
+__device__ __forceinline__ float rms_factor(const float* __restrict__ x, uint32_t K, float eps, double* red) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = (blockDim.x + 31u) >> 5;
+    double ss = 0.0;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (uint32_t i = threadIdx.x; i < K / 4u; i += blockDim.x) {
+        const float4 v = __ldcg(x4 + i);
+        ss += static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
+              static_cast<double>(v.w) * v.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (uint32_t w = 0; w < nw; ++w) t += red[w];
+        const float m = __fadd_rn(__fdiv_rn(static_cast<float>(t), static_cast<float>(K)), eps);
+        red[32] = static_cast<double>(__fdiv_rn(1.0f, __fsqrt_rn(m)));
+    }
+    __syncthreads();
+    const float r = static_cast<float>(red[32]);
+    __syncthreads();   // red is free again
+    return r;
+}
+
+// x * r * w for 8 consecutive elements starting at element e (the reference's
+// order: fl(fl(x r) w)).
+__device__ __forceinline__ void rms_apply8(float4& a, float4& b, float r, const float* __restrict__ w, uint32_t e) {
+    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + e)), wb = __ldg(reinterpret_cast<const float4*>(w + e) + 1);
+    a = make_float4(__fmul_rn(__fmul_rn(a.x, r), wa.x), __fmul_rn(__fmul_rn(a.y, r), wa.y),
+                    __fmul_rn(__fmul_rn(a.z, r), wa.z), __fmul_rn(__fmul_rn(a.w, r), wa.w));
+    b = make_float4(__fmul_rn(__fmul_rn(b.x, r), wb.x), __fmul_rn(__fmul_rn(b.y, r), wb.y),
+                    __fmul_rn(__fmul_rn(b.z, r), wb.z), __fmul_rn(__fmul_rn(b.w, r), wb.w));
+}
+
 // Turn the fp32 activations (global memory, read through L2) into limb records
 // in shared memory, in one pass, four threads per block; every thread has the
-// next round's loads in flight while it converts the current one.
+// next round's loads in flight while it converts the current one.  With
+// norm_w, each vector is RMS-normalised first (red: 33 doubles of shared memory).
 template <uint32_t DT>
 __device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, uint32_t K, uint8_t* xsb,
                                                    uint32_t xs_stride, uint32_t M, uint32_t nblk, uint32_t tid,
-                                                   uint32_t nthreads) {
+                                                   uint32_t nthreads, const float* __restrict__ norm_w = nullptr,
+                                                   float eps = 0.0f, double* red = nullptr) {
     const uint32_t lane = tid & 31u, sub = lane & 3u;
     const uint32_t tasks = nblk * 4u;   // per vector
     for (uint32_t m = 0; m < M; ++m) {
         const float4* xm = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K);
+        const float r = norm_w ? rms_factor(x + static_cast<size_t>(m) * K, K, eps, red) : 1.0f;
         uint8_t* recs = xsb + static_cast<size_t>(m) * xs_stride;
         uint32_t base = tid - lane;   // warp-uniform
         float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
@@ -435,11 +491,12 @@ __device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, 
         }
         for (; base < tasks; base += nthreads) {
             const uint32_t task = base + lane;
-            const float4 a = na, b = nb;
+            float4 a = na, b = nb;
             if (task + nthreads < tasks) {   // next round in flight
                 na = __ldcg(xm + 2u * (task + nthreads));
                 nb = __ldcg(xm + 2u * (task + nthreads) + 1u);
             }
+            if (norm_w && task < tasks) rms_apply8(a, b, r, norm_w, 8u * task);
             limb_record_part<DT>(a, b, task < tasks, recs + kLimbRec * (task >> 2), sub);
         }
     }
@@ -450,18 +507,29 @@ __device__ __forceinline__ void stage_limb_records(const float* __restrict__ x, 
 // elements over the whole grid.
 template <uint32_t DT>
 __global__ void __launch_bounds__(256) limb_prep_kernel(const float* __restrict__ x, uint32_t K, uint32_t M,
-                                                        uint32_t nblk, uint8_t* __restrict__ recs, uint32_t pdl) {
+                                                        uint32_t nblk, uint8_t* __restrict__ recs, uint32_t pdl,
+                                                        const float* __restrict__ norm_w, float eps) {
+    __shared__ double red[33];
     if (pdl) pdl_wait();
     if (pdl) pdl_launch_dependents();
     const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t per = nblk * 4u, total = M * per;
     const bool act = tid < total;
     const uint32_t m = act ? tid / per : 0u, task = act ? tid - m * per : 0u;
+    float r = 1.0f;
+    if (norm_w) {   // the vectors this CTA's tasks belong to (at most two: the first and the last)
+        const uint32_t t0 = blockIdx.x * blockDim.x, t1 = min(t0 + blockDim.x, total) - 1u;
+        const uint32_t m0 = t0 / per, m1 = t1 / per;
+        const float r0 = rms_factor(x + static_cast<size_t>(m0) * K, K, eps, red);
+        const float r1 = m1 == m0 ? r0 : rms_factor(x + static_cast<size_t>(m1) * K, K, eps, red);
+        r = m == m1 ? r1 : r0;
+    }
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     if (act) {
         const float4* xm = reinterpret_cast<const float4*>(x + static_cast<size_t>(m) * K);
         a = __ldcg(xm + 2u * task);
         b = __ldcg(xm + 2u * task + 1u);
+        if (norm_w) rms_apply8(a, b, r, norm_w, 8u * task);
     }
     limb_record_part<DT>(a, b, act, recs + (static_cast<size_t>(m) * nblk + (task >> 2)) * kLimbRec, task & 3u);
 }
@@ -551,6 +619,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
     const uint32_t part_floats = (!EXACT && p.npieces > 1) ? (p.M * p.part_rows * p.npieces + 1u) & ~1u : 0u;
     uint64_t* full = reinterpret_cast<uint64_t*>(part + part_floats);
     volatile uint32_t* slot_stage = reinterpret_cast<volatile uint32_t*>(full + nst + 1);
+    double* red = reinterpret_cast<double*>(full + nst + 1 + (nst + 1) / 2);   // 33 doubles (RMSNorm)
 
     if (blockDim.x != static_cast<uint32_t>(kRowThreads)) {
         if (threadIdx.x == 0) raise_error(kErrBadLaunch);
@@ -630,7 +699,8 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         }
         mbar_wait(&full[nst], 0u);
     } else {
-        stage_limb_records<DT>(p.x, p.K, xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u);
+        stage_limb_records<DT>(p.x, p.K, xsb, p.xs_stride, p.M, p.nblk, threadIdx.x, kRowWarps * 32u, p.norm_w,
+                               p.norm_eps, red);
     }
     __syncthreads();
 

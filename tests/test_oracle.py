@@ -154,3 +154,15 @@ def test_limb_partials_known_block(oracle_lib):
     assert c[0] == np.float32(2.0 ** -30)
     ints = int((d[0, 0].astype(np.int64) * np.array([1 << 24, 1 << 16, 1 << 8, 1])).sum())
     assert ints == int(sum(int(np.rint(float(v) * 2.0 ** 30)) for v in x))
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="oracle/_ref not built (no reference tree)")
+def test_rms_norm_matches_the_reference(oracle_lib):
+    """qo_rms_norm is ops::rms_norm_inplace (src/nn/ops.cpp:107-118) bit for bit."""
+    ref = oracle.Reference()
+    rng = np.random.default_rng(5)
+    for size, scale, eps in ((2048, 1.0, 1e-6), (4096, 30.0, 1e-5), (8192, 1e-3, 1e-6), (37, 1.0, 0.0),
+                             (28672, 5.0, 1e-6)):
+        x = (rng.normal(size=size) * scale).astype(np.float32)
+        w = rng.normal(1.0, 0.1, size=size).astype(np.float32)
+        assert oracle_lib.rms_norm(x, w, eps).tobytes() == ref.rms_norm(x, w, eps).tobytes(), (size, eps)
