@@ -211,7 +211,10 @@ class Reference:
                 ("qref_model_tensor", C.c_int, [vp, cp, C.POINTER(vp), C.POINTER(C.c_uint64),
                                                 C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
                                                 C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
-                ("qref_model_hidden_size", C.c_uint32, [vp])):
+                ("qref_model_hidden_size", C.c_uint32, [vp]),
+                ("qref_transformer_open", vp, [cp]), ("qref_transformer_close", None, [vp]),
+                ("qref_transformer_reset", None, [vp]),
+                ("qref_transformer_forward", C.c_int, [vp, C.c_uint32, C.c_int, _f32p, C.c_uint32])):
             fn = getattr(lib, name)
             fn.restype, fn.argtypes = res, args
         self.lib = lib
@@ -326,6 +329,38 @@ class Reference:
             return out
         finally:
             lib.qref_model_close(h)
+
+
+class RefTransformer:
+    """The reference's Transformer over a .qraf file (oracle/_ref,
+    src/nn/transformer.cpp): forward(token, pos) -> logits, one request at a time
+    with its own KV cache; reset() clears that cache."""
+
+    def __init__(self, ref: "Reference", path: str, vocab: int):
+        self.lib, self.vocab = ref.lib, vocab
+        self.h = ref.lib.qref_transformer_open(path.encode())
+        if not self.h:
+            raise ValueError(f"reference Transformer rejected {path}")
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        out = np.empty(self.vocab, dtype=np.float32)
+        if self.lib.qref_transformer_forward(self.h, token, pos, out, self.vocab) != 0:
+            raise ValueError("vocab size mismatch")
+        return out
+
+    def reset(self) -> None:
+        self.lib.qref_transformer_reset(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qref_transformer_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def reference_available() -> bool:

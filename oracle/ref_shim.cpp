@@ -2,7 +2,8 @@
 //
 // TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
 // the unmodified reference sources (src/tensor/{quantize,dtype,tensor}.cpp,
-// src/nn/{backend,ops,threading}.cpp, src/core/{logging,error}.cpp, read in
+// src/nn/{backend,ops,threading,attention,transformer}.cpp,
+// src/core/{logging,error}.cpp, src/qraf/{loader,header,writer}.cpp, read in
 // place from the reference tree) into oracle/_ref/libqraf_ref.so.  It is used
 // to pin the C restatement (qraf_oracle.c), to generate the golden fixtures in
 // tests/golden/, and as the timed CPU baseline.  No reference source is copied.
@@ -10,6 +11,7 @@
 #include "nn/attention.h"
 #include "nn/backend.h"
 #include "nn/ops.h"
+#include "nn/transformer.h"
 #include "qraf/format.h"
 #include "qraf/loader.h"
 #include "qraf/writer.h"
@@ -190,6 +192,30 @@ int qref_model_tensor(void* h, const char* name, const void** data, uint64_t* si
     return 0;
 }
 uint32_t qref_model_hidden_size(void* h) { return static_cast<QrafModel*>(h)->config().hidden_size; }
+
+// The reference's Transformer over a .qraf file (src/nn/transformer.cpp:
+// init at :300-440, forward -> forward_llama at :573-620 for llama / qwen2):
+// the decode engine's oracle.  forward() copies the logits out.
+struct RefTransformer {
+    QrafModel model;
+    Transformer tf;
+};
+void* qref_transformer_open(const char* path) {
+    RefTransformer* r = new RefTransformer();
+    if (!r->model.load(path) || !r->tf.init(r->model)) {
+        delete r;
+        return nullptr;
+    }
+    return r;
+}
+void qref_transformer_close(void* h) { delete static_cast<RefTransformer*>(h); }
+void qref_transformer_reset(void* h) { static_cast<RefTransformer*>(h)->tf.reset(); }
+int qref_transformer_forward(void* h, uint32_t token, int pos, float* logits, uint32_t vocab) {
+    Tensor t = static_cast<RefTransformer*>(h)->tf.forward(token, pos);
+    if (t.numel() != vocab) return 1;
+    std::memcpy(logits, t.data_f32(), vocab * sizeof(float));
+    return 0;
+}
 
 // Seeded synthetic data with the reference's idiom (std::mt19937 +
 // std::normal_distribution<float>, tools/dummy_model.cpp:12-16,

@@ -143,7 +143,8 @@ class QrafFileWriter:
         self._special = (bos, eos, pad, unk)
 
     # ── file ──
-    def to_bytes(self) -> bytes:
+    def _layout(self):
+        """Every section but the tensor data, placed: (file_size, [(offset, bytes)], tensor offsets)."""
         for key, _, _ in self._config:
             self._add_string(key)
         for t in self._tensors:
@@ -186,23 +187,35 @@ class QrafFileWriter:
         header = _HEADER.pack(QRAF_MAGIC, QRAF_VERSION, file_size, config_off, len(config), tok_off, len(tok), tdir_off,
                               tdir_size, qdir_off, qdir_size, str_off, len(strings), data_start, len(self._tensors),
                               len(self._quant), 0, 0, b"\0" * 8)
+        quant = b"".join(_QUANT.pack(i, d, b, g, 0.0, 0.0, 1, 0) for i, (d, b, g) in enumerate(self._quant))
+        sections = [(0, header), (config_off, config), (tok_off, tok), (tdir_off, b"".join(metas)), (qdir_off, quant),
+                    (str_off, strings)]
+        return file_size, sections, offsets
+
+    def to_bytes(self) -> bytes:
+        file_size, sections, offsets = self._layout()
         out = bytearray(file_size)
-        out[0:128] = header
-        out[config_off:config_off + len(config)] = config
-        out[tok_off:tok_off + len(tok)] = tok
-        out[tdir_off:tdir_off + tdir_size] = b"".join(metas)
-        out[qdir_off:qdir_off + qdir_size] = b"".join(_QUANT.pack(i, d, b, g, 0.0, 0.0, 1, 0)
-                                                      for i, (d, b, g) in enumerate(self._quant))
-        out[str_off:str_off + len(strings)] = strings
+        for o, b in sections:
+            out[o:o + len(b)] = b
         for t, o in zip(self._tensors, offsets):
             out[o:o + len(t.data)] = t.data
         return bytes(out)
 
     def write(self, path: str) -> int:
-        data = self.to_bytes()
+        """The file written section by section (the zero padding between them
+        included), without building it in memory first."""
+        file_size, sections, offsets = self._layout()
+        pieces = sorted(sections + [(o, t.data) for t, o in zip(self._tensors, offsets)], key=lambda p: p[0])
+        at = 0
         with open(path, "wb") as f:
-            f.write(data)
-        return len(data)
+            for o, b in pieces:
+                if o > at:
+                    f.write(b"\0" * (o - at))
+                f.write(b)
+                at = o + len(b)
+            if file_size > at:
+                f.write(b"\0" * (file_size - at))
+        return file_size
 
 
 @dataclass

@@ -89,6 +89,48 @@ def random_spec(seed: int) -> dict:
     return spec
 
 
+def tiny_decoder(arch: str = "qwen2", dt: int = Q8, seed: int = 11, layers: int = 2, hidden: int = 256, heads: int = 4,
+                 kv_heads: int = 2, inter: int = 512, vocab: int = 512, max_seq: int = 64) -> dict:
+    """A small random-init Llama / Qwen2 decoder under the tensor names the
+    reference's Transformer reads (src/nn/transformer.cpp:96-126, :320-400): F32
+    embedding and norms, quantized projections, an explicit quantized LM head,
+    and for qwen2 the Q/K/V biases."""
+    rng = np.random.default_rng(seed)
+    hd = hidden // heads
+    q_dim, kv_dim = heads * hd, kv_heads * hd
+
+    def w(*shape, std=0.05):
+        return rng.normal(0.0, std, size=shape).astype(np.float32)
+
+    tensors = [("model.embed_tokens.weight", (vocab, hidden), F32, w(vocab, hidden, std=1.0), None)]
+    for l in range(layers):
+        p = f"model.layers.{l}."
+        tensors += [
+            (p + "input_layernorm.weight", (hidden,), F32, (1.0 + w(hidden, std=0.1)), None),
+            (p + "self_attn.q_proj.weight", (q_dim, hidden), dt, w(q_dim, hidden), 0),
+            (p + "self_attn.k_proj.weight", (kv_dim, hidden), dt, w(kv_dim, hidden), 0),
+            (p + "self_attn.v_proj.weight", (kv_dim, hidden), dt, w(kv_dim, hidden), 0),
+            (p + "self_attn.o_proj.weight", (hidden, q_dim), dt, w(hidden, q_dim), 0),
+            (p + "post_attention_layernorm.weight", (hidden,), F32, (1.0 + w(hidden, std=0.1)), None),
+            (p + "mlp.gate_proj.weight", (inter, hidden), dt, w(inter, hidden), 0),
+            (p + "mlp.up_proj.weight", (inter, hidden), dt, w(inter, hidden), 0),
+            (p + "mlp.down_proj.weight", (hidden, inter), dt, w(hidden, inter), 0),
+        ]
+        if arch == "qwen2":
+            tensors += [(p + f"self_attn.{x}_proj.bias", (n,), F32, w(n, std=0.1), None)
+                        for x, n in (("q", q_dim), ("k", kv_dim), ("v", kv_dim))]
+    tensors += [("model.norm.weight", (hidden,), F32, (1.0 + w(hidden, std=0.1)), None),
+                ("lm_head.weight", (vocab, hidden), dt, w(vocab, hidden), 0)]
+    return {
+        "config": [("architecture", arch), ("vocab_size", vocab), ("hidden_size", hidden), ("num_layers", layers),
+                   ("num_heads", heads), ("num_kv_heads", kv_heads), ("intermediate_size", inter),
+                   ("max_seq_len", max_seq), ("rope_theta", 10000.0), ("rms_norm_eps", 1e-6)],
+        "schemes": [(dt, 32, 1)],
+        "tensors": tensors,
+        "vocab": None, "merges": [], "special": None,
+    }
+
+
 def tensor_bytes(spec, spec_tensor, quantize) -> bytes:
     """The bytes a tensor of the spec has in the file: fp32 values, or the
     quantizer's native blocks row by row with its scheme's block size."""

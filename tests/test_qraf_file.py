@@ -154,3 +154,38 @@ def test_model_open_missing_file(tmp_path):
 
     rc, msg, _ = _open_rc(str(tmp_path / "absent.qraf"))
     assert rc == qb.ERR_INVALID and "cannot open" in msg
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("arch,dt", [("qwen2", qraf_spec.Q8), ("llama", qraf_spec.Q4)])
+def test_reference_transformer_runs_our_quantized_file(tmp_path, oracle_lib, arch, dt):
+    """A decoder written by QrafFileWriter loads in the reference's own
+    Transformer (the decode engine's oracle) and decodes: finite logits that
+    follow the token and position, and reset() restarts the sequence."""
+    spec = qraf_spec.tiny_decoder(arch, dt)
+    w = qf.QrafFileWriter()
+    qraf_spec.write_with(w, spec, oracle_lib.quantize_rows)
+    path = str(tmp_path / "dec.qraf")
+    w.write(path)
+    vocab = dict(spec["config"])["vocab_size"]
+    ref = oracle.RefTransformer(oracle.Reference(), path, vocab)
+    a0 = ref.forward(5, 0)
+    a1 = ref.forward(17, 1)
+    ref.reset()
+    b0 = ref.forward(5, 0)
+    ref.close()
+    assert np.isfinite(a0).all() and np.isfinite(a1).all()
+    assert np.array_equal(a0, b0)
+    assert not np.array_equal(a0, a1)
+
+
+def test_write_streams_the_same_bytes(tmp_path, oracle_lib):
+    """write() puts the sections and the padding down one after another; the
+    file is to_bytes() exactly, for the spec the reference's writer is pinned on."""
+    spec = qraf_spec.llama_like()
+    w = qf.QrafFileWriter()
+    qraf_spec.write_with(w, spec, oracle_lib.quantize_rows)
+    path = str(tmp_path / "s.qraf")
+    assert w.write(path) == len(w.to_bytes())
+    with open(path, "rb") as f:
+        assert f.read() == w.to_bytes()
