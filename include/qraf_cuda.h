@@ -319,6 +319,15 @@ const char* qraf_cuda_model_weight_name(qraf_model_t m, uint32_t index);
 int qraf_cuda_model_config_u32(qraf_model_t m, const char* key, uint32_t* value);
 /* Free the device copy. */
 int qraf_cuda_model_close(qraf_model_t m);
+/* qraf_cuda_model_open with flags.  QRAF_MODEL_F32: the F32 tensors (embedding,
+ * norms, biases, an F32 LM head) join the same device allocation, read by
+ * qraf_cuda_model_tensor_f32 (the reference's Transformer::init loads them with
+ * load_tensor_f32, src/nn/transformer.cpp:300-440). */
+#define QRAF_MODEL_F32 1u
+int qraf_cuda_model_open_ex(const char* path, uint32_t flags, qraf_model_t* out);
+/* Device address and element count of the F32 tensor `name` of a model opened
+ * with QRAF_MODEL_F32 (QRAF_ERR_INVALID if absent). */
+int qraf_cuda_model_tensor_f32(qraf_model_t m, const char* name, const float** data, uint64_t* count);
 
 /* ── host utility ───────────────────────────────────────────────────────── */
 /* Seeded synthetic data with the reference's idiom: std::mt19937(seed) and

@@ -28,6 +28,7 @@ MODE_FAST = 1
 MODE_TC = 2
 MODE_AUTO = 3
 MODE_FLAG_OVERLAP = 0x100
+MODEL_F32 = 1               # qraf_cuda_model_open_ex: upload the F32 tensors too
 
 OK = 0
 ERR_INVALID = 1
@@ -101,6 +102,8 @@ def _load() -> C.CDLL:
         "qraf_cuda_model_weight_name": (C.c_char_p, [vp, u32]),
         "qraf_cuda_model_config_u32": (i32, [vp, C.c_char_p, C.POINTER(u32)]),
         "qraf_cuda_model_close": (i32, [vp]),
+        "qraf_cuda_model_open_ex": (i32, [C.c_char_p, u32, C.POINTER(vp)]),
+        "qraf_cuda_model_tensor_f32": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64)]),
         "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
         "qraf_cuda_comm_create": (i32, [i32, i32, u64, C.POINTER(vp)]),
         "qraf_cuda_comm_handle": (i32, [vp, vp]),
@@ -237,10 +240,16 @@ class DeviceModel:
     """A .qraf file with its Q8_0 / Q4_0 tensors resident on the current device
     (qraf_cuda_model_open: one allocation, the file's bytes unchanged)."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, f32: bool = False):
         h = C.c_void_p()
-        check(_get_lib().qraf_cuda_model_open(os.fsencode(path), C.byref(h)))
+        check(_get_lib().qraf_cuda_model_open_ex(os.fsencode(path), MODEL_F32 if f32 else 0, C.byref(h)))
         self._h = h
+
+    def tensor_f32(self, name: str):
+        """(device address, element count) of an F32 tensor (a model opened with f32=True)."""
+        p, n = C.c_void_p(), C.c_uint64()
+        check(_get_lib().qraf_cuda_model_tensor_f32(self._h, name.encode(), C.byref(p), C.byref(n)))
+        return p.value, n.value
 
     @property
     def names(self) -> list:

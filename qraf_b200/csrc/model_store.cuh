@@ -11,7 +11,9 @@
 // host fills one while the copy engine drains the other).  The mapping is
 // dropped after the upload: weights are immutable model data, so the device
 // copy is the only one the matvec needs.  F32 tensors (norms, embeddings,
-// biases) stay with the caller's own loader.
+// biases) stay with the caller's own loader, unless qraf_cuda_model_open_ex is
+// given QRAF_MODEL_F32: then they join the same allocation (the decode engine's
+// model).
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -66,11 +68,14 @@ struct Mapping {
 
 bool in_file(uint64_t off, uint64_t len, uint64_t size) { return off <= size && len <= size - off; }
 
-// One quantized tensor of the file and its place in the device allocation.
+constexpr uint32_t kFileDtypeF32 = 0;   // DType::F32 (include/core/types.h)
+
+// One tensor of the file and its place in the device allocation: a quantized
+// weight, or (dtype F32) `count` floats.
 struct StorePlace {
     std::string name;
     uint32_t dtype, bs, rows, cols;
-    uint64_t file_off, bytes, dev_off;
+    uint64_t file_off, bytes, dev_off, count;
 };
 
 // Copy every place's bytes from the mapping to base + dev_off through two
@@ -120,13 +125,17 @@ struct qraf_model {
     std::vector<std::string> names;                         // quantized tensors, directory order
     std::unordered_map<std::string, qraf_weight_t> weights;
     std::unordered_map<std::string, uint32_t> config;       // u32 and f32 (raw bits) entries
+    std::unordered_map<std::string, std::string> config_str;   // string entries
+    std::unordered_map<std::string, std::pair<const float*, uint64_t>> f32;   // QRAF_MODEL_F32: device floats
 };
 
 extern "C" {
 
-int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
+int qraf_cuda_model_open_ex(const char* path, uint32_t flags, qraf_model_t* out) {
     if (!path || !out) return fail(QRAF_ERR_INVALID, "path or out is NULL");
     *out = nullptr;
+    if (flags & ~static_cast<uint32_t>(QRAF_MODEL_F32)) return fail(QRAF_ERR_INVALID, "unknown flags 0x%x", flags);
+    const bool want_f32 = (flags & QRAF_MODEL_F32) != 0;
     Mapping mp;
     mp.fd = open(path, O_RDONLY);
     if (mp.fd < 0) return fail(QRAF_ERR_INVALID, "cannot open %s", path);
@@ -181,7 +190,14 @@ int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
             std::string key;
             if (!string_at(e.key_offset, &key))
                 return fail(QRAF_ERR_INVALID, "%s: config key %u out of range", path, i);
-            if (e.value_type <= 1) m->config[key] = e.value;
+            if (e.value_type <= 1) {
+                m->config[key] = e.value;
+            } else if (e.value_type == 2) {
+                std::string v;
+                if (!string_at(e.value, &v))
+                    return fail(QRAF_ERR_INVALID, "%s: config string '%s' out of range", path, key.c_str());
+                m->config_str[key] = v;
+            }
         }
     }
 
@@ -195,9 +211,26 @@ int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
         if (!string_at(t.name_offset, &name)) return fail(QRAF_ERR_INVALID, "%s: tensor %u has no name", path, i);
         if (!in_file(t.data_offset, t.data_size, mp.size))
             return fail(QRAF_ERR_INVALID, "%s: tensor '%s' data extends past the end of the file", path, name.c_str());
-        if (!known_dtype(t.dtype)) continue;
+        const bool is_f32 = want_f32 && t.dtype == kFileDtypeF32;
+        if (!known_dtype(t.dtype) && !is_f32) continue;
         if (t.ndim == 0 || t.ndim > 8)
             return fail(QRAF_ERR_INVALID, "%s: tensor '%s' has ndim %u", path, name.c_str(), t.ndim);
+        if (is_f32) {
+            uint64_t count = 1;
+            for (uint32_t d = 0; d < t.ndim; ++d) count *= t.shape[d];
+            if (count > (uint64_t(1) << 40) || t.data_size < count * 4)
+                return fail(QRAF_ERR_INVALID, "%s: F32 tensor '%s' holds %llu bytes, its shape needs %llu", path,
+                            name.c_str(), static_cast<unsigned long long>(t.data_size),
+                            static_cast<unsigned long long>(count * 4));
+            if (!seen.insert(name).second)
+                return fail(QRAF_ERR_INVALID, "%s: tensor '%s' appears twice", path, name.c_str());
+            StorePlace pl{name, kFileDtypeF32, 0, 0, 0, t.data_offset, count * 4, 0, count};
+            total = (total + kStoreAlign - 1) / kStoreAlign * kStoreAlign;
+            pl.dev_off = total;
+            total += pl.bytes;
+            places.push_back(pl);
+            continue;
+        }
         // rows = the product of the leading dimensions, cols = the last (row-major,
         // layout_id 0; a weight is [out_dim][in_dim])
         uint64_t rows = 1;
@@ -215,7 +248,7 @@ int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
         if (rows > 0xFFFFFFFFull) return fail(QRAF_ERR_INVALID, "%s: tensor '%s' has too many rows", path, name.c_str());
         if (bs == 0 || (t.dtype == QRAF_DTYPE_Q4_0 && bs < 2))
             return fail(QRAF_ERR_INVALID, "%s: tensor '%s' has block size %u", path, name.c_str(), bs);
-        StorePlace pl;
+        StorePlace pl{};
         pl.name = name;
         pl.dtype = t.dtype;
         pl.bs = bs;
@@ -253,6 +286,10 @@ int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
         }
     }
     for (const StorePlace& pl : places) {
+        if (pl.dtype == kFileDtypeF32) {
+            m->f32[pl.name] = {reinterpret_cast<const float*>(static_cast<uint8_t*>(m->base) + pl.dev_off), pl.count};
+            continue;
+        }
         qraf_weight_t w;
         rc = describe_weight(pl.bytes, pl.dtype, pl.bs, pl.rows, pl.cols, &w);
         if (rc) {
@@ -264,6 +301,18 @@ int qraf_cuda_model_open(const char* path, qraf_model_t* out) {
         m->names.push_back(pl.name);
     }
     *out = m.release();
+    return QRAF_OK;
+}
+
+int qraf_cuda_model_open(const char* path, qraf_model_t* out) { return qraf_cuda_model_open_ex(path, 0, out); }
+
+int qraf_cuda_model_tensor_f32(qraf_model_t m, const char* name, const float** data, uint64_t* count) {
+    if (!m || !name || !data || !count) return fail(QRAF_ERR_INVALID, "model, name, data or count is NULL");
+    auto it = m->f32.find(name);
+    if (it == m->f32.end())
+        return fail(QRAF_ERR_INVALID, "no F32 tensor named '%s' (open the model with QRAF_MODEL_F32)", name);
+    *data = it->second.first;
+    *count = it->second.second;
     return QRAF_OK;
 }
 

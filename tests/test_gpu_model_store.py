@@ -154,3 +154,26 @@ def test_host_cache_add_rejects_a_short_buffer(cuda):
     with pytest.raises(qb.QrafError) as e:
         qb.host_cache_add(buf, qb.Q8_0, 4, 64)
     assert e.value.code == qb.ERR_INVALID
+
+
+def test_f32_tensors_join_the_allocation(model_file, cuda):
+    """qraf_cuda_model_open_ex(QRAF_MODEL_F32): F32 tensors are on the device with
+    the file's values; without the flag they are absent; string config entries
+    and the quantized tensors are the same either way."""
+    import torch
+
+    path, _ = model_file
+    m = qb.DeviceModel(path, f32=True)
+    ptr, n = m.tensor_f32("norm.weight")
+    assert n == H
+    got = qb._wrap_device_floats(ptr, n, cuda).cpu().numpy()
+    assert np.array_equal(got, np.ones(H, np.float32))
+    assert sorted(m.names) == sorted(s[0] for s in SHAPES)
+    plain = qb.DeviceModel(path)
+    with pytest.raises(qb.QrafError) as e:
+        plain.tensor_f32("norm.weight")
+    assert e.value.code == qb.ERR_INVALID and "QRAF_MODEL_F32" in str(e.value)
+    assert m.info()["device_bytes"] > plain.info()["device_bytes"]
+    plain.close()
+    m.close()
+    torch.cuda.synchronize()
