@@ -91,6 +91,9 @@ const char* qraf_cuda_version(void);
 int qraf_cuda_init(int device);
 /* Free the host-pointer weight cache and staging buffers of every device. */
 int qraf_cuda_shutdown(void);
+/* Kernels the library has launched in this process, all devices and streams (a
+ * launch captured into a CUDA graph counts once, at capture). */
+uint64_t qraf_cuda_launch_count(void);
 /* Copy the calling thread's last error message into buf (always NUL-terminated). */
 int qraf_cuda_last_error(char* buf, size_t len);
 /* Synchronise the current device and return QRAF_ERR_TIMEOUT if a kernel
@@ -328,6 +331,32 @@ int qraf_cuda_model_open_ex(const char* path, uint32_t flags, qraf_model_t* out)
 /* Device address and element count of the F32 tensor `name` of a model opened
  * with QRAF_MODEL_F32 (QRAF_ERR_INVALID if absent). */
 int qraf_cuda_model_tensor_f32(qraf_model_t m, const char* name, const float** data, uint64_t* count);
+
+/* ── decode engine ─────────────────────────────────────────────────────── */
+/* A Llama / Qwen2 / Mistral decoder over a .qraf file, resident on the current
+ * device: replaces Transformer::init + Transformer::forward(token, pos)
+ * (src/nn/transformer.cpp:300-440, :573-620) and the request-at-a-time loop of
+ * BatchScheduler (include/runtime/batch_scheduler.h:187-228).  open reads the
+ * model (qraf_cuda_model_open_ex with QRAF_MODEL_F32; tensor names as
+ * Transformer::init reads them; lm_head.weight quantized or F32, else the
+ * embedding tied), allocates an F32 KV cache of max_slots x layers x max_seq
+ * x kv_dim per K and V and the RoPE angles of every position. */
+typedef struct qraf_decoder* qraf_decoder_t;
+int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_seq, qraf_decoder_t* out);
+/* One decode step for M <= max_slots slots at once: slot slots_dev[m] takes
+ * token tokens_dev[m] at position pos_dev[m] (all device int32 arrays of M;
+ * slots distinct within a step; positions < max_seq), writes K/V at that
+ * position of its cache, attends over positions 0 .. pos, and leaves the
+ * logits in logits_dev[m][vocab].  `mode` picks the projections' arithmetic
+ * (QRAF_MODE_*).  A token, position or slot out of range raises the device
+ * status (qraf_cuda_device_status). */
+int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_dev, const int32_t* pos_dev,
+                           const int32_t* slots_dev, float* logits_dev, int mode, void* stream);
+/* Sizes of the decoder (each pointer may be NULL). */
+int qraf_cuda_decoder_info(qraf_decoder_t d, uint32_t* vocab, uint32_t* hidden, uint32_t* layers, uint32_t* max_slots,
+                           uint32_t* max_seq);
+/* Free the decoder, its caches and its model. */
+int qraf_cuda_decoder_close(qraf_decoder_t d);
 
 /* ── host utility ───────────────────────────────────────────────────────── */
 /* Seeded synthetic data with the reference's idiom: std::mt19937(seed) and

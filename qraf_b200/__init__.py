@@ -102,6 +102,12 @@ def _load() -> C.CDLL:
         "qraf_cuda_model_weight_name": (C.c_char_p, [vp, u32]),
         "qraf_cuda_model_config_u32": (i32, [vp, C.c_char_p, C.POINTER(u32)]),
         "qraf_cuda_model_close": (i32, [vp]),
+        "qraf_cuda_launch_count": (u64, []),
+        "qraf_cuda_decoder_open": (i32, [C.c_char_p, u32, u32, C.POINTER(vp)]),
+        "qraf_cuda_decoder_step": (i32, [vp, u32, vp, vp, vp, vp, i32, vp]),
+        "qraf_cuda_decoder_info": (i32, [vp, C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), C.POINTER(u32),
+                                         C.POINTER(u32)]),
+        "qraf_cuda_decoder_close": (i32, [vp]),
         "qraf_cuda_model_open_ex": (i32, [C.c_char_p, u32, C.POINTER(vp)]),
         "qraf_cuda_model_tensor_f32": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64)]),
         "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
@@ -286,6 +292,51 @@ class DeviceModel:
         try:
             if self._h:
                 _get_lib().qraf_cuda_model_close(self._h)
+        except Exception:
+            pass
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process (a captured launch counts once)."""
+    return int(_get_lib().qraf_cuda_launch_count())
+
+
+class Decoder:
+    """A Llama / Qwen2 decode engine over a .qraf file (qraf_cuda_decoder_*):
+    step() runs one decode step for M slots at once, each with its own KV cache."""
+
+    def __init__(self, path: str, max_slots: int = 1, max_seq: int = 2048):
+        h = C.c_void_p()
+        check(_get_lib().qraf_cuda_decoder_open(os.fsencode(path), max_slots, max_seq, C.byref(h)))
+        self._h = h
+        v, hd, l, ms, mq = (C.c_uint32() for _ in range(5))
+        check(_get_lib().qraf_cuda_decoder_info(h, C.byref(v), C.byref(hd), C.byref(l), C.byref(ms), C.byref(mq)))
+        self.vocab, self.hidden, self.layers = v.value, hd.value, l.value
+        self.max_slots, self.max_seq = ms.value, mq.value
+
+    def step(self, tokens, positions, slots, mode: int = MODE_AUTO, logits=None, stream=None):
+        """tokens, positions, slots: contiguous CUDA int32 tensors of M; returns logits [M, vocab]."""
+        torch = _torch()
+        m = tokens.numel()
+        for t in (tokens, positions, slots):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous() or t.numel() != m:
+                raise ValueError("tokens, positions and slots must be contiguous CUDA int32 tensors of one length")
+        if logits is None:
+            logits = torch.empty((m, self.vocab), dtype=torch.float32, device=tokens.device)
+        check(_get_lib().qraf_cuda_decoder_step(self._h, m, C.c_void_p(tokens.data_ptr()),
+                                                C.c_void_p(positions.data_ptr()), C.c_void_p(slots.data_ptr()),
+                                                C.c_void_p(logits.data_ptr()), mode, _stream(stream)))
+        return logits
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, C.c_void_p()
+            check(_get_lib().qraf_cuda_decoder_close(h))
+
+    def __del__(self):
+        try:
+            if self._h:
+                _get_lib().qraf_cuda_decoder_close(self._h)
         except Exception:
             pass
 

@@ -3,6 +3,7 @@
 // drop-in entry with its device weight cache, and small host utilities; the
 // .qraf model store (model_store.cuh) is included at the end.
 #include <algorithm>
+#include <atomic>
 #include <cudaTypedefs.h>
 #include <cstdarg>
 #include <cstdio>
@@ -62,6 +63,15 @@ struct DeviceInfo {
 
 std::mutex g_dev_mutex;
 DeviceInfo g_dev[64];
+
+// Kernels this library has launched in the process (qraf_cuda_launch_count):
+// every launch site goes through count_launch() or counted().
+std::atomic<uint64_t> g_launches{0};
+inline void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+inline cudaError_t counted(cudaError_t e) {
+    if (e == cudaSuccess) count_launch();
+    return e;
+}
 
 constexpr int kSmemReserve = 1024;
 
@@ -283,6 +293,7 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     p.rows_extra = rows_extra;
     p.row_unit = unit;
     p.swiglu = 0;
+    p.accumulate = 0;
     p.norm_w = nullptr;
     p.norm_eps = 0.0f;
     for (int i = 0; i < kMaxSeg; ++i) p.seg_b[i] = nullptr;
@@ -323,7 +334,7 @@ cudaError_t launch_ex(Kern kernel, int grid, int threads, size_t smem, cudaStrea
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kernel, p);
+    return counted(cudaLaunchKernelEx(&cfg, kernel, p));
 }
 
 template <uint32_t DT>
@@ -369,9 +380,9 @@ int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStre
         cfg.gridDim = dim3((pl.p.M * pl.p.nblk * 4u + 255u) / 256u);
         cfg.blockDim = dim3(256);
         cfg.stream = st;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, dtype == QRAF_DTYPE_Q8_0 ? limb_prep_kernel<kDtypeQ8> : limb_prep_kernel<kDtypeQ4>,
+        const cudaError_t e = counted(cudaLaunchKernelEx(&cfg, dtype == QRAF_DTYPE_Q8_0 ? limb_prep_kernel<kDtypeQ8> : limb_prep_kernel<kDtypeQ4>,
                                                  pl.p.x, pl.p.K, pl.p.M, pl.p.nblk, recs, overlap ? 1u : 0u,
-                                                 pl.p.norm_w, pl.p.norm_eps);
+                                                 pl.p.norm_w, pl.p.norm_eps));
         if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "limb prep launch: %s", cudaGetErrorString(e));
         pl.p.xrec = recs;
         overlap = true;   // the row kernel waits for the prep kernel, not for the one before it
@@ -384,13 +395,13 @@ int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStre
 template <uint32_t DT>
 cudaError_t launch_stream(const StreamPlan& pl, bool exact, cudaStream_t st) {
     if (exact) {
-        qmv_stream_kernel<DT, true, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+        (qmv_stream_kernel<DT, true, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p), count_launch());
     } else if (pl.MT == 1) {
-        qmv_stream_kernel<DT, false, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+        (qmv_stream_kernel<DT, false, 1><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p), count_launch());
     } else if (pl.MT == 2) {
-        qmv_stream_kernel<DT, false, 2><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+        (qmv_stream_kernel<DT, false, 2><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p), count_launch());
     } else {
-        qmv_stream_kernel<DT, false, 4><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p);
+        (qmv_stream_kernel<DT, false, 4><<<pl.grid, pl.threads, pl.smem, st>>>(pl.p), count_launch());
     }
     return cudaGetLastError();
 }
@@ -400,7 +411,7 @@ cudaError_t launch_generic(const GenericParams& gp, uint64_t tasks, cudaStream_t
     const uint64_t grid = (tasks + 7) / 8;
     if (grid == 0) return cudaSuccess;
     if (grid > 0x7FFFFFFFull) return cudaErrorInvalidConfiguration;
-    qmv_generic_kernel<DT, EXACT, PARTIALS><<<static_cast<unsigned>(grid), 256, 0, st>>>(gp);
+    (qmv_generic_kernel<DT, EXACT, PARTIALS><<<static_cast<unsigned>(grid), 256, 0, st>>>(gp), count_launch());
     return cudaGetLastError();
 }
 
@@ -572,14 +583,14 @@ cudaError_t launch_tc_mv(const TcPlan& pl, const CUtensorMap& map, const float* 
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cfg.numAttrs = pdl_prep ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, tc_prep_kernel<DT>, x, const_cast<uint8_t*>(p.act), p.tile_count, p.tiles,
-                                       K, p.M, p.nblk, p.n_pad, pdl_prep ? 1u : 0u);
+    cudaError_t e = counted(cudaLaunchKernelEx(&cfg, tc_prep_kernel<DT>, x, const_cast<uint8_t*>(p.act), p.tile_count, p.tiles,
+                                       K, p.M, p.nblk, p.n_pad, pdl_prep ? 1u : 0u));
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.numAttrs = 1;   // weights stream while the prep kernel runs; activations wait for it
-    return cudaLaunchKernelEx(&cfg, qmm_tc_kernel<DT, MV>, map, p);
+    return counted(cudaLaunchKernelEx(&cfg, qmm_tc_kernel<DT, MV>, map, p));
 }
 
 template <uint32_t DT>
@@ -706,13 +717,24 @@ int launch_tc1(uint32_t dtype, Tc1Plan& pl, bool overlap, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = overlap ? 1 : 0;
-    const cudaError_t e = dtype == QRAF_DTYPE_Q8_0 ? cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ8>, pl.p)
-                                                   : cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ4>, pl.p);
+    const cudaError_t e = dtype == QRAF_DTYPE_Q8_0 ? counted(cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ8>, pl.p))
+                                                   : counted(cudaLaunchKernelEx(&cfg, qmv_tc1_kernel<kDtypeQ4>, pl.p));
     if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "batch-1 tensor-core kernel launch: %s", cudaGetErrorString(e));
     return QRAF_OK;
 }
 
-int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode_in, cudaStream_t st) {
+// y = fl(t + y), element by element (the residual add of an unfused projection).
+static __global__ void __launch_bounds__(256) residual_add_kernel(float* __restrict__ y, const float* __restrict__ t,
+                                                                  size_t n) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        y[i] = __fadd_rn(t[i], y[i]);
+}
+
+// y = W x, or with accumulate y = fl(W x + y): in the row kernel's store where
+// that kernel runs, else through a per-stream buffer and residual_add_kernel.
+int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, int mode_in, cudaStream_t st,
+                bool accumulate = false) {
     int rc = check_weight(w);
     if (rc) return rc;
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
@@ -728,6 +750,7 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
     if (M == 0 || w->rows == 0) return QRAF_OK;
     if (!y) return fail(QRAF_ERR_INVALID, "y is NULL");
     if (w->cols == 0) {   // an empty dot is 0 (quantize.cpp:189-209 with no blocks); x is not read
+        if (accumulate) return fail(QRAF_ERR_UNSUPPORTED, "a residual projection needs at least one column");
         QRAF_CUDA_TRY(cudaMemsetAsync(y, 0, static_cast<size_t>(M) * w->rows * sizeof(float), st));
         return QRAF_OK;
     }
@@ -735,6 +758,20 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
     DeviceInfo* dev = nullptr;
     rc = ensure_device(nullptr, &dev);
     if (rc) return rc;
+    auto accumulate_via_scratch = [&]() -> int {
+        const size_t n = static_cast<size_t>(M) * w->rows;
+        uint8_t* buf = nullptr;
+        int r = stream_scratch(st, n * sizeof(float), &buf, "a residual projection's output", 3);
+        if (r) return r;
+        r = matvec_impl(w, x, reinterpret_cast<float*>(buf), M, mode_in, st, false);
+        if (r) return r;
+        const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev->sm_count));
+        (residual_add_kernel<<<grid, 256, 0, st>>>(y, reinterpret_cast<const float*>(buf), n), count_launch());
+        QRAF_CUDA_TRY(cudaGetLastError());
+        return QRAF_OK;
+    };
+    if (accumulate && !((mode == QRAF_MODE_EXACT || (mode == QRAF_MODE_FAST && M <= 2)) && rows_eligible(*w, x)))
+        return accumulate_via_scratch();
     if (M == 1 && mode == QRAF_MODE_TC) {   // tensor cores for one vector: the batch-1 kernel where it applies
         Tc1Plan t1;
         if (plan_tc1(w, 1, x, &y, *dev, &t1)) return launch_tc1(w->dtype, t1, overlap, st);
@@ -760,6 +797,7 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
                 one.p.x = x + static_cast<size_t>(m0) * w->cols;
                 one.p.y = y + static_cast<size_t>(m0) * w->rows;
                 one.p.M = cnt;
+                one.p.accumulate = accumulate ? 1u : 0u;
                 const int MT = exact ? 1 : static_cast<int>(cnt);
                 if (!exact) {
                     const int rc2 = launch_rows_fast(w->dtype, one, MT, overlap, st);
@@ -772,6 +810,7 @@ int matvec_impl(const qraf_weight_t* w, const float* x, float* y, uint32_t M, in
             return QRAF_OK;
         }
     }
+    if (accumulate) return accumulate_via_scratch();
 
     // K-split streaming kernel: FAST for three or more vectors.
     StreamPlan pl;
@@ -936,6 +975,8 @@ int qraf_cuda_init(int device) {
     return ensure_device(nullptr, nullptr);
 }
 
+uint64_t qraf_cuda_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 int qraf_cuda_last_error(char* buf, size_t len) {
     if (!buf || len == 0) return QRAF_ERR_INVALID;
     const size_t n = std::min(len - 1, t_last_error.size());
@@ -1082,7 +1123,7 @@ static int normalize_into_scratch(const float* x, const float* norm_w, float eps
     const int rc = stream_scratch(st, static_cast<size_t>(M) * K * sizeof(float), &buf,
                                   "the normalised activations of a fused call", 2);
     if (rc) return rc;
-    rmsnorm_kernel<<<M, 256, 0, st>>>(x, norm_w, eps, K, reinterpret_cast<float*>(buf), exact ? 1 : 0);
+    (rmsnorm_kernel<<<M, 256, 0, st>>>(x, norm_w, eps, K, reinterpret_cast<float*>(buf), exact ? 1 : 0), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     *out = reinterpret_cast<const float*>(buf);
     return QRAF_OK;
@@ -1091,7 +1132,7 @@ static int normalize_into_scratch(const float* x, const float* norm_w, float eps
 static int add_bias(float* y, const float* b, uint32_t rows, uint32_t M, const DeviceInfo& dev, cudaStream_t st) {
     const size_t n = static_cast<size_t>(M) * rows;
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev.sm_count));
-    if (n) bias_add_kernel<<<grid, 256, 0, st>>>(y, b, rows, n);
+    if (n) (bias_add_kernel<<<grid, 256, 0, st>>>(y, b, rows, n), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
@@ -1276,7 +1317,7 @@ static int swiglu_impl(const qraf_weight_t* gate, const qraf_weight_t* up, const
     rc = matvec_impl(up, x_in, reinterpret_cast<float*>(ubuf), M, mode_in, st);
     if (rc) return rc;
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8u * dev->sm_count));
-    swiglu_apply_kernel<<<grid, 256, 0, st>>>(h_dev, reinterpret_cast<const float*>(ubuf), n);
+    (swiglu_apply_kernel<<<grid, 256, 0, st>>>(h_dev, reinterpret_cast<const float*>(ubuf), n), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
@@ -1362,11 +1403,11 @@ int qraf_cuda_limb_partials(const qraf_weight_t* w, const float* x_dev, int32_t*
         return fail(QRAF_ERR_UNSUPPORTED, "K = %u needs %zu bytes of shared memory", w->cols, smem);
     const unsigned grid = (w->rows + 7u) / 8u;
     if (w->dtype == QRAF_DTYPE_Q8_0)
-        limb_partials_kernel<kDtypeQ8><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev);
+        (limb_partials_kernel<kDtypeQ8><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev), count_launch());
     else
-        limb_partials_kernel<kDtypeQ4><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev);
+        (limb_partials_kernel<kDtypeQ4><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint8_t*>(w->data), w->row_bytes, w->rows, w->cols, nblk, x_dev, d_dev, c_dev), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
@@ -1413,9 +1454,9 @@ static int quantize_launch(uint32_t dtype, const float* x, uint64_t rows, uint64
     const uint64_t grid = (qp.nblocks_total + 255) / 256;
     if (grid > 0x7FFFFFFFull) return fail(QRAF_ERR_INVALID, "too many blocks");
     if (dtype == QRAF_DTYPE_Q8_0)
-        quantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp);
+        (quantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp), count_launch());
     else
-        quantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp);
+        (quantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(qp), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
@@ -1441,11 +1482,11 @@ int qraf_cuda_dequantize(uint32_t dtype, const void* q_dev, uint64_t count, uint
     const uint32_t bb = static_cast<uint32_t>(block_bytes_of(dtype, block_size));
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (dtype == QRAF_DTYPE_Q8_0)
-        dequantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(
-            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb);
+        (dequantize_kernel<kDtypeQ8><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb), count_launch());
     else
-        dequantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(
-            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb);
+        (dequantize_kernel<kDtypeQ4><<<static_cast<unsigned>(grid), 256, 0, st>>>(
+            static_cast<const uint8_t*>(q_dev), out_dev, count, block_size, bb, nb), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
     return QRAF_OK;
 }
@@ -1704,8 +1745,8 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
         cfg.blockDim = dim3(256);
         cfg.stream = s.stream;
         uint32_t* status = from_host ? nullptr : s.status_map;
-        QRAF_CUDA_TRY(from_host ? cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n, status)
-                                : cudaLaunchKernelEx(&cfg, host_copy_kernel<false>, src, dst, n, status));
+        QRAF_CUDA_TRY(from_host ? counted(cudaLaunchKernelEx(&cfg, host_copy_kernel<true>, src, dst, n, status))
+                                : counted(cudaLaunchKernelEx(&cfg, host_copy_kernel<false>, src, dst, n, status)));
         return QRAF_OK;
     };
     auto enqueue = [&]() -> int {
@@ -1718,9 +1759,9 @@ int qraf_cuda_matvec_q_host(const void* w_host, uint64_t w_size, uint32_t dtype,
         if (r) return r;
         if (s.y_map && s.status_map) return sm_copy(false, s.y_dev, s.y_map, yn);
         // no mapped host memory: the status word through a one-thread copy kernel, then copy engines
-        QRAF_CUDA_TRY(cudaLaunchKernelEx(&(const cudaLaunchConfig_t&)cudaLaunchConfig_t{dim3(1), dim3(1), 0, s.stream,
+        QRAF_CUDA_TRY(counted(cudaLaunchKernelEx(&(const cudaLaunchConfig_t&)cudaLaunchConfig_t{dim3(1), dim3(1), 0, s.stream,
                                                                                         nullptr, 0},
-                                         host_copy_kernel<false>, s.y_dev, s.y_dev, size_t{0}, s.status_dev));
+                                         host_copy_kernel<false>, s.y_dev, s.y_dev, size_t{0}, s.status_dev)));
         QRAF_CUDA_TRY(cudaMemcpyAsync(s.status_pinned, s.status_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost,
                                       s.stream));
         QRAF_CUDA_TRY(cudaMemcpyAsync(s.y_pinned, s.y_dev, yn * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
@@ -1810,3 +1851,4 @@ void qraf_fill_normal(uint32_t seed, float mean, float stddev, float* out_host, 
 }  // extern "C"
 
 #include "model_store.cuh"
+#include "decoder.cuh"

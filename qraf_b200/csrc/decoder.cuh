@@ -1,0 +1,662 @@
+// decoder.cuh — a Llama / Qwen2 decode step on the device for M slots at once
+// (continuous batching): qraf_cuda_decoder_*.  Included once, at the end of
+// capi.cu, after model_store.cuh.
+//
+// The reference runs one request at a time: Transformer::forward_llama
+// (src/nn/transformer.cpp:573-620) for one token, attention_forward and
+// mlp_forward (src/nn/attention.cpp:70-183), and its BatchScheduler calls that
+// forward request by request (include/runtime/batch_scheduler.h:187-228).  Here
+// one step takes M slots, each with its own token, position and KV cache, and
+// every projection of a layer runs once for all M rows:
+//   x = embedding[token]                                         (per slot)
+//   per layer:  q, k, v = RMSNorm(x) W_qkv (+ biases)            one launch
+//               a = attention(RoPE(q), cache + RoPE(k), v)       one launch: RoPE,
+//                                                                KV store, softmax
+//               x = x + a W_o                                    one launch
+//               h = silu(RMSNorm(x) W_gate) * (RMSNorm(x) W_up)  one launch
+//               x = x + h W_down                                 one launch
+//   logits = RMSNorm(x) W_lm_head                                one launch
+// The projections are the library's (any mode: EXACT, FAST, TC, AUTO), the
+// residual adds folded into their stores; every launch of a step after the
+// embedding uses programmatic dependent launch, so a projection streams its
+// weights while the launch before it finishes.  RoPE, softmax and SiLU use
+// CUDA's powf / cosf / sinf / expf where the reference calls the C library's.
+#pragma once
+
+namespace {
+
+constexpr uint32_t kAttnThreads = 256;
+constexpr uint32_t kAttnWarps = kAttnThreads / 32u;
+constexpr uint32_t kAttnMinChunk = 32;        // positions per CTA, at least (fewer CTAs for short sequences)
+constexpr uint32_t kAttnMaxGroup = 16;        // query heads per KV head, at most
+constexpr uint32_t kAttnMaxHeadDim = 256;
+constexpr uint32_t kAttnMaxSplits = 256;      // CTAs per (slot, KV head), at most
+constexpr uint64_t kAttnScoreBytes = 64 << 10;   // shared score buffer the split count aims under
+
+// x[m] = emb[tokens[m]]; a token outside the vocabulary gives zeros and raises
+// kErrBadLaunch.
+__global__ void __launch_bounds__(256) dec_embed_kernel(const float* __restrict__ emb, const int32_t* __restrict__ tokens,
+                                                        uint32_t vocab, uint32_t hidden, float* __restrict__ x) {
+    const int32_t tok = tokens[blockIdx.x];
+    const bool ok = tok >= 0 && static_cast<uint32_t>(tok) < vocab;
+    if (!ok && threadIdx.x == 0) raise_error(kErrBadLaunch);
+    float* xm = x + static_cast<size_t>(blockIdx.x) * hidden;
+    const float* row = emb + static_cast<size_t>(ok ? tok : 0) * hidden;
+    for (uint32_t i = threadIdx.x; i < hidden; i += blockDim.x) xm[i] = ok ? row[i] : 0.0f;
+}
+
+// The RoPE angles of every position (ops::rope, src/nn/ops.cpp:158-177): entry
+// [pos][i / 2] = (cos val, sin val) with freq = 1 / pow(theta, i / head_dim) and
+// val = pos * freq, for even i < head_dim: the expressions the reference
+// evaluates on every call, evaluated once when the decoder opens.
+__global__ void __launch_bounds__(256) dec_rope_table_kernel(float2* __restrict__ tab, uint32_t max_seq, uint32_t hd,
+                                                             float theta) {
+    const uint32_t half = hd / 2u;
+    for (size_t j = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < static_cast<size_t>(max_seq) * half;
+         j += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint32_t p = static_cast<uint32_t>(j / half), i = 2u * static_cast<uint32_t>(j % half);
+        const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn(static_cast<float>(i), static_cast<float>(hd))));
+        const float val = __fmul_rn(static_cast<float>(p), freq);
+        tab[j] = make_float2(cosf(val), sinf(val));
+    }
+}
+
+// (a, b) rotated by (c, s): (a c - b s, a s + b c), the reference's expressions.
+__device__ __forceinline__ float2 rope_pair(float a, float b, float2 cs) {
+    return make_float2(__fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y)),
+                       __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x)));
+}
+
+struct AttnParams {
+    const float* q;            // [M][heads * hd], before RoPE
+    const float* k;            // [M][kv_dim], before RoPE
+    const float* v;            // [M][kv_dim]
+    const float2* rope;        // [max_seq][hd / 2]
+    const int32_t* pos;        // [M]
+    const int32_t* slots;      // [M]
+    float* kc;                 // [max_slots][layers][max_seq][kv_dim]
+    float* vc;
+    float* out;                // [M][heads * hd]
+    float* part;               // [M][kv_heads][S][G][hd + 2]: unnormalised output, max, sum
+    uint32_t* counter;         // [M][kv_heads]: CTAs of the group finished (the last resets it)
+    uint32_t heads, kv_heads, hd, G, layer, layers, max_seq, max_slots;
+    uint32_t chunk_cap;        // floats per head row of the shared score buffer (>= positions per CTA, >= 2 S)
+    float scale;               // 1 / sqrt(head_dim)
+};
+
+// Attention of one step, fused with RoPE and the KV-cache store
+// (attention_forward, src/nn/attention.cpp:104-150).  CTA (s, kvh, m) takes slot
+// m's KV head kvh and the G = heads / kv_heads query heads that share it (the
+// reference's kv_h = h / kv_rep), over chunk s of positions 0 .. pos, so each K
+// and V row is read once for G heads.  The chunking follows the slot's position
+// on the device: chunk = ceil(seq / min(S, ceil(seq / 32))), S_eff =
+// ceil(seq / chunk) <= S working CTAs, each with at least one position.  The CTA
+// of the last chunk rotates the new k and stores k, v at pos in the slot's cache
+// (KVCache::store, attention.cpp:39-44) and reads them from shared memory.  Per
+// chunk: scores q.k_t * scale, then max, e_t = exp(score - max), their sum and
+// sum_t e_t v_t (the reference's softmax and weighted sum, src/nn/ops.cpp:242-259,
+// attention.cpp:128-147, with 1 / sum applied once at the end).  One chunk
+// writes the result; with several, each leaves a partial and the last CTA of the
+// group to finish (an atomic count, no waiting) merges them:
+// out = sum_c exp(max_c - max) o_c / sum_c exp(max_c - max) l_c.
+// Slots of one step must be distinct.  Launched with programmatic dependent
+// launch: all reads after griddepcontrol.wait.
+__global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnParams a) {
+    extern __shared__ float att_smem[];
+    __shared__ float s_max[kAttnMaxGroup], s_sum[kAttnMaxGroup];
+    __shared__ uint32_t s_last;
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint32_t s = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const int32_t p = a.pos[m], sl = a.slots[m];
+    if (!(p >= 0 && static_cast<uint32_t>(p) < a.max_seq && sl >= 0 && static_cast<uint32_t>(sl) < a.max_slots)) {
+        if (tid == 0 && s == 0 && kvh == 0) raise_error(kErrBadLaunch);
+        return;
+    }
+    const uint32_t seq = static_cast<uint32_t>(p) + 1u;
+    const uint32_t s0 = min(gridDim.x, (seq + kAttnMinChunk - 1u) / kAttnMinChunk);
+    const uint32_t chunk = (seq + s0 - 1u) / s0;
+    const uint32_t s_eff = (seq + chunk - 1u) / chunk;
+    if (s >= s_eff) return;
+    const uint32_t t0 = s * chunk, t1 = min(seq, t0 + chunk), n_t = t1 - t0;
+    const uint32_t G = a.G, hd = a.hd, half = hd / 2u, kv_dim = a.kv_heads * hd;
+    float* qs = att_smem;                       // [G][hd], rotated
+    float* knew = qs + G * hd;                  // [hd]: k at pos, rotated (last chunk)
+    float* vnew = knew + hd;                    // [hd]
+    float* sc = vnew + hd;                      // [G][chunk_cap]
+    const bool owner = (s == s_eff - 1u);
+    const float2* cs = a.rope + static_cast<size_t>(p) * half;
+    const float* qm = a.q + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
+    for (uint32_t j = tid; j < G * half; j += kAttnThreads) {
+        const uint32_t g = j / half, i = j - g * half;
+        const float2 r = rope_pair(qm[g * hd + 2u * i], qm[g * hd + 2u * i + 1u], cs[i]);
+        qs[g * hd + 2u * i] = r.x;
+        qs[g * hd + 2u * i + 1u] = r.y;
+    }
+    const size_t base =
+        (static_cast<size_t>(sl) * a.layers + a.layer) * a.max_seq * kv_dim + static_cast<size_t>(kvh) * hd;
+    if (owner) {
+        const float* km = a.k + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
+        const float* vm = a.v + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
+        float* kdst = a.kc + base + static_cast<size_t>(p) * kv_dim;
+        float* vdst = a.vc + base + static_cast<size_t>(p) * kv_dim;
+        for (uint32_t i = tid; i < half; i += kAttnThreads) {
+            const float2 r = rope_pair(km[2u * i], km[2u * i + 1u], cs[i]);
+            knew[2u * i] = r.x;
+            knew[2u * i + 1u] = r.y;
+            kdst[2u * i] = r.x;
+            kdst[2u * i + 1u] = r.y;
+        }
+        for (uint32_t d = tid; d < hd; d += kAttnThreads) {
+            const float x = vm[d];
+            vnew[d] = x;
+            vdst[d] = x;
+        }
+    }
+    __syncthreads();
+
+    // scores: one warp per position, lanes over the head dimension, the G dot
+    // products reduced together (independent shuffle chains)
+    for (uint32_t t = t0 + warp; t < t1; t += kAttnWarps) {
+        const float* kt = (t == static_cast<uint32_t>(p)) ? knew : a.kc + base + static_cast<size_t>(t) * kv_dim;
+        float kd[kAttnMaxHeadDim / 32];
+#pragma unroll
+        for (uint32_t j = 0; j < kAttnMaxHeadDim / 32; ++j) kd[j] = (lane + 32u * j < hd) ? kt[lane + 32u * j] : 0.0f;
+        float acc[kAttnMaxGroup];
+#pragma unroll
+        for (uint32_t g = 0; g < kAttnMaxGroup; ++g) {
+            acc[g] = 0.0f;
+            if (g < G) {
+#pragma unroll
+                for (uint32_t j = 0; j < kAttnMaxHeadDim / 32; ++j)
+                    if (lane + 32u * j < hd) acc[g] = __fadd_rn(acc[g], __fmul_rn(qs[g * hd + lane + 32u * j], kd[j]));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (uint32_t g = 0; g < kAttnMaxGroup; ++g)
+                if (g < G) acc[g] = __fadd_rn(acc[g], __shfl_xor_sync(0xFFFFFFFFu, acc[g], o));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (uint32_t g = 0; g < kAttnMaxGroup; ++g)
+                if (g < G) sc[g * a.chunk_cap + (t - t0)] = __fmul_rn(acc[g], a.scale);
+        }
+    }
+    __syncthreads();
+
+    // the chunk's softmax terms: one warp per head
+    for (uint32_t g = warp; g < G; g += kAttnWarps) {
+        float* row = sc + g * a.chunk_cap;
+        float mx = -INFINITY;
+        for (uint32_t t = lane; t < n_t; t += 32u) mx = fmaxf(mx, row[t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        float sum = 0.0f;
+        for (uint32_t t = lane; t < n_t; t += 32u) {
+            const float e = expf(__fsub_rn(row[t], mx));
+            row[t] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) {
+            s_max[g] = mx;
+            s_sum[g] = sum;
+        }
+    }
+    __syncthreads();
+
+    // sum_t e_t v_t: thread (set, d) for the heads set, set + nsets, ...
+    const uint32_t nsets = kAttnThreads / hd;
+    const uint32_t d = tid % hd, set = tid / hd;
+    const bool active = set < nsets;
+    float acc[kAttnMaxGroup];
+#pragma unroll
+    for (uint32_t i = 0; i < kAttnMaxGroup; ++i) acc[i] = 0.0f;
+    if (active) {
+        for (uint32_t t = t0; t < t1; ++t) {
+            const float vd = (t == static_cast<uint32_t>(p)) ? vnew[d] : a.vc[base + static_cast<size_t>(t) * kv_dim + d];
+#pragma unroll
+            for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+                const uint32_t g = set + i * nsets;
+                if (g < G) acc[i] = __fadd_rn(acc[i], __fmul_rn(sc[g * a.chunk_cap + (t - t0)], vd));
+            }
+        }
+    }
+    float* om = a.out + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
+    if (s_eff == 1u) {
+        if (active) {
+#pragma unroll
+            for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+                const uint32_t g = set + i * nsets;
+                if (g < G) om[g * hd + d] = __fmul_rn(acc[i], __fdiv_rn(1.0f, s_sum[g]));
+            }
+        }
+        return;
+    }
+    const size_t rec = hd + 2u;
+    float* pg = a.part + ((static_cast<size_t>(m) * a.kv_heads + kvh) * gridDim.x) * G * rec;
+    if (active) {
+#pragma unroll
+        for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+            const uint32_t g = set + i * nsets;
+            if (g < G) {
+                float* r = pg + (static_cast<size_t>(s) * G + g) * rec;
+                r[d] = acc[i];
+                if (d == 0) {
+                    r[hd] = s_max[g];
+                    r[hd + 1u] = s_sum[g];
+                }
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t* c = a.counter + static_cast<size_t>(m) * a.kv_heads + kvh;
+        s_last = (atomicAdd(c, 1u) == s_eff - 1u) ? 1u : 0u;
+        if (s_last) *c = 0u;      // every CTA of the group has counted: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // merge: the chunks' (max, sum) into shared memory in one round of loads
+    // (sc is free now and holds 2 * S * G floats), per head the overall max and
+    // the chunk weights exp(max_c - max), then each output's weighted sum
+    float* pm = sc;                      // [s_eff][G]: max_c, then the weight of chunk c
+    float* pl = sc + s_eff * G;          // [s_eff][G]: sum_c
+    for (uint32_t j = tid; j < s_eff * G; j += kAttnThreads) {
+        const float* r = pg + static_cast<size_t>(j) * rec;
+        pm[j] = __ldcg(r + hd);
+        pl[j] = __ldcg(r + hd + 1u);
+    }
+    __syncthreads();
+    for (uint32_t g = warp; g < G; g += kAttnWarps) {
+        float mx = -INFINITY;
+        for (uint32_t c = lane; c < s_eff; c += 32u) mx = fmaxf(mx, pm[c * G + g]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        float l = 0.0f;
+        for (uint32_t c = lane; c < s_eff; c += 32u) {
+            const float w = expf(__fsub_rn(pm[c * G + g], mx));
+            pm[c * G + g] = w;
+            l = __fadd_rn(l, __fmul_rn(w, pl[c * G + g]));
+        }
+        l = warp_sum(l);
+        if (lane == 0) s_sum[g] = l;
+    }
+    __syncthreads();
+    for (uint32_t j = tid; j < G * hd; j += kAttnThreads) {
+        const uint32_t g = j / hd, dd = j - g * hd;
+        float o = 0.0f;
+#pragma unroll 4
+        for (uint32_t c = 0; c < s_eff; ++c)
+            o = __fadd_rn(o, __fmul_rn(pm[c * G + g], __ldcg(pg + (static_cast<size_t>(c) * G + g) * rec + dd)));
+        om[g * hd + dd] = __fmul_rn(o, __fdiv_rn(1.0f, s_sum[g]));
+    }
+}
+
+// logits[m][r] = dot(W[r], x[m]) for an F32 LM head (a tied embedding,
+// dispatch_matvec_opt at transformer.cpp:607-609): one warp per (row, vector),
+// lane stripes then a warp sum.
+__global__ void __launch_bounds__(256) dec_f32_matvec_kernel(const float* __restrict__ w, const float* __restrict__ x,
+                                                             uint32_t rows, uint32_t cols, uint32_t M,
+                                                             float* __restrict__ y) {
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31u;
+    if (warp >= rows * M) return;
+    const uint32_t m = warp / rows, r = warp - m * rows;
+    const float* wr = w + static_cast<size_t>(r) * cols;
+    const float* xm = x + static_cast<size_t>(m) * cols;
+    float acc = 0.0f;
+    for (uint32_t i = lane; i < cols; i += 32u) acc = fmaf(wr[i], xm[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) y[static_cast<size_t>(m) * rows + r] = acc;
+}
+
+struct DecLayer {
+    qraf_weight_t qkv[3], o, gate, up, down;
+    const float* attn_norm = nullptr;
+    const float* ffn_norm = nullptr;
+    const float* bias[3] = {nullptr, nullptr, nullptr};
+};
+
+}  // namespace
+
+struct qraf_decoder {
+    qraf_model* model = nullptr;
+    int device = 0;
+    uint32_t vocab = 0, hidden = 0, layers = 0, heads = 0, kv_heads = 0, hd = 0, inter = 0, G = 1;
+    uint32_t max_slots = 0, max_seq = 0;
+    float theta = 10000.0f, eps = 1e-5f;
+    const float* emb = nullptr;
+    const float* out_norm = nullptr;
+    bool tied = false;
+    qraf_weight_t lm_head{};
+    std::vector<DecLayer> L;
+    float* kc = nullptr;          // [max_slots][layers][max_seq][kv_dim]
+    float* vc = nullptr;
+    float2* rope = nullptr;       // [max_seq][hd / 2]
+    float* part = nullptr;        // attention partials, sized for the largest step
+    uint32_t* counter = nullptr;  // [max_slots][kv_heads]
+    float* work = nullptr;        // x, q, k, v, attention output, h, normalised x (tied head)
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr, *xn = nullptr;
+};
+
+namespace {
+
+// CTAs per (slot, KV head) of a step of M slots: about two per SM over the
+// step, at most one per 32 positions of max_seq, and enough that a chunk's
+// scores fit the shared buffer.
+uint32_t attn_splits(const qraf_decoder* d, uint32_t M, int sm_count) {
+    const uint32_t by_len = std::max<uint32_t>(1u, (d->max_seq + kAttnMinChunk - 1u) / kAttnMinChunk);
+    const uint32_t groups = M * d->kv_heads;
+    const uint32_t target = std::max<uint32_t>(1u, (2u * static_cast<uint32_t>(sm_count) + groups - 1u) / groups);
+    uint32_t S = std::min(by_len, target);
+    const uint64_t need = (static_cast<uint64_t>(d->G) * d->max_seq * 4u + kAttnScoreBytes - 1u) / kAttnScoreBytes;
+    S = std::max<uint32_t>(S, static_cast<uint32_t>(std::min<uint64_t>(need, by_len)));
+    return std::max<uint32_t>(1u, std::min(S, kAttnMaxSplits));
+}
+
+uint32_t attn_chunk_cap(const qraf_decoder* d, uint32_t S) {
+    return std::max({kAttnMinChunk, (d->max_seq + S - 1u) / S, 2u * S});
+}
+
+size_t attn_smem_bytes(const qraf_decoder* d, uint32_t S) {
+    return (static_cast<size_t>(d->G) * d->hd + 2u * d->hd + static_cast<size_t>(d->G) * attn_chunk_cap(d, S)) *
+           sizeof(float);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qraf_cuda_decoder_close(qraf_decoder_t d) {
+    if (!d) return QRAF_OK;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    for (void* p : {static_cast<void*>(d->kc), static_cast<void*>(d->vc), static_cast<void*>(d->rope),
+                    static_cast<void*>(d->part), static_cast<void*>(d->counter), static_cast<void*>(d->work)})
+        if (p) cudaFree(p);
+    cudaSetDevice(cur);
+    if (d->model) qraf_cuda_model_close(d->model);
+    delete d;
+    return QRAF_OK;
+}
+
+int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_seq, qraf_decoder_t* out) {
+    if (!out) return fail(QRAF_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    if (max_slots == 0 || max_seq == 0) return fail(QRAF_ERR_INVALID, "max_slots and max_seq must be positive");
+    if (max_slots > 65535u || max_seq > (1u << 24))
+        return fail(QRAF_ERR_UNSUPPORTED, "max_slots above 65535 or max_seq above 2^24");
+    qraf_model_t m = nullptr;
+    int rc = qraf_cuda_model_open_ex(path, QRAF_MODEL_F32, &m);
+    if (rc) return rc;
+    std::unique_ptr<qraf_decoder> d(new qraf_decoder());
+    d->model = m;
+    d->device = m->device;
+    auto cfg = [&](const char* key, uint32_t def) {
+        auto it = m->config.find(key);
+        return it == m->config.end() ? def : it->second;
+    };
+    auto cfgf = [&](const char* key, float def) {
+        auto it = m->config.find(key);
+        if (it == m->config.end()) return def;
+        float f;
+        std::memcpy(&f, &it->second, sizeof(f));
+        return f;
+    };
+    auto fail_close = [&](int code, const std::string& msg) {
+        qraf_cuda_decoder_close(d.release());
+        return fail(code, "%s: %s", path, msg.c_str());
+    };
+    const auto arch = m->config_str.count("architecture") ? m->config_str["architecture"] : std::string("llama");
+    if (arch != "llama" && arch != "qwen2" && arch != "mistral")
+        return fail_close(QRAF_ERR_UNSUPPORTED, "architecture '" + arch + "' (the decoder runs llama / qwen2 / mistral)");
+    d->vocab = cfg("vocab_size", 0);
+    d->hidden = cfg("hidden_size", 0);
+    d->layers = cfg("num_layers", 0);
+    d->heads = cfg("num_heads", 0);
+    d->kv_heads = cfg("num_kv_heads", 0);
+    if (d->kv_heads == 0) d->kv_heads = d->heads;
+    d->inter = cfg("intermediate_size", 0);
+    d->theta = cfgf("rope_theta", 10000.0f);
+    d->eps = cfgf("rms_norm_eps", 1e-5f);
+    if (!d->vocab || !d->hidden || !d->layers || !d->heads || !d->inter || d->hidden % d->heads ||
+        d->heads % d->kv_heads)
+        return fail_close(QRAF_ERR_INVALID,
+                          "config lacks vocab / hidden / layers / heads / intermediate sizes or has inconsistent heads");
+    d->hd = d->hidden / d->heads;
+    d->G = d->heads / d->kv_heads;
+    if (d->hd % 2u || d->hd > kAttnMaxHeadDim)
+        return fail_close(QRAF_ERR_UNSUPPORTED, "head_dim must be even and at most 256");
+    if (d->G > kAttnMaxGroup) return fail_close(QRAF_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
+    if (d->hidden % 8u) return fail_close(QRAF_ERR_UNSUPPORTED, "hidden_size must be a multiple of 8");
+    d->max_slots = max_slots;
+    d->max_seq = max_seq;
+    auto f32 = [&](const std::string& name, uint64_t count, const float** outp, bool required) -> bool {
+        auto it = m->f32.find(name);
+        if (it == m->f32.end() || it->second.second != count) {
+            if (required)
+                fail(QRAF_ERR_INVALID, "%s: F32 tensor '%s' of %llu elements missing", path, name.c_str(),
+                     static_cast<unsigned long long>(count));
+            *outp = nullptr;
+            return !required;
+        }
+        *outp = it->second.first;
+        return true;
+    };
+    auto qw = [&](const std::string& name, uint32_t rows, uint32_t cols, qraf_weight_t* w) -> bool {
+        auto it = m->weights.find(name);
+        if (it == m->weights.end() || it->second.rows != rows || it->second.cols != cols) {
+            fail(QRAF_ERR_INVALID, "%s: quantized tensor '%s' [%u][%u] missing", path, name.c_str(), rows, cols);
+            return false;
+        }
+        *w = it->second;
+        return true;
+    };
+    const uint32_t q_dim = d->heads * d->hd, kv_dim = d->kv_heads * d->hd;
+    bool ok = f32("model.embed_tokens.weight", static_cast<uint64_t>(d->vocab) * d->hidden, &d->emb, true) &&
+              f32("model.norm.weight", d->hidden, &d->out_norm, true);
+    d->L.resize(d->layers);
+    for (uint32_t l = 0; ok && l < d->layers; ++l) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        DecLayer& ly = d->L[l];
+        ok = qw(p + "self_attn.q_proj.weight", q_dim, d->hidden, &ly.qkv[0]) &&
+             qw(p + "self_attn.k_proj.weight", kv_dim, d->hidden, &ly.qkv[1]) &&
+             qw(p + "self_attn.v_proj.weight", kv_dim, d->hidden, &ly.qkv[2]) &&
+             qw(p + "self_attn.o_proj.weight", d->hidden, q_dim, &ly.o) &&
+             qw(p + "mlp.gate_proj.weight", d->inter, d->hidden, &ly.gate) &&
+             qw(p + "mlp.up_proj.weight", d->inter, d->hidden, &ly.up) &&
+             qw(p + "mlp.down_proj.weight", d->hidden, d->inter, &ly.down) &&
+             f32(p + "input_layernorm.weight", d->hidden, &ly.attn_norm, true) &&
+             f32(p + "post_attention_layernorm.weight", d->hidden, &ly.ffn_norm, true) &&
+             f32(p + "self_attn.q_proj.bias", q_dim, &ly.bias[0], false) &&
+             f32(p + "self_attn.k_proj.bias", kv_dim, &ly.bias[1], false) &&
+             f32(p + "self_attn.v_proj.bias", kv_dim, &ly.bias[2], false);
+    }
+    if (!ok) {
+        const std::string msg = t_last_error;
+        qraf_cuda_decoder_close(d.release());
+        t_last_error = msg;
+        return QRAF_ERR_INVALID;
+    }
+    // the LM head: lm_head.weight (quantized or F32), else the embedding (tied,
+    // transformer.cpp:374-400)
+    if (m->weights.count("lm_head.weight")) {
+        if (!qw("lm_head.weight", d->vocab, d->hidden, &d->lm_head)) return fail_close(QRAF_ERR_INVALID, t_last_error);
+    } else {
+        const float* head = nullptr;
+        f32("lm_head.weight", static_cast<uint64_t>(d->vocab) * d->hidden, &head, false);
+        d->tied = true;
+        d->lm_head.data = head ? head : d->emb;
+    }
+    DeviceInfo* dev = nullptr;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    rc = ensure_device(nullptr, &dev);
+    if (rc) {
+        cudaSetDevice(cur);
+        const std::string msg = t_last_error;
+        qraf_cuda_decoder_close(d.release());
+        t_last_error = msg;
+        return rc;
+    }
+    // attention: the largest partial buffer and shared-memory need over steps of 1 .. max_slots slots
+    uint64_t part_floats = 0;
+    size_t smem_max = 0;
+    for (uint32_t M = 1; M <= max_slots; ++M) {
+        const uint32_t S = attn_splits(d.get(), M, dev->sm_count);
+        part_floats = std::max<uint64_t>(part_floats, static_cast<uint64_t>(M) * d->heads * S * (d->hd + 2u));
+        smem_max = std::max(smem_max, attn_smem_bytes(d.get(), S));
+    }
+    if (smem_max + kSmemReserve > static_cast<size_t>(dev->smem_optin)) {
+        cudaSetDevice(cur);
+        return fail_close(QRAF_ERR_UNSUPPORTED, "max_seq " + std::to_string(max_seq) + " needs " +
+                                                    std::to_string(smem_max) + " bytes of shared memory per CTA");
+    }
+    const uint64_t cache = static_cast<uint64_t>(max_slots) * d->layers * max_seq * kv_dim;
+    const size_t ws = static_cast<size_t>(max_slots) * (2u * d->hidden + 2u * q_dim + 2u * kv_dim + d->inter);
+    const size_t rope_n = static_cast<size_t>(max_seq) * (d->hd / 2u);
+    bool alloc_ok = cudaMalloc(&d->kc, cache * sizeof(float)) == cudaSuccess &&
+                    cudaMalloc(&d->vc, cache * sizeof(float)) == cudaSuccess &&
+                    cudaMalloc(&d->rope, rope_n * sizeof(float2)) == cudaSuccess &&
+                    cudaMalloc(&d->part, std::max<uint64_t>(part_floats, 1) * sizeof(float)) == cudaSuccess &&
+                    cudaMalloc(&d->counter, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t)) ==
+                        cudaSuccess &&
+                    cudaMalloc(&d->work, ws * sizeof(float)) == cudaSuccess;
+    cudaError_t e = cudaSuccess;
+    if (alloc_ok) {
+        e = cudaMemset(d->kc, 0, cache * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(d->vc, 0, cache * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemset(d->counter, 0, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(smem_max));
+        if (e == cudaSuccess) {
+            (dec_rope_table_kernel<<<static_cast<unsigned>(std::min<size_t>((rope_n + 255) / 256, 4u * dev->sm_count)),
+                                     256>>>(d->rope, max_seq, d->hd, d->theta), count_launch());
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    cudaSetDevice(cur);
+    if (!alloc_ok) {
+        cudaGetLastError();
+        return fail_close(QRAF_ERR_NOMEM, "the KV caches and work buffers (" +
+                                              std::to_string(2 * cache * 4 + ws * 4 + part_floats * 4) +
+                                              " bytes) could not be allocated");
+    }
+    if (e != cudaSuccess) return fail_close(QRAF_ERR_CUDA, std::string("decoder set-up: ") + cudaGetErrorString(e));
+    float* w = d->work;
+    d->x = w;   w += static_cast<size_t>(max_slots) * d->hidden;
+    d->q = w;   w += static_cast<size_t>(max_slots) * q_dim;
+    d->k = w;   w += static_cast<size_t>(max_slots) * kv_dim;
+    d->v = w;   w += static_cast<size_t>(max_slots) * kv_dim;
+    d->att = w; w += static_cast<size_t>(max_slots) * q_dim;
+    d->h = w;   w += static_cast<size_t>(max_slots) * d->inter;
+    d->xn = w;
+    *out = d.release();
+    return QRAF_OK;
+}
+
+int qraf_cuda_decoder_info(qraf_decoder_t d, uint32_t* vocab, uint32_t* hidden, uint32_t* layers, uint32_t* max_slots,
+                           uint32_t* max_seq) {
+    if (!d) return fail(QRAF_ERR_INVALID, "decoder is NULL");
+    if (vocab) *vocab = d->vocab;
+    if (hidden) *hidden = d->hidden;
+    if (layers) *layers = d->layers;
+    if (max_slots) *max_slots = d->max_slots;
+    if (max_seq) *max_seq = d->max_seq;
+    return QRAF_OK;
+}
+
+int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_dev, const int32_t* pos_dev,
+                           const int32_t* slots_dev, float* logits_dev, int mode, void* stream) {
+    if (!d) return fail(QRAF_ERR_INVALID, "decoder is NULL");
+    if (M == 0) return QRAF_OK;
+    if (M > d->max_slots) return fail(QRAF_ERR_INVALID, "M = %u exceeds max_slots = %u", M, d->max_slots);
+    if (!tokens_dev || !pos_dev || !slots_dev || !logits_dev) return fail(QRAF_ERR_INVALID, "a pointer is NULL");
+    const int base_mode = mode & 0xFF;
+    if (base_mode != QRAF_MODE_EXACT && base_mode != QRAF_MODE_FAST && base_mode != QRAF_MODE_TC &&
+        base_mode != QRAF_MODE_AUTO)
+        return fail(QRAF_ERR_INVALID, "unknown mode %d", mode);
+    const int pmode = base_mode | QRAF_MODE_FLAG_OVERLAP;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    DeviceInfo* dev = nullptr;
+    int cur = 0;
+    int rc = ensure_device(&cur, &dev);
+    if (rc) return rc;
+    if (cur != d->device)
+        return fail(QRAF_ERR_INVALID, "the decoder lives on device %d, the current device is %d", d->device, cur);
+    const uint32_t S = attn_splits(d, M, dev->sm_count);
+    AttnParams ap{};
+    ap.q = d->q;
+    ap.k = d->k;
+    ap.v = d->v;
+    ap.rope = d->rope;
+    ap.pos = pos_dev;
+    ap.slots = slots_dev;
+    ap.kc = d->kc;
+    ap.vc = d->vc;
+    ap.out = d->att;
+    ap.part = d->part;
+    ap.counter = d->counter;
+    ap.heads = d->heads;
+    ap.kv_heads = d->kv_heads;
+    ap.hd = d->hd;
+    ap.G = d->G;
+    ap.layers = d->layers;
+    ap.max_seq = d->max_seq;
+    ap.max_slots = d->max_slots;
+    ap.chunk_cap = attn_chunk_cap(d, S);
+    ap.scale = 1.0f / std::sqrt(static_cast<float>(d->hd));   // attention.cpp:118, IEEE on the host as there
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, d->kv_heads, M);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = attn_smem_bytes(d, S);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+
+    (dec_embed_kernel<<<M, 256, 0, st>>>(d->emb, tokens_dev, d->vocab, d->hidden, d->x), count_launch());
+    QRAF_CUDA_TRY(cudaGetLastError());
+    for (uint32_t l = 0; l < d->layers; ++l) {
+        const DecLayer& ly = d->L[l];
+        float* qkv_out[3] = {d->q, d->k, d->v};
+        const float* biases[3] = {ly.bias[0], ly.bias[1], ly.bias[2]};
+        const bool any_bias = biases[0] || biases[1] || biases[2];
+        rc = multi_impl(ly.qkv, 3, d->x, ly.attn_norm, d->eps, any_bias ? biases : nullptr, qkv_out, M, pmode, st);
+        if (rc) return rc;
+        ap.layer = l;
+        QRAF_CUDA_TRY(counted(cudaLaunchKernelEx(&cfg, dec_attention_kernel, ap)));
+        rc = matvec_impl(&ly.o, d->att, d->x, M, pmode, st, true);
+        if (rc) return rc;
+        rc = swiglu_impl(&ly.gate, &ly.up, d->x, ly.ffn_norm, d->eps, d->h, M, pmode, st);
+        if (rc) return rc;
+        rc = matvec_impl(&ly.down, d->h, d->x, M, pmode, st, true);
+        if (rc) return rc;
+    }
+    if (!d->tied) {
+        float* outs[1] = {logits_dev};
+        return multi_impl(&d->lm_head, 1, d->x, d->out_norm, d->eps, nullptr, outs, M, pmode, st);
+    }
+    (rmsnorm_kernel<<<M, 256, 0, st>>>(d->x, d->out_norm, d->eps, d->hidden, d->xn, base_mode == QRAF_MODE_EXACT),
+     count_launch());
+    QRAF_CUDA_TRY(cudaGetLastError());
+    const size_t warps = static_cast<size_t>(d->vocab) * M;
+    (dec_f32_matvec_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
+         static_cast<const float*>(d->lm_head.data), d->xn, d->vocab, d->hidden, M, logits_dev),
+     count_launch());
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+}  // extern "C"

@@ -99,6 +99,10 @@ struct RowParams {
     const float* norm_w;
     float norm_eps;
     const float* seg_b[kMaxSeg];
+    // accumulate = 1 (one weight, unsharded): y = fl(W x + y), the residual add of
+    // a projection whose output joins the residual stream (src/nn/transformer.cpp:593,
+    // :601); each element is read and written by the one thread that stores it.
+    uint32_t accumulate;
     // Row-sharded launch (world > 0): this GPU computes rows [row_off, row_off + N)
     // of a y with y_ld rows in all (the ranks' row ranges partition them).  Each
     // output element goes into this rank's y and, as one 8-byte word (call number
@@ -151,7 +155,9 @@ __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uin
     if (p.world == 0) {
         if (p.nseg <= 1) {
             if (p.seg_b[0]) t = __fadd_rn(t, p.seg_b[0][row]);
-            p.y[static_cast<size_t>(v) * p.N + row] = t;
+            float* dst = p.y + static_cast<size_t>(v) * p.N + row;
+            if (p.accumulate) t = __fadd_rn(t, *dst);
+            *dst = t;
         } else {
             const uint32_t i = seg_of(p, row);
             const uint32_t r = row - p.seg_row0[i];
