@@ -17,7 +17,8 @@ timed steps; roofline.achieved is the same bytes per launch over the average
 launch duration in that timed region.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>][_shard]|<model>_token[_m<M>]]
+                  [--workload q4_4096x4096|q8_4096x4096|<q4|q8>_<N>x<K>[_m<M>][_shard]|<model>_token[_m<M>]
+                             |qwen3b_decode[_m<M>][_c<context>]]
                   [--mode fast|exact|tc|auto]
 
 Under torch.distributed.run (WORLD_SIZE > 1) the default workload is the
@@ -1094,6 +1095,309 @@ def run_token_reference(args, model, m):
 
 
 
+# ── decode workloads: the whole decode step (qraf_cuda_decoder_step) ──────
+# BASELINE.json config 3's shapes as a Qwen2 model file: every projection, the
+# attention over each slot's KV cache, RoPE, the norms, SwiGLU, the residuals.
+DECODE_MODELS = {
+    "qwen3b": {"arch": "qwen2", "heads": 16, "kv_heads": 2, "inter": 11008},
+}
+DECODE_METRIC = "decode tokens/s"
+
+
+def parse_decode_workload(name: str):
+    """'qwen3b_decode' / 'qwen3b_decode_m8_c1024' -> (model, M slots, context length), else None."""
+    parts = name.split("_")
+    if len(parts) < 2 or parts[0] not in DECODE_MODELS or parts[1] != "decode":
+        return None
+    m, ctx = 1, 512
+    for p in parts[2:]:
+        if p.startswith("m") and p[1:].isdigit():
+            m = int(p[1:])
+        elif p.startswith("c") and p[1:].isdigit():
+            ctx = int(p[1:])
+        else:
+            raise SystemExit(f"unknown decode workload part '{p}' in {name}")
+    return parts[0], m, ctx
+
+
+def decode_shapes(model):
+    tok, dec = TOKEN_MODELS[model], DECODE_MODELS[model]
+    hidden, heads, kvh, inter = tok["hidden"], dec["heads"], dec["kv_heads"], dec["inter"]
+    hd = hidden // heads
+    return {"q_proj": (heads * hd, hidden), "k_proj": (kvh * hd, hidden), "v_proj": (kvh * hd, hidden),
+            "o_proj": (hidden, heads * hd), "gate_proj": (inter, hidden), "up_proj": (inter, hidden),
+            "down_proj": (hidden, inter)}
+
+
+def write_decode_file(model, path, fill, quantize, max_seq):
+    """The model as a .qraf file that the reference's Transformer loads
+    (src/nn/transformer.cpp:96-126, :320-400).  Each projection shape is one
+    std::mt19937(42) N(0, 0.02) draw over the whole tensor, quantized once and
+    written into every layer; the LM head is the draw of its shape, quantized, and
+    the F32 embedding is that same draw; norms 1 + N(0, 0.1) (seed 45) and Qwen2's
+    Q/K/V biases N(0, 0.1) (seed 46).  fill(seed, std, n) and quantize(dtype,
+    w[n][k]) -> bytes are the caller's.  Returns the file's size in bytes."""
+    from qraf_b200 import qraf_file as qf
+
+    tok, dec = TOKEN_MODELS[model], DECODE_MODELS[model]
+    dt, hidden, vocab, layers = tok["dtype"], tok["hidden"], tok["vocab"], tok["layers"]
+    shapes = decode_shapes(model)
+    w = qf.QrafFileWriter()
+    for key, v in (("architecture", dec["arch"]), ("vocab_size", vocab), ("hidden_size", hidden),
+                   ("num_layers", layers), ("num_heads", dec["heads"]), ("num_kv_heads", dec["kv_heads"]),
+                   ("intermediate_size", dec["inter"]), ("max_seq_len", max_seq), ("rope_theta", 1000000.0),
+                   ("rms_norm_eps", 1e-6)):
+        (w.set_config_string if isinstance(v, str) else w.set_config)(key, v)
+    scheme = w.add_quant_scheme(dt, 32, 1)
+    qbytes = {}
+    for n, k in sorted(set(shapes.values())):
+        qbytes[(n, k)] = bytes(quantize(dt, fill(42, 0.02, n * k).reshape(n, k)))
+    head = fill(42, 0.02, vocab * hidden).reshape(vocab, hidden)
+    w.add_tensor("model.embed_tokens.weight", (vocab, hidden), qf.DTYPE_F32, head.tobytes())
+    head_q = bytes(quantize(dt, head))
+    del head
+    norms = fill(45, 0.1, (2 * layers + 1) * hidden) + np.float32(1.0)
+    q_dim, kv_dim = shapes["q_proj"][0], shapes["k_proj"][0]
+    biases = fill(46, 0.1, layers * (q_dim + 2 * kv_dim))
+    for l in range(layers):
+        p = f"model.layers.{l}."
+        w.add_tensor(p + "input_layernorm.weight", (hidden,), qf.DTYPE_F32, norms[2 * l * hidden:(2 * l + 1) * hidden])
+        for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            w.add_tensor(p + f"self_attn.{name}.weight", shapes[name], dt, qbytes[shapes[name]], scheme)
+        if dec["arch"] == "qwen2":
+            off = l * (q_dim + 2 * kv_dim)
+            for name, a, b in (("q_proj", 0, q_dim), ("k_proj", q_dim, q_dim + kv_dim),
+                               ("v_proj", q_dim + kv_dim, q_dim + 2 * kv_dim)):
+                w.add_tensor(p + f"self_attn.{name}.bias", (b - a,), qf.DTYPE_F32, biases[off + a:off + b])
+        w.add_tensor(p + "post_attention_layernorm.weight", (hidden,), qf.DTYPE_F32,
+                     norms[(2 * l + 1) * hidden:(2 * l + 2) * hidden])
+        for name in ("gate_proj", "up_proj", "down_proj"):
+            w.add_tensor(p + f"mlp.{name}.weight", shapes[name], dt, qbytes[shapes[name]], scheme)
+    w.add_tensor("model.norm.weight", (hidden,), qf.DTYPE_F32, norms[2 * layers * hidden:])
+    w.add_tensor("lm_head.weight", (vocab, hidden), dt, head_q, scheme)
+    return w.write(path)
+
+
+def decode_file_path(model):
+    """A scratch path for the model file: /dev/shm when it has room, else the temp directory."""
+    import shutil
+    import tempfile
+
+    tok = TOKEN_MODELS[model]
+    need = 3 * tok["vocab"] * tok["hidden"] * 4 + tok["layers"] * 10 ** 8
+    d = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > need else \
+        tempfile.gettempdir()
+    return os.path.join(d, f"qraf_bench_{model}_{os.getpid()}.qraf")
+
+
+def decode_bytes_per_step(model, m, ctx):
+    """Algorithmic HBM bytes of one decode step of M slots at position ctx: every
+    quantized weight once, the F32 norms and biases, each slot's embedding row,
+    its K and V over ctx + 1 positions of every layer, and the step's K/V writes.
+    Returns (total, weights)."""
+    tok = TOKEN_MODELS[model]
+    shapes = decode_shapes(model)
+    bb = BLOCK_BYTES[tok["dtype"]]
+    layers, hidden, vocab = tok["layers"], tok["hidden"], tok["vocab"]
+    weights = layers * sum(n * (k // 32) * bb for n, k in shapes.values()) + vocab * (hidden // 32) * bb
+    kv_dim = shapes["k_proj"][0]
+    small = 4 * ((2 * layers + 1) * hidden + layers * (shapes["q_proj"][0] + 2 * kv_dim))
+    kv = m * layers * (ctx + 1) * kv_dim * 4 * 2 + m * layers * kv_dim * 4 * 2
+    return weights + small + m * hidden * 4 + kv, weights
+
+
+def run_decode(args, model, m, ctx):
+    """One STEP = one decode token for each of M slots through the whole model
+    (qraf_cuda_decoder_step over a .qraf file written here), every slot at
+    position ctx with ctx positions of its KV cache filled by earlier steps;
+    captured once as a CUDA graph and replayed (every replay recomputes the
+    position-ctx token and rewrites its K/V).  value = M x steps / device time."""
+    import torch
+
+    import qraf_b200 as qb
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("decode workloads run on one GPU (replicas only)")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    qb.init(0)
+    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
+
+    def fill(seed, std, n):
+        return qb.fill_normal(seed, 0.0, std, n)
+
+    def quantize(dtype, w2d):
+        return qb.quantize_rows(dtype, torch.from_numpy(w2d).to(dev), 32).cpu().numpy()
+
+    path = decode_file_path(model)
+    try:
+        t_w = time.perf_counter()
+        file_bytes = write_decode_file(model, path, fill, quantize, max_seq=ctx + 1)
+        t_w = time.perf_counter() - t_w
+        t_o = time.perf_counter()
+        dec = qb.Decoder(path, max_slots=m, max_seq=ctx + 1)
+        t_o = time.perf_counter() - t_o
+        line = _decode_measure(args, model, m, ctx, dec, mode)
+        line["config"].update({"file_bytes": file_bytes, "write_s": round(t_w, 2), "open_s": round(t_o, 2)})
+        dec.close()
+        line["cpu_baseline"] = decode_cpu_baseline(model, ctx, args.cpu_seconds, path) if args.cpu_seconds > 0 \
+            else None
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    print(json.dumps(line), flush=True)
+
+
+def _decode_measure(args, model, m, ctx, dec, mode):
+    import torch
+
+    import qraf_b200 as qb
+
+    dev = torch.device("cuda", 0)
+    tok = TOKEN_MODELS[model]
+    dt, vocab = tok["dtype"], tok["vocab"]
+    rng = np.random.default_rng(47)
+    prompt = torch.from_numpy(rng.integers(0, vocab, size=(ctx + 1, m)).astype(np.int32)).to(dev)
+    slots = torch.arange(m, dtype=torch.int32, device=dev)
+    logits = torch.empty((m, vocab), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        for p in range(ctx):      # fill positions 0 .. ctx-1 of every slot's cache
+            pos_p = torch.full((m,), p, dtype=torch.int32, device=dev)
+            dec.step(prompt[p], pos_p, slots, mode=mode, logits=logits, stream=s)
+    torch.cuda.synchronize(dev)
+    tokens = prompt[ctx].clone()
+    pos = torch.full((m,), ctx, dtype=torch.int32, device=dev)
+    launches0 = qb.launch_count()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        dec.step(tokens, pos, slots, mode=mode, logits=logits, stream=s)
+    per_step = qb.launch_count() - launches0
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    if qb.device_status() != qb.OK:
+        raise SystemExit("device status not OK after warm-up")
+
+    clocks = ClockSampler(0)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    with torch.cuda.stream(s):
+        t0.record()
+        for _ in range(args.steps):
+            g.replay()
+        t1.record()
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+
+    # e2e: the user's call (Decoder.step, no graph) with the step's tokens copied in
+    # from pinned host memory and its logits copied out, every step.
+    tok_host = prompt[ctx].cpu().pin_memory()
+    lg_host = torch.empty((m, vocab), dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 50))
+    te = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(s):
+            tokens.copy_(tok_host, non_blocking=True)
+            dec.step(tokens, pos, slots, mode=mode, logits=logits, stream=s)
+            lg_host.copy_(logits, non_blocking=True)
+        s.synchronize()
+    e2e_s = time.perf_counter() - te
+    status = qb.device_status()
+    step_s = elapsed_ms / 1e3 / args.steps
+    bytes_step, weight_bytes = decode_bytes_per_step(model, m, ctx)
+    peak, peak_src = measured_peaks()
+    achieved = bytes_step / step_s / 1e9
+    line = {
+        "metric": DECODE_METRIC, "value": m * args.steps / (elapsed_ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "model_shapes": model, "architecture": DECODE_MODELS[model]["arch"],
+                   "M": m, "context": ctx, "layers": tok["layers"], "quant": "Q4_0" if dt == Q4 else "Q8_0",
+                   "mode": args.mode, "weight_bytes_per_step": weight_bytes,
+                   "l2_policy": f"inputs larger than L2: {weight_bytes / 1e9:.1f} GB of distinct weights per step",
+                   "weights": "N(0,0.02) std::mt19937(42) per projection shape, quantized on GPU (byte-exact Q*_0), "
+                              "one copy per layer in the file; embedding = the LM head's draw in F32",
+                   "step": "one token per slot at position ctx over ctx filled cache positions: embedding, per "
+                           "layer RMSNorm+QKV+bias, attention with RoPE and the KV store, O + residual, "
+                           "RMSNorm+SwiGLU, down + residual; final RMSNorm + LM head; one CUDA graph replay"},
+        "e2e": {"value": m * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": m * 4,
+                "d2h_bytes_per_step": m * vocab * 4, "steps": e2e_steps,
+                "path": "H2D of the step's tokens from pinned memory, Decoder.step (qraf_cuda_decoder_step, no "
+                        "graph), D2H of the logits, stream sync, every step"},
+        "gpu_launches": args.steps * per_step,
+        "launches_per_step": per_step,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_src,
+                     "what": "weights + norms/biases + embedding rows + each slot's K/V over ctx+1 positions, "
+                             "per step / time per step", "bytes_per_step": bytes_step},
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    del g
+    return line
+
+
+def decode_cpu_baseline(model, ctx, budget_s, path):
+    """The reference's own Transformer::forward (oracle/_ref) on the model file at
+    position ctx (its cache zeros below ctx: the cost is the same): forwards for
+    about budget_s seconds, at least one."""
+    import oracle
+
+    if not oracle.reference_available():
+        return None
+    ref = oracle.RefTransformer(oracle.Reference(), path, TOKEN_MODELS[model]["vocab"])
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ref.forward(1 + n, ctx)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt_s = time.perf_counter() - t0
+    ref.close()
+    return {"value": n / dt_s, "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"{n} forward(token, {ctx}) calls of the reference's Transformer (oracle/_ref, "
+                      f"single-threaded, as it runs on Linux) over the same .qraf file, {dt_s:.1f} s"}
+
+
+def run_decode_reference(args, model, m, ctx):
+    """The reference arm: its Transformer over the same file (written with the
+    reference's own quantizer and RNG), one request at a time as its scheduler
+    runs them; M slots cost M forwards, so tokens/s does not depend on M."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import oracle
+
+    if not oracle.reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference library) is not built"}))
+        return
+    qz = oracle.Reference()
+
+    def fill(seed, std, n):
+        return host_normal(seed, std, n)
+
+    def quantize(dtype, w2d):
+        return qz.quantize(dtype, np.ascontiguousarray(w2d).reshape(-1), 32)
+
+    budget = max(5.0, min(120.0, 10.0 * args.steps))
+    path = decode_file_path(model)
+    try:
+        write_decode_file(model, path, fill, quantize, max_seq=ctx + 1)
+        cpu = decode_cpu_baseline(model, ctx, budget, path)
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    line = {"impl": "reference", "metric": DECODE_METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cpu["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "model_shapes": model, "M": m, "context": ctx},
+            "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1120,6 +1424,10 @@ def main():
                     help="token workloads on N > 1 GPUs: all-gather fused into the kernel, or NCCL after it")
     args = ap.parse_args()
     args.workload = resolve_workload(args.workload, int(os.environ.get("WORLD_SIZE", "1")))
+    dec = parse_decode_workload(args.workload)
+    if dec:
+        (run_decode_reference if args.impl == "reference" else run_decode)(args, *dec)
+        return
     tok = parse_token_workload(args.workload)
     if tok:
         (run_token_reference if args.impl == "reference" else run_token)(args, *tok)

@@ -30,8 +30,8 @@ constexpr uint32_t kAttnWarps = kAttnThreads / 32u;
 constexpr uint32_t kAttnMinChunk = 32;        // positions per CTA, at least (fewer CTAs for short sequences)
 constexpr uint32_t kAttnMaxGroup = 16;        // query heads per KV head, at most
 constexpr uint32_t kAttnMaxHeadDim = 256;
-constexpr uint32_t kAttnMaxSplits = 256;      // CTAs per (slot, KV head), at most
-constexpr uint64_t kAttnScoreBytes = 64 << 10;   // shared score buffer the split count aims under
+constexpr uint32_t kAttnMaxSplits = 16;       // CTAs per (slot, KV head), at most (the merge reads them all)
+constexpr uint32_t kAttnTile = 32;            // positions per shared-memory tile (one per lane)
 
 // x[m] = emb[tokens[m]]; a token outside the vocabulary gives zeros and raises
 // kErrBadLaunch.
@@ -80,21 +80,37 @@ struct AttnParams {
     float* part;               // [M][kv_heads][S][G][hd + 2]: unnormalised output, max, sum
     uint32_t* counter;         // [M][kv_heads]: CTAs of the group finished (the last resets it)
     uint32_t heads, kv_heads, hd, G, layer, layers, max_seq, max_slots;
-    uint32_t chunk_cap;        // floats per head row of the shared score buffer (>= positions per CTA, >= 2 S)
     float scale;               // 1 / sqrt(head_dim)
 };
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Floats of dynamic shared memory: q rotated [G][hd], the new k and v [hd] each,
+// two stages of K and V tiles [kAttnTile][hd + 4] each, probabilities [G][kAttnTile].
+__host__ __device__ constexpr size_t attn_smem_floats(uint32_t G, uint32_t hd) {
+    return static_cast<size_t>(G) * hd + 2u * hd + 4u * kAttnTile * (hd + 4u) + static_cast<size_t>(G) * kAttnTile;
+}
 
 // Attention of one step, fused with RoPE and the KV-cache store
 // (attention_forward, src/nn/attention.cpp:104-150).  CTA (s, kvh, m) takes slot
 // m's KV head kvh and the G = heads / kv_heads query heads that share it (the
-// reference's kv_h = h / kv_rep), over chunk s of positions 0 .. pos, so each K
-// and V row is read once for G heads.  The chunking follows the slot's position
+// reference's kv_h = h / kv_rep), over chunk s of positions 0 .. pos: each K and
+// V row is read once for the G heads.  The chunking follows the slot's position
 // on the device: chunk = ceil(seq / min(S, ceil(seq / 32))), S_eff =
 // ceil(seq / chunk) <= S working CTAs, each with at least one position.  The CTA
 // of the last chunk rotates the new k and stores k, v at pos in the slot's cache
-// (KVCache::store, attention.cpp:39-44) and reads them from shared memory.  Per
-// chunk: scores q.k_t * scale, then max, e_t = exp(score - max), their sum and
-// sum_t e_t v_t (the reference's softmax and weighted sum, src/nn/ops.cpp:242-259,
+// (KVCache::store, attention.cpp:39-44), and takes them from shared memory.
+// A chunk goes in tiles of 32 positions, each tile's K and V rows copied to
+// shared memory (cp.async, the next tile's copies in flight while this one is
+// used): scores q.k_t * scale with one lane per position, the softmax running
+// over the tiles (max, exp(score - max), their sum, the output rescaled when the
+// max grows: the reference's softmax and weighted sum, src/nn/ops.cpp:242-259,
 // attention.cpp:128-147, with 1 / sum applied once at the end).  One chunk
 // writes the result; with several, each leaves a partial and the last CTA of the
 // group to finish (an atomic count, no waiting) merges them:
@@ -102,8 +118,9 @@ struct AttnParams {
 // Slots of one step must be distinct.  Launched with programmatic dependent
 // launch: all reads after griddepcontrol.wait.
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnParams a) {
-    extern __shared__ float att_smem[];
-    __shared__ float s_max[kAttnMaxGroup], s_sum[kAttnMaxGroup];
+    extern __shared__ __align__(16) float att_smem[];
+    __shared__ float s_alpha[kAttnMaxGroup], s_sum[kAttnMaxGroup], s_pm[kAttnMaxSplits * kAttnMaxGroup],
+        s_pl[kAttnMaxSplits * kAttnMaxGroup];
     __shared__ uint32_t s_last;
     pdl_wait();
     pdl_launch_dependents();
@@ -119,14 +136,37 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     const uint32_t chunk = (seq + s0 - 1u) / s0;
     const uint32_t s_eff = (seq + chunk - 1u) / chunk;
     if (s >= s_eff) return;
-    const uint32_t t0 = s * chunk, t1 = min(seq, t0 + chunk), n_t = t1 - t0;
-    const uint32_t G = a.G, hd = a.hd, half = hd / 2u, kv_dim = a.kv_heads * hd;
-    float* qs = att_smem;                       // [G][hd], rotated
-    float* knew = qs + G * hd;                  // [hd]: k at pos, rotated (last chunk)
-    float* vnew = knew + hd;                    // [hd]
-    float* sc = vnew + hd;                      // [G][chunk_cap]
+    const uint32_t t0 = s * chunk, t1 = min(seq, t0 + chunk);
+    const uint32_t G = a.G, hd = a.hd, half = hd / 2u, kv_dim = a.kv_heads * hd, ld = hd + 4u, q4 = hd / 4u;
+    float* qs = att_smem;                                  // [G][hd], rotated
+    float* knew = qs + G * hd;                             // [hd]
+    float* vnew = knew + hd;                               // [hd]
+    float* kv_st = vnew + hd;                              // stage b: K at kv_st + 2 b T ld, V after it
+    float* pr = kv_st + 4u * kAttnTile * ld;               // [G][kAttnTile]
     const bool owner = (s == s_eff - 1u);
     const float2* cs = a.rope + static_cast<size_t>(p) * half;
+    const size_t base =
+        (static_cast<size_t>(sl) * a.layers + a.layer) * a.max_seq * kv_dim + static_cast<size_t>(kvh) * hd;
+    const float* kbase = a.kc + base;
+    const float* vbase = a.vc + base;
+
+    // tile copies: rows [tt, tt + nt) of K and V into stage b, row pos excluded
+    // (it is this step's, taken from knew / vnew)
+    auto issue = [&](uint32_t tt, uint32_t b) {
+        const uint32_t nt = min(kAttnTile, t1 - tt);
+        float* ks = kv_st + 2u * b * kAttnTile * ld;
+        float* vs = ks + kAttnTile * ld;
+        for (uint32_t j = tid; j < 2u * nt * q4; j += kAttnThreads) {
+            const uint32_t which = j / (nt * q4), r = (j - which * nt * q4) / q4, c = j % q4;
+            const uint32_t t = tt + r;
+            if (t == static_cast<uint32_t>(p)) continue;
+            const float* src = (which ? vbase : kbase) + static_cast<size_t>(t) * kv_dim + 4u * c;
+            cp_async16((which ? vs : ks) + r * ld + 4u * c, src);
+        }
+        cp_async_commit();
+    };
+    issue(t0, 0);
+
     const float* qm = a.q + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
     for (uint32_t j = tid; j < G * half; j += kAttnThreads) {
         const uint32_t g = j / half, i = j - g * half;
@@ -134,8 +174,6 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         qs[g * hd + 2u * i] = r.x;
         qs[g * hd + 2u * i + 1u] = r.y;
     }
-    const size_t base =
-        (static_cast<size_t>(sl) * a.layers + a.layer) * a.max_seq * kv_dim + static_cast<size_t>(kvh) * hd;
     if (owner) {
         const float* km = a.k + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
         const float* vm = a.v + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
@@ -154,77 +192,97 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
             vdst[d] = x;
         }
     }
-    __syncthreads();
 
-    // scores: one warp per position, lanes over the head dimension, the G dot
-    // products reduced together (independent shuffle chains)
-    for (uint32_t t = t0 + warp; t < t1; t += kAttnWarps) {
-        const float* kt = (t == static_cast<uint32_t>(p)) ? knew : a.kc + base + static_cast<size_t>(t) * kv_dim;
-        float kd[kAttnMaxHeadDim / 32];
-#pragma unroll
-        for (uint32_t j = 0; j < kAttnMaxHeadDim / 32; ++j) kd[j] = (lane + 32u * j < hd) ? kt[lane + 32u * j] : 0.0f;
-        float acc[kAttnMaxGroup];
-#pragma unroll
-        for (uint32_t g = 0; g < kAttnMaxGroup; ++g) {
-            acc[g] = 0.0f;
-            if (g < G) {
-#pragma unroll
-                for (uint32_t j = 0; j < kAttnMaxHeadDim / 32; ++j)
-                    if (lane + 32u * j < hd) acc[g] = __fadd_rn(acc[g], __fmul_rn(qs[g * hd + lane + 32u * j], kd[j]));
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (uint32_t g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) acc[g] = __fadd_rn(acc[g], __shfl_xor_sync(0xFFFFFFFFu, acc[g], o));
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (uint32_t g = 0; g < kAttnMaxGroup; ++g)
-                if (g < G) sc[g * a.chunk_cap + (t - t0)] = __fmul_rn(acc[g], a.scale);
-        }
-    }
-    __syncthreads();
-
-    // the chunk's softmax terms: one warp per head
-    for (uint32_t g = warp; g < G; g += kAttnWarps) {
-        float* row = sc + g * a.chunk_cap;
-        float mx = -INFINITY;
-        for (uint32_t t = lane; t < n_t; t += 32u) mx = fmaxf(mx, row[t]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-        float sum = 0.0f;
-        for (uint32_t t = lane; t < n_t; t += 32u) {
-            const float e = expf(__fsub_rn(row[t], mx));
-            row[t] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        sum = warp_sum(sum);
-        if (lane == 0) {
-            s_max[g] = mx;
-            s_sum[g] = sum;
-        }
-    }
-    __syncthreads();
-
-    // sum_t e_t v_t: thread (set, d) for the heads set, set + nsets, ...
+    // running softmax state: per head the max (held by the warp that scores it)
+    // and the sum; per (head, d) the output (thread (set, d), heads set + i nsets)
     const uint32_t nsets = kAttnThreads / hd;
     const uint32_t d = tid % hd, set = tid / hd;
     const bool active = set < nsets;
     float acc[kAttnMaxGroup];
 #pragma unroll
     for (uint32_t i = 0; i < kAttnMaxGroup; ++i) acc[i] = 0.0f;
-    if (active) {
-        for (uint32_t t = t0; t < t1; ++t) {
-            const float vd = (t == static_cast<uint32_t>(p)) ? vnew[d] : a.vc[base + static_cast<size_t>(t) * kv_dim + d];
+    float run_max[kAttnMaxGroup / kAttnWarps], run_sum[kAttnMaxGroup / kAttnWarps];
+#pragma unroll
+    for (uint32_t i = 0; i < kAttnMaxGroup / kAttnWarps; ++i) {
+        run_max[i] = -INFINITY;
+        run_sum[i] = 0.0f;
+    }
+
+    __syncthreads();   // qs, knew and vnew are read across threads below
+    const uint32_t ntiles = (t1 - t0 + kAttnTile - 1u) / kAttnTile;
+    for (uint32_t it = 0; it < ntiles; ++it) {
+        const uint32_t tt = t0 + it * kAttnTile, nt = min(kAttnTile, t1 - tt), b = it & 1u;
+        if (it + 1u < ntiles) {
+            issue(tt + kAttnTile, b ^ 1u);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        float* ks = kv_st + 2u * b * kAttnTile * ld;
+        float* vs = ks + kAttnTile * ld;
+        if (static_cast<uint32_t>(p) >= tt && static_cast<uint32_t>(p) < tt + nt) {
+            const uint32_t r = static_cast<uint32_t>(p) - tt;
+            for (uint32_t j = tid; j < hd; j += kAttnThreads) {
+                ks[r * ld + j] = knew[j];
+                vs[r * ld + j] = vnew[j];
+            }
+        }
+        __syncthreads();
+        // scores and the running softmax: warp w takes heads w, w + 8; lane = position
+#pragma unroll
+        for (uint32_t i = 0; i < kAttnMaxGroup / kAttnWarps; ++i) {
+            const uint32_t g = warp + i * kAttnWarps;
+            if (g < G) {
+                float sc = -INFINITY;
+                if (lane < nt) {
+                    const float4* kr = reinterpret_cast<const float4*>(ks + lane * ld);
+                    const float4* qr = reinterpret_cast<const float4*>(qs + g * hd);
+                    float dot = 0.0f;
+                    for (uint32_t c = 0; c < q4; ++c) {
+                        const float4 kk = kr[c], qq = qr[c];
+                        dot = fmaf(qq.x, kk.x, dot);
+                        dot = fmaf(qq.y, kk.y, dot);
+                        dot = fmaf(qq.z, kk.z, dot);
+                        dot = fmaf(qq.w, kk.w, dot);
+                    }
+                    sc = __fmul_rn(dot, a.scale);
+                }
+                float mt = sc;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
+                const float mnew = fmaxf(run_max[i], mt);
+                const float e = (lane < nt) ? expf(__fsub_rn(sc, mnew)) : 0.0f;
+                pr[g * kAttnTile + lane] = e;
+                const float alpha = expf(__fsub_rn(run_max[i], mnew));   // 0 on the first tile
+                run_sum[i] = __fadd_rn(__fmul_rn(run_sum[i], alpha), warp_sum(e));
+                run_max[i] = mnew;
+                if (lane == 0) s_alpha[g] = alpha;
+            }
+        }
+        __syncthreads();
+        if (active) {
 #pragma unroll
             for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
                 const uint32_t g = set + i * nsets;
-                if (g < G) acc[i] = __fadd_rn(acc[i], __fmul_rn(sc[g * a.chunk_cap + (t - t0)], vd));
+                if (g < G) {
+                    float o = __fmul_rn(acc[i], s_alpha[g]);
+                    for (uint32_t t = 0; t < nt; ++t) o = fmaf(pr[g * kAttnTile + t], vs[t * ld + d], o);
+                    acc[i] = o;
+                }
             }
         }
+        __syncthreads();   // the stage and the probabilities are reused by the next tile
     }
+#pragma unroll
+    for (uint32_t i = 0; i < kAttnMaxGroup / kAttnWarps; ++i) {
+        const uint32_t g = warp + i * kAttnWarps;
+        if (g < G && lane == 0) {
+            s_sum[g] = run_sum[i];
+            s_alpha[g] = run_max[i];
+        }
+    }
+    __syncthreads();
+
     float* om = a.out + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
     if (s_eff == 1u) {
         if (active) {
@@ -246,7 +304,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
                 float* r = pg + (static_cast<size_t>(s) * G + g) * rec;
                 r[d] = acc[i];
                 if (d == 0) {
-                    r[hd] = s_max[g];
+                    r[hd] = s_alpha[g];     // the chunk's max
                     r[hd + 1u] = s_sum[g];
                 }
             }
@@ -262,27 +320,24 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // merge: the chunks' (max, sum) into shared memory in one round of loads
-    // (sc is free now and holds 2 * S * G floats), per head the overall max and
-    // the chunk weights exp(max_c - max), then each output's weighted sum
-    float* pm = sc;                      // [s_eff][G]: max_c, then the weight of chunk c
-    float* pl = sc + s_eff * G;          // [s_eff][G]: sum_c
+    // merge: the chunks' (max, sum) into shared memory, per head the overall max
+    // and the chunk weights exp(max_c - max), then each output's weighted sum
+    // (at most kAttnMaxSplits independent loads per output)
     for (uint32_t j = tid; j < s_eff * G; j += kAttnThreads) {
         const float* r = pg + static_cast<size_t>(j) * rec;
-        pm[j] = __ldcg(r + hd);
-        pl[j] = __ldcg(r + hd + 1u);
+        s_pm[j] = __ldcg(r + hd);
+        s_pl[j] = __ldcg(r + hd + 1u);
     }
     __syncthreads();
     for (uint32_t g = warp; g < G; g += kAttnWarps) {
-        float mx = -INFINITY;
-        for (uint32_t c = lane; c < s_eff; c += 32u) mx = fmaxf(mx, pm[c * G + g]);
+        float mx = (lane < s_eff) ? s_pm[lane * G + g] : -INFINITY;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
         float l = 0.0f;
-        for (uint32_t c = lane; c < s_eff; c += 32u) {
-            const float w = expf(__fsub_rn(pm[c * G + g], mx));
-            pm[c * G + g] = w;
-            l = __fadd_rn(l, __fmul_rn(w, pl[c * G + g]));
+        if (lane < s_eff) {
+            const float w = expf(__fsub_rn(s_pm[lane * G + g], mx));
+            l = __fmul_rn(w, s_pl[lane * G + g]);
+            s_pm[lane * G + g] = w;
         }
         l = warp_sum(l);
         if (lane == 0) s_sum[g] = l;
@@ -290,10 +345,14 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     __syncthreads();
     for (uint32_t j = tid; j < G * hd; j += kAttnThreads) {
         const uint32_t g = j / hd, dd = j - g * hd;
+        float v[kAttnMaxSplits];
+#pragma unroll
+        for (uint32_t c = 0; c < kAttnMaxSplits; ++c)
+            v[c] = (c < s_eff) ? __ldcg(pg + (static_cast<size_t>(c) * G + g) * rec + dd) : 0.0f;
         float o = 0.0f;
-#pragma unroll 4
-        for (uint32_t c = 0; c < s_eff; ++c)
-            o = __fadd_rn(o, __fmul_rn(pm[c * G + g], __ldcg(pg + (static_cast<size_t>(c) * G + g) * rec + dd)));
+#pragma unroll
+        for (uint32_t c = 0; c < kAttnMaxSplits; ++c)
+            if (c < s_eff) o = fmaf(s_pm[c * G + g], v[c], o);
         om[g * hd + dd] = __fmul_rn(o, __fdiv_rn(1.0f, s_sum[g]));
     }
 }
@@ -347,25 +406,12 @@ struct qraf_decoder {
 namespace {
 
 // CTAs per (slot, KV head) of a step of M slots: about two per SM over the
-// step, at most one per 32 positions of max_seq, and enough that a chunk's
-// scores fit the shared buffer.
+// step, at most one per 32 positions of max_seq and at most kAttnMaxSplits.
 uint32_t attn_splits(const qraf_decoder* d, uint32_t M, int sm_count) {
     const uint32_t by_len = std::max<uint32_t>(1u, (d->max_seq + kAttnMinChunk - 1u) / kAttnMinChunk);
     const uint32_t groups = M * d->kv_heads;
     const uint32_t target = std::max<uint32_t>(1u, (2u * static_cast<uint32_t>(sm_count) + groups - 1u) / groups);
-    uint32_t S = std::min(by_len, target);
-    const uint64_t need = (static_cast<uint64_t>(d->G) * d->max_seq * 4u + kAttnScoreBytes - 1u) / kAttnScoreBytes;
-    S = std::max<uint32_t>(S, static_cast<uint32_t>(std::min<uint64_t>(need, by_len)));
-    return std::max<uint32_t>(1u, std::min(S, kAttnMaxSplits));
-}
-
-uint32_t attn_chunk_cap(const qraf_decoder* d, uint32_t S) {
-    return std::max({kAttnMinChunk, (d->max_seq + S - 1u) / S, 2u * S});
-}
-
-size_t attn_smem_bytes(const qraf_decoder* d, uint32_t S) {
-    return (static_cast<size_t>(d->G) * d->hd + 2u * d->hd + static_cast<size_t>(d->G) * attn_chunk_cap(d, S)) *
-           sizeof(float);
+    return std::max<uint32_t>(1u, std::min({by_len, target, kAttnMaxSplits}));
 }
 
 }  // namespace
@@ -431,8 +477,8 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
                           "config lacks vocab / hidden / layers / heads / intermediate sizes or has inconsistent heads");
     d->hd = d->hidden / d->heads;
     d->G = d->heads / d->kv_heads;
-    if (d->hd % 2u || d->hd > kAttnMaxHeadDim)
-        return fail_close(QRAF_ERR_UNSUPPORTED, "head_dim must be even and at most 256");
+    if (d->hd % 8u || d->hd > kAttnMaxHeadDim)
+        return fail_close(QRAF_ERR_UNSUPPORTED, "head_dim must be a multiple of 8, at most 256");
     if (d->G > kAttnMaxGroup) return fail_close(QRAF_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
     if (d->hidden % 8u) return fail_close(QRAF_ERR_UNSUPPORTED, "hidden_size must be a multiple of 8");
     d->max_slots = max_slots;
@@ -506,18 +552,18 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
         t_last_error = msg;
         return rc;
     }
-    // attention: the largest partial buffer and shared-memory need over steps of 1 .. max_slots slots
+    // attention: the largest partial buffer over steps of 1 .. max_slots slots
     uint64_t part_floats = 0;
-    size_t smem_max = 0;
     for (uint32_t M = 1; M <= max_slots; ++M) {
         const uint32_t S = attn_splits(d.get(), M, dev->sm_count);
         part_floats = std::max<uint64_t>(part_floats, static_cast<uint64_t>(M) * d->heads * S * (d->hd + 2u));
-        smem_max = std::max(smem_max, attn_smem_bytes(d.get(), S));
     }
+    const size_t smem_max = attn_smem_floats(d->G, d->hd) * sizeof(float);
     if (smem_max + kSmemReserve > static_cast<size_t>(dev->smem_optin)) {
         cudaSetDevice(cur);
-        return fail_close(QRAF_ERR_UNSUPPORTED, "max_seq " + std::to_string(max_seq) + " needs " +
-                                                    std::to_string(smem_max) + " bytes of shared memory per CTA");
+        return fail_close(QRAF_ERR_UNSUPPORTED, "head_dim " + std::to_string(d->hd) + " with " + std::to_string(d->G) +
+                                                    " query heads per KV head needs " + std::to_string(smem_max) +
+                                                    " bytes of shared memory per CTA");
     }
     const uint64_t cache = static_cast<uint64_t>(max_slots) * d->layers * max_seq * kv_dim;
     const size_t ws = static_cast<size_t>(max_slots) * (2u * d->hidden + 2u * q_dim + 2u * kv_dim + d->inter);
@@ -613,12 +659,11 @@ int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_d
     ap.layers = d->layers;
     ap.max_seq = d->max_seq;
     ap.max_slots = d->max_slots;
-    ap.chunk_cap = attn_chunk_cap(d, S);
     ap.scale = 1.0f / std::sqrt(static_cast<float>(d->hd));   // attention.cpp:118, IEEE on the host as there
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, d->kv_heads, M);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(d, S);
+    cfg.dynamicSmemBytes = attn_smem_floats(d->G, d->hd) * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

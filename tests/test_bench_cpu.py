@@ -69,3 +69,38 @@ def test_reference_arm_prints_the_contract_line():
     assert d["config"] == {"workload": "q8_256x512", "N": 256, "K": 512, "M": 1, "block": 32, "quant": "Q8_0",
                            "mode": "fast"}
     assert "PRODUCT_SO_MAPPED False" in out.stdout
+
+
+def test_decode_workload_names_and_bytes():
+    assert bench.parse_decode_workload("qwen3b_decode") == ("qwen3b", 1, 512)
+    assert bench.parse_decode_workload("qwen3b_decode_m8_c1024") == ("qwen3b", 8, 1024)
+    assert bench.parse_decode_workload("qwen3b_token") is None
+    total, weights = bench.decode_bytes_per_step("qwen3b", 1, 512)
+    # 36 layers of Q8_0 projections (q, k, v, o, gate, up, down) + the 151936 x 2048 head
+    assert weights == 36 * (2048 * 2048 * 2 + 256 * 2048 * 2 + 11008 * 2048 * 3) * 36 // 32 + 151936 * 64 * 36
+    kv = 36 * 513 * 256 * 4 * 2 + 36 * 256 * 4 * 2
+    small = 4 * (73 * 2048 + 36 * (2048 + 512))
+    assert total == weights + kv + small + 2048 * 4
+
+
+def test_decode_file_runs_in_the_reference_transformer(tmp_path, monkeypatch):
+    """The bench's model file (a smaller model of the same layout) loads in the
+    reference's Transformer and decodes: the CPU baseline's path."""
+    import numpy as np
+
+    import oracle
+
+    if not oracle.reference_available():
+        import pytest
+
+        pytest.skip("oracle/_ref not built")
+    monkeypatch.setitem(bench.TOKEN_MODELS, "tiny", {"dtype": bench.Q4, "layers": 2, "hidden": 256, "vocab": 300,
+                                                     "projs": []})
+    monkeypatch.setitem(bench.DECODE_MODELS, "tiny", {"arch": "qwen2", "heads": 4, "kv_heads": 2, "inter": 512})
+    ref = oracle.Reference()
+    path = str(tmp_path / "tiny.qraf")
+    n = bench.write_decode_file("tiny", path, lambda seed, std, k: bench.host_normal(seed, std, k),
+                                lambda dt, w: ref.quantize(dt, np.ascontiguousarray(w).reshape(-1), 32), max_seq=9)
+    assert n == os.path.getsize(path)
+    cpu = bench.decode_cpu_baseline("tiny", 8, 0.05, path)
+    assert cpu["kind"] == "reference" and cpu["value"] > 0

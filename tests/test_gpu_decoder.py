@@ -73,14 +73,15 @@ def test_one_slot_matches_the_reference_forward(tmp_path, cuda, oracle_lib, arch
     assert qb.device_status() == qb.OK
 
 
-@pytest.mark.parametrize("max_seq", [160, 4096])
-def test_long_sequence_splits_attention(tmp_path, cuda, oracle_lib, max_seq):
-    """150 positions: from position 32 on, a slot's attention runs over several
-    chunks (the CTA count follows max_seq, up to one per 32 positions) whose
-    partials the last CTA merges; GQA with 4 query heads per KV head."""
+@pytest.mark.parametrize("max_seq,n", [(160, 150), (1024, 600)])
+def test_long_sequence_splits_attention(tmp_path, cuda, oracle_lib, max_seq, n):
+    """From position 32 on, a slot's attention runs over several chunks (one CTA
+    per 32 positions of max_seq, at most 16) whose partials the last CTA merges;
+    past 512 positions a chunk spans several 32-position tiles.  GQA with 4
+    query heads per KV head."""
     path, vocab = _model(tmp_path, oracle_lib, "qwen2", qb.Q8_0, heads=8, kv_heads=2, max_seq=max_seq)
     rng = np.random.default_rng(3)
-    tokens = [int(t) for t in rng.integers(0, vocab, 150)]
+    tokens = [int(t) for t in rng.integers(0, vocab, n)]
     want = _reference_runs(path, vocab, [tokens])[0]
     dec = qb.Decoder(path, max_slots=1, max_seq=max_seq)
     for p, t in enumerate(tokens):
