@@ -1409,7 +1409,9 @@ def main():
                          "over the ranks) under torch.distributed.run")
     ap.add_argument("--no-1gpu-ref", dest="no_1gpu_ref", action="store_true",
                     help="sharded workloads on N > 1 GPUs: skip the unsharded one-GPU figure of the same projection")
-    ap.add_argument("--mode", choices=["fast", "exact", "tc", "auto"], default="fast")
+    ap.add_argument("--mode", choices=["fast", "exact", "tc", "auto"], default=None,
+                    help="projection arithmetic (default: fast; auto for decode workloads, which takes the "
+                         "tensor-core tile from three slots)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="launch matvecs strictly one after another (no programmatic dependent launch)")
@@ -1425,6 +1427,8 @@ def main():
     args = ap.parse_args()
     args.workload = resolve_workload(args.workload, int(os.environ.get("WORLD_SIZE", "1")))
     dec = parse_decode_workload(args.workload)
+    if args.mode is None:
+        args.mode = "auto" if dec else "fast"
     if dec:
         (run_decode_reference if args.impl == "reference" else run_decode)(args, *dec)
         return

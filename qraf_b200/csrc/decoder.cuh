@@ -30,7 +30,7 @@ constexpr uint32_t kAttnWarps = kAttnThreads / 32u;
 constexpr uint32_t kAttnMinChunk = 32;        // positions per CTA, at least (fewer CTAs for short sequences)
 constexpr uint32_t kAttnMaxGroup = 16;        // query heads per KV head, at most
 constexpr uint32_t kAttnMaxHeadDim = 256;
-constexpr uint32_t kAttnMaxSplits = 16;       // CTAs per (slot, KV head), at most (the merge reads them all)
+constexpr uint32_t kAttnMaxSplits = 32;       // CTAs per (slot, KV head), at most (the merge reads them all)
 constexpr uint32_t kAttnTile = 32;            // positions per shared-memory tile (one per lane)
 
 // x[m] = emb[tokens[m]]; a token outside the vocabulary gives zeros and raises
@@ -117,6 +117,7 @@ __host__ __device__ constexpr size_t attn_smem_floats(uint32_t G, uint32_t hd) {
 // out = sum_c exp(max_c - max) o_c / sum_c exp(max_c - max) l_c.
 // Slots of one step must be distinct.  Launched with programmatic dependent
 // launch: all reads after griddepcontrol.wait.
+template <uint32_t HPT>   // query heads per P.V thread, at least ceil(G / (threads / hd))
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnParams a) {
     extern __shared__ __align__(16) float att_smem[];
     __shared__ float s_alpha[kAttnMaxGroup], s_sum[kAttnMaxGroup], s_pm[kAttnMaxSplits * kAttnMaxGroup],
@@ -151,17 +152,21 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     const float* vbase = a.vc + base;
 
     // tile copies: rows [tt, tt + nt) of K and V into stage b, row pos excluded
-    // (it is this step's, taken from knew / vnew)
+    // (it is this step's, taken from knew / vnew).  Thread: 16-byte column c0 of
+    // rows r0, r0 + rstep, ... (no division in the loop)
+    const uint32_t rstep = kAttnThreads / q4, c0 = tid % q4, r0 = tid / q4;
     auto issue = [&](uint32_t tt, uint32_t b) {
         const uint32_t nt = min(kAttnTile, t1 - tt);
         float* ks = kv_st + 2u * b * kAttnTile * ld;
         float* vs = ks + kAttnTile * ld;
-        for (uint32_t j = tid; j < 2u * nt * q4; j += kAttnThreads) {
-            const uint32_t which = j / (nt * q4), r = (j - which * nt * q4) / q4, c = j % q4;
-            const uint32_t t = tt + r;
-            if (t == static_cast<uint32_t>(p)) continue;
-            const float* src = (which ? vbase : kbase) + static_cast<size_t>(t) * kv_dim + 4u * c;
-            cp_async16((which ? vs : ks) + r * ld + 4u * c, src);
+        if (r0 < rstep) {
+            for (uint32_t r = r0; r < nt; r += rstep) {
+                const uint32_t t = tt + r;
+                if (t == static_cast<uint32_t>(p)) continue;
+                const size_t off = static_cast<size_t>(t) * kv_dim + 4u * c0;
+                cp_async16(ks + r * ld + 4u * c0, kbase + off);
+                cp_async16(vs + r * ld + 4u * c0, vbase + off);
+            }
         }
         cp_async_commit();
     };
@@ -198,9 +203,9 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     const uint32_t nsets = kAttnThreads / hd;
     const uint32_t d = tid % hd, set = tid / hd;
     const bool active = set < nsets;
-    float acc[kAttnMaxGroup];
+    float acc[HPT];
 #pragma unroll
-    for (uint32_t i = 0; i < kAttnMaxGroup; ++i) acc[i] = 0.0f;
+    for (uint32_t i = 0; i < HPT; ++i) acc[i] = 0.0f;
     float run_max[kAttnMaxGroup / kAttnWarps], run_sum[kAttnMaxGroup / kAttnWarps];
 #pragma unroll
     for (uint32_t i = 0; i < kAttnMaxGroup / kAttnWarps; ++i) {
@@ -237,15 +242,16 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
                 if (lane < nt) {
                     const float4* kr = reinterpret_cast<const float4*>(ks + lane * ld);
                     const float4* qr = reinterpret_cast<const float4*>(qs + g * hd);
-                    float dot = 0.0f;
+                    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;   // four chains
+#pragma unroll 4
                     for (uint32_t c = 0; c < q4; ++c) {
                         const float4 kk = kr[c], qq = qr[c];
-                        dot = fmaf(qq.x, kk.x, dot);
-                        dot = fmaf(qq.y, kk.y, dot);
-                        dot = fmaf(qq.z, kk.z, dot);
-                        dot = fmaf(qq.w, kk.w, dot);
+                        d0 = fmaf(qq.x, kk.x, d0);
+                        d1 = fmaf(qq.y, kk.y, d1);
+                        d2 = fmaf(qq.z, kk.z, d2);
+                        d3 = fmaf(qq.w, kk.w, d3);
                     }
-                    sc = __fmul_rn(dot, a.scale);
+                    sc = __fmul_rn(__fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)), a.scale);
                 }
                 float mt = sc;
 #pragma unroll
@@ -261,13 +267,27 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         }
         __syncthreads();
         if (active) {
+            // heads interleaved (independent chains), probabilities four positions at a time
 #pragma unroll
-            for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+            for (uint32_t i = 0; i < HPT; ++i) {
                 const uint32_t g = set + i * nsets;
-                if (g < G) {
-                    float o = __fmul_rn(acc[i], s_alpha[g]);
-                    for (uint32_t t = 0; t < nt; ++t) o = fmaf(pr[g * kAttnTile + t], vs[t * ld + d], o);
-                    acc[i] = o;
+                if (g < G) acc[i] = __fmul_rn(acc[i], s_alpha[g]);
+            }
+            for (uint32_t t = 0; t < nt; t += 4u) {   // pr is zero past nt; vs rows past nt are finite-or-unused
+                const float v0 = vs[t * ld + d];
+                const float v1 = (t + 1u < nt) ? vs[(t + 1u) * ld + d] : 0.0f;
+                const float v2 = (t + 2u < nt) ? vs[(t + 2u) * ld + d] : 0.0f;
+                const float v3 = (t + 3u < nt) ? vs[(t + 3u) * ld + d] : 0.0f;
+#pragma unroll
+                for (uint32_t i = 0; i < HPT; ++i) {
+                    const uint32_t g = set + i * nsets;
+                    if (g < G) {
+                        const float4 e4 = *reinterpret_cast<const float4*>(pr + g * kAttnTile + t);
+                        float o = fmaf(e4.x, v0, acc[i]);
+                        o = fmaf(e4.y, v1, o);
+                        o = fmaf(e4.z, v2, o);
+                        acc[i] = fmaf(e4.w, v3, o);
+                    }
                 }
             }
         }
@@ -287,7 +307,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     if (s_eff == 1u) {
         if (active) {
 #pragma unroll
-            for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+            for (uint32_t i = 0; i < HPT; ++i) {
                 const uint32_t g = set + i * nsets;
                 if (g < G) om[g * hd + d] = __fmul_rn(acc[i], __fdiv_rn(1.0f, s_sum[g]));
             }
@@ -298,7 +318,7 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     float* pg = a.part + ((static_cast<size_t>(m) * a.kv_heads + kvh) * gridDim.x) * G * rec;
     if (active) {
 #pragma unroll
-        for (uint32_t i = 0; i < kAttnMaxGroup; ++i) {
+        for (uint32_t i = 0; i < HPT; ++i) {
             const uint32_t g = set + i * nsets;
             if (g < G) {
                 float* r = pg + (static_cast<size_t>(s) * G + g) * rec;
@@ -399,6 +419,7 @@ struct qraf_decoder {
     float2* rope = nullptr;       // [max_seq][hd / 2]
     float* part = nullptr;        // attention partials, sized for the largest step
     uint32_t* counter = nullptr;  // [max_slots][kv_heads]
+    void (*attn_kernel)(AttnParams) = nullptr;   // the instance for this model's heads per P.V thread
     float* work = nullptr;        // x, q, k, v, attention output, h, normalised x (tied head)
     float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr, *xn = nullptr;
 };
@@ -581,7 +602,11 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
         if (e == cudaSuccess) e = cudaMemset(d->vc, 0, cache * sizeof(float));
         if (e == cudaSuccess)
             e = cudaMemset(d->counter, 0, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t));
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(dec_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const uint32_t per = (d->G + kAttnThreads / d->hd - 1u) / (kAttnThreads / d->hd);
+        d->attn_kernel = per <= 1u ? dec_attention_kernel<1> : per <= 2u ? dec_attention_kernel<2>
+                         : per <= 4u ? dec_attention_kernel<4> : per <= 8u ? dec_attention_kernel<8>
+                                                                            : dec_attention_kernel<16>;
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(d->attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        static_cast<int>(smem_max));
         if (e == cudaSuccess) {
             (dec_rope_table_kernel<<<static_cast<unsigned>(std::min<size_t>((rope_n + 255) / 256, 4u * dev->sm_count)),
@@ -681,7 +706,7 @@ int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_d
         rc = multi_impl(ly.qkv, 3, d->x, ly.attn_norm, d->eps, any_bias ? biases : nullptr, qkv_out, M, pmode, st);
         if (rc) return rc;
         ap.layer = l;
-        QRAF_CUDA_TRY(counted(cudaLaunchKernelEx(&cfg, dec_attention_kernel, ap)));
+        QRAF_CUDA_TRY(counted(cudaLaunchKernelEx(&cfg, d->attn_kernel, ap)));
         rc = matvec_impl(&ly.o, d->att, d->x, M, pmode, st, true);
         if (rc) return rc;
         rc = swiglu_impl(&ly.gate, &ly.up, d->x, ly.ffn_norm, d->eps, d->h, M, pmode, st);
