@@ -1422,6 +1422,8 @@ def main():
                          "(default: one SwiGLU launch, down reading silu(gate) * up)")
     ap.add_argument("--no-multi", dest="multi", action="store_false",
                     help="token workloads: one launch per projection even where several share an input")
+    ap.add_argument("--decode-layers", dest="decode_layers", type=int, default=None,
+                    help="decode workloads: this many layers instead of the model's (a small case for profiling)")
     ap.add_argument("--allgather", choices=["fused", "nccl"], default="fused",
                     help="token workloads on N > 1 GPUs: all-gather fused into the kernel, or NCCL after it")
     args = ap.parse_args()
@@ -1429,6 +1431,8 @@ def main():
     dec = parse_decode_workload(args.workload)
     if args.mode is None:
         args.mode = "auto" if dec else "fast"
+    if dec and args.decode_layers:
+        TOKEN_MODELS[dec[0]] = dict(TOKEN_MODELS[dec[0]], layers=args.decode_layers)
     if dec:
         (run_decode_reference if args.impl == "reference" else run_decode)(args, *dec)
         return
