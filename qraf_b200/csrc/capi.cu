@@ -440,6 +440,7 @@ bool plan_tc(const qraf_weight_t& w, uint32_t M, const DeviceInfo& dev, TcPlan* 
     if (!tc_eligible(w) || M == 0 || M > kTcMaxVectors) return false;
     const bool q4 = w.dtype == QRAF_DTYPE_Q4_0;
     TcParams& p = out->p;
+    p = TcParams{};   // no output fusions unless the caller sets them
     out->mv = M <= 16 ? 16u : (M <= 32 ? 32u : 64u);
     p.w = static_cast<const uint8_t*>(w.data);
     p.row_bytes = w.row_bytes;
@@ -569,9 +570,17 @@ bool weight_map(const qraf_weight_t& w, CUtensorMap* map) {
     return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, w.data, dims, w.row_bytes, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// Input fusions of a tensor-core call (TcInput): the prep kernel forms the
+// activations from x (silu(x) * up, or RMSNorm(x) with norm_w) on the way.
+struct TcInput {
+    const float* up = nullptr;       // [M][K]: the input is silu(x) * up
+    const float* norm_w = nullptr;   // [K]: the input is RMSNorm(x) * norm_w
+    float eps = 0.0f;
+};
+
 template <uint32_t DT, uint32_t MV>
 cudaError_t launch_tc_mv(const TcPlan& pl, const CUtensorMap& map, const float* x, uint32_t K, bool pdl_prep,
-                         cudaStream_t st) {
+                         cudaStream_t st, const TcInput* in = nullptr) {
     const TcParams& p = pl.p;
     const uint64_t threads = static_cast<uint64_t>(p.nblk) * MV * 32u;
     cudaLaunchConfig_t cfg = {};
@@ -583,8 +592,16 @@ cudaError_t launch_tc_mv(const TcPlan& pl, const CUtensorMap& map, const float* 
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cfg.numAttrs = pdl_prep ? 1 : 0;
-    cudaError_t e = counted(cudaLaunchKernelEx(&cfg, tc_prep_kernel<DT>, x, const_cast<uint8_t*>(p.act), p.tile_count, p.tiles,
+    cudaError_t e;
+    if (in && (in->up || in->norm_w)) {
+        cfg.gridDim = dim3(p.n_pad / 2u, (p.nblk + kTcPrepBlocks - 1u) / kTcPrepBlocks);   // (vector slot, blocks)
+        e = counted(cudaLaunchKernelEx(&cfg, tc_prep_fused_kernel<DT>, x, in->up, in->norm_w, in->eps,
+                                       const_cast<uint8_t*>(p.act), p.tile_count, p.tiles, K, p.M, p.nblk, p.n_pad,
+                                       pdl_prep ? 1u : 0u));
+    } else {
+        e = counted(cudaLaunchKernelEx(&cfg, tc_prep_kernel<DT>, x, const_cast<uint8_t*>(p.act), p.tile_count, p.tiles,
                                        K, p.M, p.nblk, p.n_pad, pdl_prep ? 1u : 0u));
+    }
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
     cfg.blockDim = dim3(kTcThreads);
@@ -595,16 +612,29 @@ cudaError_t launch_tc_mv(const TcPlan& pl, const CUtensorMap& map, const float* 
 
 template <uint32_t DT>
 cudaError_t launch_tc_dt(const TcPlan& pl, const CUtensorMap& map, const float* x, uint32_t K, bool pdl_prep,
-                         cudaStream_t st) {
-    if (pl.mv == 16) return launch_tc_mv<DT, 16>(pl, map, x, K, pdl_prep, st);
-    if (pl.mv == 32) return launch_tc_mv<DT, 32>(pl, map, x, K, pdl_prep, st);
-    return launch_tc_mv<DT, 64>(pl, map, x, K, pdl_prep, st);
+                         cudaStream_t st, const TcInput* in = nullptr) {
+    if (pl.mv == 16) return launch_tc_mv<DT, 16>(pl, map, x, K, pdl_prep, st, in);
+    if (pl.mv == 32) return launch_tc_mv<DT, 32>(pl, map, x, K, pdl_prep, st, in);
+    return launch_tc_mv<DT, 64>(pl, map, x, K, pdl_prep, st, in);
 }
+
+// Fusions of a tensor-core call: the input's (TcInput) and the outputs' (the
+// TcParams fields of the same names): weights back to back in memory as
+// segments with their own outputs and biases, a bias for a single weight, the
+// residual add.
+struct TcFusion {
+    TcInput in;
+    uint32_t nseg = 0;
+    float* seg_y[kMaxSeg] = {};
+    const float* seg_b[kMaxSeg] = {};
+    uint32_t seg_row0[kMaxSeg + 1] = {};
+    bool accumulate = false;
+};
 
 // Y = W X on the tensor cores, in groups of up to 64 vectors, with scratch at
 // `scratch` (pl.bytes for the largest group; nullptr: the stream's own area).
 int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool overlap, cudaStream_t st,
-              const DeviceInfo& dev, uint8_t* scratch, size_t scratch_cap) {
+              const DeviceInfo& dev, uint8_t* scratch, size_t scratch_cap, const TcFusion* fz = nullptr) {
     TcPlan pl;
     const uint32_t first = std::min(M, kTcMaxVectors);
     if (!plan_tc(w, first, dev, &pl)) return fail(QRAF_ERR_UNSUPPORTED, "no tensor-core plan for this weight");
@@ -625,11 +655,27 @@ int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool
         one.p.act = base;
         one.p.partial = reinterpret_cast<float*>(base + one.off_part);
         one.p.tile_count = reinterpret_cast<uint32_t*>(base + one.off_cnt);
-        one.p.y = y + static_cast<size_t>(m0) * w.rows;
+        one.p.y = y ? y + static_cast<size_t>(m0) * w.rows : nullptr;
         const float* xm = x + static_cast<size_t>(m0) * w.cols;
+        TcInput in;
+        if (fz) {
+            TcParams& p = one.p;
+            p.nseg = fz->nseg;
+            p.accumulate = fz->accumulate ? 1u : 0u;
+            for (int i = 0; i < kMaxSeg; ++i) {
+                p.seg_b[i] = fz->seg_b[i];
+                p.seg_y[i] = (fz->nseg > 1 && fz->seg_y[i])
+                                 ? fz->seg_y[i] + static_cast<size_t>(m0) * (fz->seg_row0[i + 1] - fz->seg_row0[i])
+                                 : nullptr;
+            }
+            for (int i = 0; i <= kMaxSeg; ++i) p.seg_row0[i] = fz->seg_row0[i];
+            in = fz->in;
+            if (in.up) in.up += static_cast<size_t>(m0) * w.cols;
+        }
         const bool pdl_prep = overlap || m0 > 0;
-        const cudaError_t e = w.dtype == QRAF_DTYPE_Q8_0 ? launch_tc_dt<kDtypeQ8>(one, map, xm, w.cols, pdl_prep, st)
-                                                         : launch_tc_dt<kDtypeQ4>(one, map, xm, w.cols, pdl_prep, st);
+        const cudaError_t e = w.dtype == QRAF_DTYPE_Q8_0
+                                  ? launch_tc_dt<kDtypeQ8>(one, map, xm, w.cols, pdl_prep, st, fz ? &in : nullptr)
+                                  : launch_tc_dt<kDtypeQ4>(one, map, xm, w.cols, pdl_prep, st, fz ? &in : nullptr);
         if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "tensor-core launch: %s", cudaGetErrorString(e));
     }
     return QRAF_OK;

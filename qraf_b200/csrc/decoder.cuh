@@ -396,6 +396,7 @@ __global__ void __launch_bounds__(256) dec_f32_matvec_kernel(const float* __rest
 
 struct DecLayer {
     qraf_weight_t qkv[3], o, gate, up, down;
+    qraf_weight_t qkv_all{}, gate_up{};   // the same bytes as one weight each (tensor-core route)
     const float* attn_norm = nullptr;
     const float* ffn_norm = nullptr;
     const float* bias[3] = {nullptr, nullptr, nullptr};
@@ -420,8 +421,12 @@ struct qraf_decoder {
     float* part = nullptr;        // attention partials, sized for the largest step
     uint32_t* counter = nullptr;  // [max_slots][kv_heads]
     void (*attn_kernel)(AttnParams) = nullptr;   // the instance for this model's heads per P.V thread
-    float* work = nullptr;        // x, q, k, v, attention output, h, normalised x (tied head)
-    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr, *xn = nullptr;
+    float* work = nullptr;        // x, q, k, v, attention output, h, up, normalised x (tied head)
+    float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *h = nullptr, *u = nullptr,
+          *xn = nullptr;
+    // the tensor-core route (TC, or AUTO from three slots): every projection one
+    // launch pair with its fusions; needs Q/K/V and gate/up back to back in memory
+    bool tc_route = false;
 };
 
 namespace {
@@ -587,7 +592,7 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
                                                     " bytes of shared memory per CTA");
     }
     const uint64_t cache = static_cast<uint64_t>(max_slots) * d->layers * max_seq * kv_dim;
-    const size_t ws = static_cast<size_t>(max_slots) * (2u * d->hidden + 2u * q_dim + 2u * kv_dim + d->inter);
+    const size_t ws = static_cast<size_t>(max_slots) * (2u * d->hidden + 2u * q_dim + 2u * kv_dim + 2u * d->inter);
     const size_t rope_n = static_cast<size_t>(max_seq) * (d->hd / 2u);
     bool alloc_ok = cudaMalloc(&d->kc, cache * sizeof(float)) == cudaSuccess &&
                     cudaMalloc(&d->vc, cache * sizeof(float)) == cudaSuccess &&
@@ -630,7 +635,29 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
     d->v = w;   w += static_cast<size_t>(max_slots) * kv_dim;
     d->att = w; w += static_cast<size_t>(max_slots) * q_dim;
     d->h = w;   w += static_cast<size_t>(max_slots) * d->inter;
+    d->u = w;   w += static_cast<size_t>(max_slots) * d->inter;
     d->xn = w;
+    // the tensor-core route: every projection tile-eligible, Q/K/V and gate/up contiguous
+    auto joined = [](const qraf_weight_t* ws, uint32_t n, qraf_weight_t* out) {
+        qraf_weight_t v = ws[0];
+        for (uint32_t i = 1; i < n; ++i) {
+            const uint8_t* end = static_cast<const uint8_t*>(ws[i - 1].data) + ws[i - 1].rows * ws[i - 1].row_bytes;
+            if (ws[i].data != end || ws[i].dtype != v.dtype || ws[i].cols != v.cols || ws[i].block_size != v.block_size)
+                return false;
+            v.rows += ws[i].rows;
+        }
+        v.bytes = static_cast<uint64_t>(v.rows) * v.row_bytes;
+        *out = v;
+        return true;
+    };
+    bool tc = d->tied || tc_eligible(d->lm_head);
+    for (uint32_t l = 0; tc && l < d->layers; ++l) {
+        DecLayer& ly = d->L[l];
+        const qraf_weight_t gu[2] = {ly.gate, ly.up};
+        tc = joined(ly.qkv, 3, &ly.qkv_all) && joined(gu, 2, &ly.gate_up) && tc_eligible(ly.qkv_all) &&
+             tc_eligible(ly.o) && tc_eligible(ly.gate_up) && tc_eligible(ly.down);
+    }
+    d->tc_route = tc;
     *out = d.release();
     return QRAF_OK;
 }
@@ -645,6 +672,78 @@ int qraf_cuda_decoder_info(qraf_decoder_t d, uint32_t* vocab, uint32_t* hidden, 
     if (max_seq) *max_seq = d->max_seq;
     return QRAF_OK;
 }
+
+}  // extern "C"
+
+namespace {
+
+// The step on the tensor-core route: per layer four launch pairs (prep +
+// tile) and the attention launch.  QKV: RMSNorm formed by the prep kernel,
+// Q/K/V one weight with three outputs and their biases; O: the residual added
+// by the tile's store; gate/up: RMSNorm in the prep, one weight, outputs gate
+// and up; down: silu(gate) * up formed by the prep, the residual in the store;
+// the LM head: the final RMSNorm in the prep.  The arithmetic is that of the
+// separate passes (tests/test_gpu_decoder.py compares with the reference).
+int tc_step(qraf_decoder* d, uint32_t M, const DeviceInfo* dev, AttnParams ap, cudaLaunchConfig_t cfg,
+            float* logits_dev, cudaStream_t st) {
+    const uint32_t q_dim = d->heads * d->hd, kv_dim = d->kv_heads * d->hd;
+    int rc = QRAF_OK;
+    for (uint32_t l = 0; l < d->layers; ++l) {
+        const DecLayer& ly = d->L[l];
+        TcFusion qkv;
+        qkv.in.norm_w = ly.attn_norm;
+        qkv.in.eps = d->eps;
+        qkv.nseg = 3;
+        float* outs[3] = {d->q, d->k, d->v};
+        const uint32_t row0[kMaxSeg + 1] = {0u, q_dim, q_dim + kv_dim, q_dim + 2u * kv_dim, q_dim + 2u * kv_dim};
+        for (int i = 0; i < 3; ++i) {
+            qkv.seg_y[i] = outs[i];
+            qkv.seg_b[i] = ly.bias[i];
+        }
+        for (int i = 0; i <= kMaxSeg; ++i) qkv.seg_row0[i] = row0[i];
+        rc = matmul_tc(ly.qkv_all, d->x, nullptr, M, true, st, *dev, nullptr, 0, &qkv);
+        if (rc) return rc;
+        ap.layer = l;
+        QRAF_CUDA_TRY(counted(cudaLaunchKernelEx(&cfg, d->attn_kernel, ap)));
+        TcFusion res;
+        res.accumulate = true;
+        rc = matmul_tc(ly.o, d->att, d->x, M, true, st, *dev, nullptr, 0, &res);
+        if (rc) return rc;
+        TcFusion gu;
+        gu.in.norm_w = ly.ffn_norm;
+        gu.in.eps = d->eps;
+        gu.nseg = 2;
+        gu.seg_y[0] = d->h;
+        gu.seg_y[1] = d->u;
+        gu.seg_row0[1] = d->inter;
+        for (int i = 2; i <= kMaxSeg; ++i) gu.seg_row0[i] = 2u * d->inter;
+        rc = matmul_tc(ly.gate_up, d->x, nullptr, M, true, st, *dev, nullptr, 0, &gu);
+        if (rc) return rc;
+        TcFusion down;
+        down.in.up = d->u;
+        down.accumulate = true;
+        rc = matmul_tc(ly.down, d->h, d->x, M, true, st, *dev, nullptr, 0, &down);
+        if (rc) return rc;
+    }
+    if (!d->tied) {
+        TcFusion head;
+        head.in.norm_w = d->out_norm;
+        head.in.eps = d->eps;
+        return matmul_tc(d->lm_head, d->x, logits_dev, M, true, st, *dev, nullptr, 0, &head);
+    }
+    (rmsnorm_kernel<<<M, 256, 0, st>>>(d->x, d->out_norm, d->eps, d->hidden, d->xn, 0), count_launch());
+    QRAF_CUDA_TRY(cudaGetLastError());
+    const size_t warps = static_cast<size_t>(d->vocab) * M;
+    (dec_f32_matvec_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
+         static_cast<const float*>(d->lm_head.data), d->xn, d->vocab, d->hidden, M, logits_dev),
+     count_launch());
+    QRAF_CUDA_TRY(cudaGetLastError());
+    return QRAF_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_dev, const int32_t* pos_dev,
                            const int32_t* slots_dev, float* logits_dev, int mode, void* stream) {
@@ -698,6 +797,9 @@ int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_d
 
     (dec_embed_kernel<<<M, 256, 0, st>>>(d->emb, tokens_dev, d->vocab, d->hidden, d->x), count_launch());
     QRAF_CUDA_TRY(cudaGetLastError());
+    const bool tc = d->tc_route && M >= 2 &&
+                    (base_mode == QRAF_MODE_TC || (base_mode == QRAF_MODE_AUTO && M >= kAutoTcMinVectors));
+    if (tc) return tc_step(d, M, dev, ap, cfg, logits_dev, st);
     for (uint32_t l = 0; l < d->layers; ++l) {
         const DecLayer& ly = d->L[l];
         float* qkv_out[3] = {d->q, d->k, d->v};

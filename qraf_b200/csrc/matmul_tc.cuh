@@ -41,6 +41,7 @@
 #include <cuda.h>   // CUtensorMap
 
 #include "common.cuh"
+#include "matvec_rows.cuh"   // kMaxSeg, rms_factor
 
 namespace qraf_dev {
 
@@ -71,7 +72,37 @@ struct TcParams {
     uint32_t nraw, nab, nbb, nd, ns, nf;   // ring depths: raw units; weight, activation, accumulator, scale,
                                            // factor stages (two blocks each)
     uint32_t pdl;
+    // Output fusions (tc_store).  nseg >= 2: rows [seg_row0[i], seg_row0[i+1]) are
+    // weight i of a multi-weight call (weights back to back in memory, one
+    // tensor map), written to seg_y[i] ([M][rows of weight i]) with bias seg_b[i];
+    // nseg <= 1: y with bias seg_b[0].  accumulate: y = fl(result + y) (a
+    // residual add).  Biases: fl(result + b), before the accumulation.
+    uint32_t nseg, accumulate;
+    float* seg_y[kMaxSeg];
+    const float* seg_b[kMaxSeg];
+    uint32_t seg_row0[kMaxSeg + 1];
 };
+
+// One output element of row r (of the virtual weight) and vector m of this launch.
+__device__ __forceinline__ void tc_store(const TcParams& p, uint32_t r, uint32_t m, float v) {
+    float* dst;
+    const float* b;
+    if (p.nseg <= 1) {
+        dst = p.y + static_cast<size_t>(m) * p.N + r;
+        b = p.seg_b[0] ? p.seg_b[0] + r : nullptr;
+    } else {
+        uint32_t i = 0;
+#pragma unroll
+        for (int j = 1; j < kMaxSeg; ++j)
+            if (static_cast<uint32_t>(j) < p.nseg && r >= p.seg_row0[j]) i = static_cast<uint32_t>(j);
+        const uint32_t rr = r - p.seg_row0[i];
+        dst = p.seg_y[i] + static_cast<size_t>(m) * (p.seg_row0[i + 1] - p.seg_row0[i]) + rr;
+        b = p.seg_b[i] ? p.seg_b[i] + rr : nullptr;
+    }
+    if (b) v = __fadd_rn(v, *b);
+    if (p.accumulate) v = __fadd_rn(v, *dst);
+    *dst = v;
+}
 
 // ── shared-memory matrix layout: K-major, 128-byte swizzle ─────────────────
 // A tile of R rows x 64 fp16 (128 bytes per row) is R/8 atoms of 1024 bytes;
@@ -137,20 +168,14 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 // slot).  Also
 // zeroes the stream-K tile counters of the call.  A block holding a NaN or an
 // infinity gets a NaN factor, so its outputs come out NaN.
+//
+// Block b of vector m (lane = element): the two fp16 limbs into the block
+// pair's tile and the block factor 2^(e - 23) (zero for padding vectors m >= M,
+// NaN for a block holding NaN or infinity).  One warp, all lanes.
 template <uint32_t DT>
-__global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ x, uint8_t* __restrict__ act,
-                                                      uint32_t* __restrict__ tile_count, uint32_t tiles, uint32_t K,
-                                                      uint32_t M, uint32_t nblk, uint32_t n_pad, uint32_t pdl) {
-    if (pdl) pdl_wait();
-    if (pdl) pdl_launch_dependents();
-    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
-    for (uint32_t i = tid; i < tiles; i += gridDim.x * blockDim.x) tile_count[i] = 0u;
+__device__ __forceinline__ void tc_prep_block(float v, uint32_t b, uint32_t m, uint32_t lane, uint8_t* __restrict__ act,
+                                              uint32_t M, uint32_t n_pad) {
     const uint32_t half = n_pad >> 1;
-    const uint32_t gw = tid >> 5, lane = threadIdx.x & 31u;
-    if (gw >= nblk * half) return;
-    const uint32_t b = gw / half, m = gw % half;
-    float v = 0.0f;
-    if (m < M) v = __ldcg(x + static_cast<size_t>(m) * K + 32u * b + lane);
     float mx = fabsf(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
@@ -168,6 +193,59 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ 
     if (lane == 0)
         reinterpret_cast<float*>(tile + n_pad * 128u)[(b & 1u) * half + m] =
             m >= M ? 0.0f : finite ? ldexpf(1.0f, e - 23) : __int_as_float(0x7FC00000);
+}
+
+template <uint32_t DT>
+__global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ x, uint8_t* __restrict__ act,
+                                                      uint32_t* __restrict__ tile_count, uint32_t tiles, uint32_t K,
+                                                      uint32_t M, uint32_t nblk, uint32_t n_pad, uint32_t pdl) {
+    if (pdl) pdl_wait();
+    if (pdl) pdl_launch_dependents();
+    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    for (uint32_t i = tid; i < tiles; i += gridDim.x * blockDim.x) tile_count[i] = 0u;
+    const uint32_t half = n_pad >> 1;
+    const uint32_t gw = tid >> 5, lane = threadIdx.x & 31u;
+    if (gw >= nblk * half) return;
+    const uint32_t b = gw / half, m = gw % half;
+    float v = 0.0f;
+    if (m < M) v = __ldcg(x + static_cast<size_t>(m) * K + 32u * b + lane);
+    tc_prep_block<DT>(v, b, m, lane, act, M, n_pad);
+}
+
+constexpr uint32_t kTcPrepBlocks = 16;   // blocks per CTA of the fused prep kernel (two per warp)
+
+// The prep kernel with the input formed on the way (CTA (m, c) of 256 threads:
+// vector slot m, blocks [16 c, 16 c + 16); RMSNorm takes the same rms_factor as
+// the unfused pass, once per CTA):
+// up != nullptr: the input is silu(x) * up, as swiglu_apply_kernel forms it;
+// norm_w != nullptr: the input is fl(fl(x * r) * norm_w) with r = rms_factor(x),
+// as rmsnorm_kernel forms it.  Results are the bits of those passes followed
+// by tc_prep_kernel.
+template <uint32_t DT>
+__global__ void __launch_bounds__(256) tc_prep_fused_kernel(const float* __restrict__ x, const float* __restrict__ up,
+                                                            const float* __restrict__ norm_w, float eps,
+                                                            uint8_t* __restrict__ act, uint32_t* __restrict__ tile_count,
+                                                            uint32_t tiles, uint32_t K, uint32_t M, uint32_t nblk,
+                                                            uint32_t n_pad, uint32_t pdl) {
+    __shared__ double red[33];
+    if (pdl) pdl_wait();
+    if (pdl) pdl_launch_dependents();
+    const uint32_t m = blockIdx.x, lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (blockIdx.y == 0)
+        for (uint32_t i = m * blockDim.x + threadIdx.x; i < tiles; i += gridDim.x * blockDim.x) tile_count[i] = 0u;
+    const bool live = m < M;
+    const float* xm = x + static_cast<size_t>(m) * K;
+    const float r = (norm_w && live) ? rms_factor(xm, K, eps, red) : 1.0f;
+    const uint32_t b1 = min(nblk, (blockIdx.y + 1u) * kTcPrepBlocks);
+    for (uint32_t b = blockIdx.y * kTcPrepBlocks + warp; b < b1; b += blockDim.x >> 5) {
+        float v = 0.0f;
+        if (live) {
+            v = __ldcg(xm + 32u * b + lane);
+            if (up) v = (v / (1.0f + expf(-v))) * __ldcg(up + static_cast<size_t>(m) * K + 32u * b + lane);
+            if (norm_w) v = __fmul_rn(__fmul_rn(v, r), norm_w[32u * b + lane]);
+        }
+        tc_prep_block<DT>(v, b, m, lane, act, M, n_pad);
+    }
 }
 
 // ── raw block bytes -> fp16 codes in the A layout ───────────────────────────
@@ -670,12 +748,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             }
             const uint32_t t0u = t_now * p.upt, t1u = t0u + p.upt;
             const uint32_t rows = min(kTcRows, p.N - t_now * kTcRows);
-            float* yt = p.y + static_cast<size_t>(t_now) * kTcRows + row;
+            const uint32_t grow = t_now * kTcRows + row;
             if (u0 <= t0u && u1 >= t1u) {
                 if (row < rows) {
 #pragma unroll
                     for (uint32_t v = 0; v < HV; ++v)
-                        if (m0 + v < p.M) yt[static_cast<size_t>(m0 + v) * p.N] = acc[v];
+                        if (m0 + v < p.M) tc_store(p, grow, m0 + v, acc[v]);
                 }
                 continue;
             }
@@ -716,7 +794,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             if (row < rows) {
 #pragma unroll
                 for (uint32_t v = 0; v < HV; ++v)
-                    if (m0 + v < p.M) yt[static_cast<size_t>(m0 + v) * p.N] = sum[v];
+                    if (m0 + v < p.M) tc_store(p, grow, m0 + v, sum[v]);
             }
         }
         tc_fence_before();

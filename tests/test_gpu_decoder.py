@@ -181,3 +181,32 @@ def test_decoder_rejects_a_file_without_the_tensors(tmp_path, cuda):
     with pytest.raises(qb.QrafError) as e:
         qb.Decoder(path, 1, 16)
     assert e.value.code == qb.ERR_INVALID and "missing" in str(e.value)
+
+
+@pytest.mark.parametrize("arch,dt,tied", [("llama", qb.Q4_0, True), ("qwen2", qb.Q8_0, False)])
+def test_tensor_core_route(tmp_path, cuda, oracle_lib, arch, dt, tied):
+    """Three or more slots under AUTO take the tensor-core route: per layer one
+    prep + tile pair for Q/K/V (RMSNorm in the prep, three outputs and biases in
+    the store), one for O (residual in the store), one for gate/up, one for down
+    (silu(gate) * up formed in the prep, residual in the store), and the attention
+    launch; four slots at different positions against the reference."""
+    path, vocab = _model(tmp_path, oracle_lib, arch, dt, tied, max_seq=64)
+    rng = np.random.default_rng(9)
+    seqs = [[int(t) for t in rng.integers(0, vocab, 40)] for _ in range(4)]
+    start = [0, 3, 7, 12]
+    want = _reference_runs(path, vocab, seqs)
+    dec = qb.Decoder(path, max_slots=4, max_seq=64)
+    per_layer = None
+    for step in range(52):
+        active = [(i, step - start[i]) for i in range(4) if 0 <= step - start[i] < len(seqs[i])]
+        c0 = qb.launch_count()
+        got = dec.step(_i32([seqs[i][p] for i, p in active], cuda), _i32([p for _, p in active], cuda),
+                       _i32([i for i, _ in active], cuda),
+                       mode=qb.MODE_AUTO).cpu().numpy()
+        if len(active) >= 3:
+            per_layer = (qb.launch_count() - c0 - 1 - 2) / dec.layers   # embedding; head: two launches
+        for row, (i, p) in enumerate(active):
+            _close(got[row], want[i][p], f"{arch} tied={tied} step {step} sequence {i} position {p}")
+    dec.close()
+    assert per_layer == 9
+    assert qb.device_status() == qb.OK
