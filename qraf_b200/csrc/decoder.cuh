@@ -77,7 +77,7 @@ struct AttnParams {
     float* kc;                 // [max_slots][layers][max_seq][kv_dim]
     float* vc;
     float* out;                // [M][heads * hd]
-    float* part;               // [M][kv_heads][S][G][hd + 2]: unnormalised output, max, sum
+    float* part;               // [M][kv_heads][S][G][hd + 4]: unnormalised output, max, sum (16-byte records)
     uint32_t* counter;         // [M][kv_heads]: CTAs of the group finished (the last resets it)
     uint32_t heads, kv_heads, hd, G, layer, layers, max_seq, max_slots;
     float scale;               // 1 / sqrt(head_dim)
@@ -116,14 +116,14 @@ __host__ __device__ constexpr size_t attn_smem_floats(uint32_t G, uint32_t hd) {
 // group to finish (an atomic count, no waiting) merges them:
 // out = sum_c exp(max_c - max) o_c / sum_c exp(max_c - max) l_c.
 // Slots of one step must be distinct.  Launched with programmatic dependent
-// launch: all reads after griddepcontrol.wait.
-template <uint32_t HPT>   // query heads per P.V thread, at least ceil(G / (threads / hd))
+// launch: the positions, slots and the first K/V tile (earlier steps' rows) are
+// read before griddepcontrol.wait, this step's q, k and v after it.
+template <uint32_t QPT>   // output quads (four dimensions of one head) per thread: ceil(G hd / 4 / threads)
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnParams a) {
     extern __shared__ __align__(16) float att_smem[];
     __shared__ float s_alpha[kAttnMaxGroup], s_sum[kAttnMaxGroup], s_pm[kAttnMaxSplits * kAttnMaxGroup],
         s_pl[kAttnMaxSplits * kAttnMaxGroup];
     __shared__ uint32_t s_last;
-    pdl_wait();
     pdl_launch_dependents();
     const uint32_t s = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
@@ -170,7 +170,11 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         }
         cp_async_commit();
     };
+    // The first tile's copies go out before the dependency wait: positions below
+    // pos were written by earlier steps, and pos / slots by the caller before the
+    // step, so none of it depends on the launch before this one.  q, k and v do.
     issue(t0, 0);
+    pdl_wait();
 
     const float* qm = a.q + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
     for (uint32_t j = tid; j < G * half; j += kAttnThreads) {
@@ -199,13 +203,12 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     }
 
     // running softmax state: per head the max (held by the warp that scores it)
-    // and the sum; per (head, d) the output (thread (set, d), heads set + i nsets)
-    const uint32_t nsets = kAttnThreads / hd;
-    const uint32_t d = tid % hd, set = tid / hd;
-    const bool active = set < nsets;
-    float acc[HPT];
+    // and the sum; the output by quads: quad j = tid + i * threads is dimensions
+    // 4 (j % q4) .. +3 of head j / q4, accumulated as a float4 (four chains)
+    const uint32_t nquads = G * q4;
+    float4 acc[QPT];
 #pragma unroll
-    for (uint32_t i = 0; i < HPT; ++i) acc[i] = 0.0f;
+    for (uint32_t i = 0; i < QPT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     float run_max[kAttnMaxGroup / kAttnWarps], run_sum[kAttnMaxGroup / kAttnWarps];
 #pragma unroll
     for (uint32_t i = 0; i < kAttnMaxGroup / kAttnWarps; ++i) {
@@ -266,29 +269,32 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
             }
         }
         __syncthreads();
-        if (active) {
-            // heads interleaved (independent chains), probabilities four positions at a time
+        // sum_t e_t v_t by quads: V rows as float4, probabilities four positions at a
+        // time (zero past nt; the rows past nt are not read)
 #pragma unroll
-            for (uint32_t i = 0; i < HPT; ++i) {
-                const uint32_t g = set + i * nsets;
-                if (g < G) acc[i] = __fmul_rn(acc[i], s_alpha[g]);
-            }
-            for (uint32_t t = 0; t < nt; t += 4u) {   // pr is zero past nt; vs rows past nt are finite-or-unused
-                const float v0 = vs[t * ld + d];
-                const float v1 = (t + 1u < nt) ? vs[(t + 1u) * ld + d] : 0.0f;
-                const float v2 = (t + 2u < nt) ? vs[(t + 2u) * ld + d] : 0.0f;
-                const float v3 = (t + 3u < nt) ? vs[(t + 3u) * ld + d] : 0.0f;
+        for (uint32_t i = 0; i < QPT; ++i) {
+            const uint32_t j = tid + i * kAttnThreads;
+            if (j < nquads) {
+                const uint32_t g = j / q4, c4 = 4u * (j - g * q4);
+                const float al = s_alpha[g];
+                float4 o = make_float4(__fmul_rn(acc[i].x, al), __fmul_rn(acc[i].y, al), __fmul_rn(acc[i].z, al),
+                                       __fmul_rn(acc[i].w, al));
+                const float* vcol = vs + c4;
+                for (uint32_t t = 0; t < nt; t += 4u) {
+                    const float4 e4 = *reinterpret_cast<const float4*>(pr + g * kAttnTile + t);
+                    const float e[4] = {e4.x, e4.y, e4.z, e4.w};
 #pragma unroll
-                for (uint32_t i = 0; i < HPT; ++i) {
-                    const uint32_t g = set + i * nsets;
-                    if (g < G) {
-                        const float4 e4 = *reinterpret_cast<const float4*>(pr + g * kAttnTile + t);
-                        float o = fmaf(e4.x, v0, acc[i]);
-                        o = fmaf(e4.y, v1, o);
-                        o = fmaf(e4.z, v2, o);
-                        acc[i] = fmaf(e4.w, v3, o);
+                    for (uint32_t k = 0; k < 4u; ++k) {
+                        if (t + k < nt) {
+                            const float4 v = *reinterpret_cast<const float4*>(vcol + (t + k) * ld);
+                            o.x = fmaf(e[k], v.x, o.x);
+                            o.y = fmaf(e[k], v.y, o.y);
+                            o.z = fmaf(e[k], v.z, o.z);
+                            o.w = fmaf(e[k], v.w, o.w);
+                        }
                     }
                 }
+                acc[i] = o;
             }
         }
         __syncthreads();   // the stage and the probabilities are reused by the next tile
@@ -305,28 +311,31 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
 
     float* om = a.out + (static_cast<size_t>(m) * a.heads + static_cast<size_t>(kvh) * G) * hd;
     if (s_eff == 1u) {
-        if (active) {
 #pragma unroll
-            for (uint32_t i = 0; i < HPT; ++i) {
-                const uint32_t g = set + i * nsets;
-                if (g < G) om[g * hd + d] = __fmul_rn(acc[i], __fdiv_rn(1.0f, s_sum[g]));
+        for (uint32_t i = 0; i < QPT; ++i) {
+            const uint32_t j = tid + i * kAttnThreads;
+            if (j < nquads) {
+                const uint32_t g = j / q4, c4 = 4u * (j - g * q4);
+                const float inv = __fdiv_rn(1.0f, s_sum[g]);
+                *reinterpret_cast<float4*>(om + g * hd + c4) =
+                    make_float4(__fmul_rn(acc[i].x, inv), __fmul_rn(acc[i].y, inv), __fmul_rn(acc[i].z, inv),
+                                __fmul_rn(acc[i].w, inv));
             }
         }
         return;
     }
-    const size_t rec = hd + 2u;
+    const size_t rec = hd + 4u;
     float* pg = a.part + ((static_cast<size_t>(m) * a.kv_heads + kvh) * gridDim.x) * G * rec;
-    if (active) {
 #pragma unroll
-        for (uint32_t i = 0; i < HPT; ++i) {
-            const uint32_t g = set + i * nsets;
-            if (g < G) {
-                float* r = pg + (static_cast<size_t>(s) * G + g) * rec;
-                r[d] = acc[i];
-                if (d == 0) {
-                    r[hd] = s_alpha[g];     // the chunk's max
-                    r[hd + 1u] = s_sum[g];
-                }
+    for (uint32_t i = 0; i < QPT; ++i) {
+        const uint32_t j = tid + i * kAttnThreads;
+        if (j < nquads) {
+            const uint32_t g = j / q4, c4 = 4u * (j - g * q4);
+            float* r = pg + (static_cast<size_t>(s) * G + g) * rec;
+            *reinterpret_cast<float4*>(r + c4) = acc[i];
+            if (c4 == 0) {
+                r[hd] = s_alpha[g];     // the chunk's max
+                r[hd + 1u] = s_sum[g];
             }
         }
     }
@@ -363,17 +372,29 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         if (lane == 0) s_sum[g] = l;
     }
     __syncthreads();
-    for (uint32_t j = tid; j < G * hd; j += kAttnThreads) {
-        const uint32_t g = j / hd, dd = j - g * hd;
-        float v[kAttnMaxSplits];
+    for (uint32_t j = tid; j < nquads; j += kAttnThreads) {   // one quad per thread, every chunk's load in flight
+        const uint32_t g = j / q4, c4 = 4u * (j - g * q4);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t c0 = 0; c0 < s_eff; c0 += 8u) {   // eight chunks' loads in flight at a time
+            float4 v[8];
 #pragma unroll
-        for (uint32_t c = 0; c < kAttnMaxSplits; ++c)
-            v[c] = (c < s_eff) ? __ldcg(pg + (static_cast<size_t>(c) * G + g) * rec + dd) : 0.0f;
-        float o = 0.0f;
+            for (uint32_t k = 0; k < 8u; ++k)
+                if (c0 + k < s_eff)
+                    v[k] = __ldcg(reinterpret_cast<const float4*>(pg + (static_cast<size_t>(c0 + k) * G + g) * rec + c4));
 #pragma unroll
-        for (uint32_t c = 0; c < kAttnMaxSplits; ++c)
-            if (c < s_eff) o = fmaf(s_pm[c * G + g], v[c], o);
-        om[g * hd + dd] = __fmul_rn(o, __fdiv_rn(1.0f, s_sum[g]));
+            for (uint32_t k = 0; k < 8u; ++k) {
+                if (c0 + k < s_eff) {
+                    const float w = s_pm[(c0 + k) * G + g];
+                    o.x = fmaf(w, v[k].x, o.x);
+                    o.y = fmaf(w, v[k].y, o.y);
+                    o.z = fmaf(w, v[k].z, o.z);
+                    o.w = fmaf(w, v[k].w, o.w);
+                }
+            }
+        }
+        const float inv = __fdiv_rn(1.0f, s_sum[g]);
+        *reinterpret_cast<float4*>(om + g * hd + c4) =
+            make_float4(__fmul_rn(o.x, inv), __fmul_rn(o.y, inv), __fmul_rn(o.z, inv), __fmul_rn(o.w, inv));
     }
 }
 
@@ -582,7 +603,7 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
     uint64_t part_floats = 0;
     for (uint32_t M = 1; M <= max_slots; ++M) {
         const uint32_t S = attn_splits(d.get(), M, dev->sm_count);
-        part_floats = std::max<uint64_t>(part_floats, static_cast<uint64_t>(M) * d->heads * S * (d->hd + 2u));
+        part_floats = std::max<uint64_t>(part_floats, static_cast<uint64_t>(M) * d->heads * S * (d->hd + 4u));
     }
     const size_t smem_max = attn_smem_floats(d->G, d->hd) * sizeof(float);
     if (smem_max + kSmemReserve > static_cast<size_t>(dev->smem_optin)) {
@@ -607,10 +628,9 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
         if (e == cudaSuccess) e = cudaMemset(d->vc, 0, cache * sizeof(float));
         if (e == cudaSuccess)
             e = cudaMemset(d->counter, 0, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t));
-        const uint32_t per = (d->G + kAttnThreads / d->hd - 1u) / (kAttnThreads / d->hd);
+        const uint32_t per = (d->G * (d->hd / 4u) + kAttnThreads - 1u) / kAttnThreads;   // quads per thread
         d->attn_kernel = per <= 1u ? dec_attention_kernel<1> : per <= 2u ? dec_attention_kernel<2>
-                         : per <= 4u ? dec_attention_kernel<4> : per <= 8u ? dec_attention_kernel<8>
-                                                                            : dec_attention_kernel<16>;
+                                                                         : dec_attention_kernel<4>;
         if (e == cudaSuccess) e = cudaFuncSetAttribute(d->attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        static_cast<int>(smem_max));
         if (e == cudaSuccess) {
