@@ -1105,19 +1105,22 @@ DECODE_METRIC = "decode tokens/s"
 
 
 def parse_decode_workload(name: str):
-    """'qwen3b_decode' / 'qwen3b_decode_m8_c1024' -> (model, M slots, context length), else None."""
+    """'qwen3b_decode' / 'qwen3b_decode_m8_c1024[_kv8]' -> (model, M slots, context length, int8 KV cache),
+    else None."""
     parts = name.split("_")
     if len(parts) < 2 or parts[0] not in DECODE_MODELS or parts[1] != "decode":
         return None
-    m, ctx = 1, 512
+    m, ctx, kv8 = 1, 512, False
     for p in parts[2:]:
         if p.startswith("m") and p[1:].isdigit():
             m = int(p[1:])
         elif p.startswith("c") and p[1:].isdigit():
             ctx = int(p[1:])
+        elif p == "kv8":
+            kv8 = True
         else:
             raise SystemExit(f"unknown decode workload part '{p}' in {name}")
-    return parts[0], m, ctx
+    return parts[0], m, ctx, kv8
 
 
 def decode_shapes(model):
@@ -1190,11 +1193,11 @@ def decode_file_path(model):
     return os.path.join(d, f"qraf_bench_{model}_{os.getpid()}.qraf")
 
 
-def decode_bytes_per_step(model, m, ctx):
+def decode_bytes_per_step(model, m, ctx, kv8=False):
     """Algorithmic HBM bytes of one decode step of M slots at position ctx: every
     quantized weight once, the F32 norms and biases, each slot's embedding row,
-    its K and V over ctx + 1 positions of every layer, and the step's K/V writes.
-    Returns (total, weights)."""
+    its K and V over ctx + 1 positions of every layer (int8 codes and a scale per
+    KV head with kv8), and the step's K/V writes.  Returns (total, weights)."""
     tok = TOKEN_MODELS[model]
     shapes = decode_shapes(model)
     bb = BLOCK_BYTES[tok["dtype"]]
@@ -1202,11 +1205,13 @@ def decode_bytes_per_step(model, m, ctx):
     weights = layers * sum(n * (k // 32) * bb for n, k in shapes.values()) + vocab * (hidden // 32) * bb
     kv_dim = shapes["k_proj"][0]
     small = 4 * ((2 * layers + 1) * hidden + layers * (shapes["q_proj"][0] + 2 * kv_dim))
-    kv = m * layers * (ctx + 1) * kv_dim * 4 * 2 + m * layers * kv_dim * 4 * 2
+    kvh = DECODE_MODELS[model]["kv_heads"]
+    per_pos = 2 * (kv_dim + 4 * kvh) if kv8 else 2 * 4 * kv_dim
+    kv = m * layers * (ctx + 1) * per_pos + m * layers * per_pos
     return weights + small + m * hidden * 4 + kv, weights
 
 
-def run_decode(args, model, m, ctx):
+def run_decode(args, model, m, ctx, kv8=False):
     """One STEP = one decode token for each of M slots through the whole model
     (qraf_cuda_decoder_step over a .qraf file written here), every slot at
     position ctx with ctx positions of its KV cache filled by earlier steps;
@@ -1235,9 +1240,9 @@ def run_decode(args, model, m, ctx):
         file_bytes = write_decode_file(model, path, fill, quantize, max_seq=ctx + 1)
         t_w = time.perf_counter() - t_w
         t_o = time.perf_counter()
-        dec = qb.Decoder(path, max_slots=m, max_seq=ctx + 1)
+        dec = qb.Decoder(path, max_slots=m, max_seq=ctx + 1, kv_int8=kv8)
         t_o = time.perf_counter() - t_o
-        line = _decode_measure(args, model, m, ctx, dec, mode)
+        line = _decode_measure(args, model, m, ctx, dec, mode, kv8)
         line["config"].update({"file_bytes": file_bytes, "write_s": round(t_w, 2), "open_s": round(t_o, 2)})
         dec.close()
         line["cpu_baseline"] = decode_cpu_baseline(model, ctx, args.cpu_seconds, path) if args.cpu_seconds > 0 \
@@ -1248,7 +1253,7 @@ def run_decode(args, model, m, ctx):
     print(json.dumps(line), flush=True)
 
 
-def _decode_measure(args, model, m, ctx, dec, mode):
+def _decode_measure(args, model, m, ctx, dec, mode, kv8=False):
     import torch
 
     import qraf_b200 as qb
@@ -1307,7 +1312,7 @@ def _decode_measure(args, model, m, ctx, dec, mode):
     e2e_s = time.perf_counter() - te
     status = qb.device_status()
     step_s = elapsed_ms / 1e3 / args.steps
-    bytes_step, weight_bytes = decode_bytes_per_step(model, m, ctx)
+    bytes_step, weight_bytes = decode_bytes_per_step(model, m, ctx, kv8)
     peak, peak_src = measured_peaks()
     achieved = bytes_step / step_s / 1e9
     line = {
@@ -1317,6 +1322,8 @@ def _decode_measure(args, model, m, ctx, dec, mode):
         "config": {"workload": args.workload, "model_shapes": model, "architecture": DECODE_MODELS[model]["arch"],
                    "M": m, "context": ctx, "layers": tok["layers"], "quant": "Q4_0" if dt == Q4 else "Q8_0",
                    "mode": args.mode, "weight_bytes_per_step": weight_bytes,
+                   "kv_cache": "int8 codes + fp32 scale per (position, KV head) (QuantizedKVCache layout)" if kv8
+                   else "f32",
                    "l2_policy": f"inputs larger than L2: {weight_bytes / 1e9:.1f} GB of distinct weights per step",
                    "weights": "N(0,0.02) std::mt19937(42) per projection shape, quantized on GPU (byte-exact Q*_0), "
                               "one copy per layer in the file; embedding = the LM head's draw in F32",
@@ -1362,7 +1369,7 @@ def decode_cpu_baseline(model, ctx, budget_s, path):
                       f"single-threaded, as it runs on Linux) over the same .qraf file, {dt_s:.1f} s"}
 
 
-def run_decode_reference(args, model, m, ctx):
+def run_decode_reference(args, model, m, ctx, kv8=False):
     """The reference arm: its Transformer over the same file (written with the
     reference's own quantizer and RNG), one request at a time as its scheduler
     runs them; M slots cost M forwards, so tokens/s does not depend on M."""

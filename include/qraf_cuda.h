@@ -343,6 +343,19 @@ int qraf_cuda_model_tensor_f32(qraf_model_t m, const char* name, const float** d
  * x kv_dim per K and V and the RoPE angles of every position. */
 typedef struct qraf_decoder* qraf_decoder_t;
 int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_seq, qraf_decoder_t* out);
+/* qraf_cuda_decoder_open with flags.  QRAF_DECODER_KV_INT8: the KV cache holds
+ * int8 codes with an fp32 scale per (position, KV head), quantized as the
+ * reference's QuantizedKVCache::store does (include/nn/kv_cache_quant.h:61-94:
+ * scale = max |x| / 127, codes clamp(round(x / scale), -127, 127)); attention
+ * reads the codes (scores dot(q, codes) * scale, kv_cache_quant.h:113-123).
+ * A quarter of the cache's bytes; needs head_dim % 16 == 0. */
+#define QRAF_DECODER_KV_INT8 1u
+int qraf_cuda_decoder_open_ex(const char* path, uint32_t max_slots, uint32_t max_seq, uint32_t flags,
+                              qraf_decoder_t* out);
+/* Copy one cache row (slot, layer, position) to host memory: kv_dim floats of K
+ * and of V, or with the int8 cache kv_dim codes of each and kv_heads scales of each. */
+int qraf_cuda_decoder_kv_read(qraf_decoder_t d, uint32_t slot, uint32_t layer, uint32_t pos, void* k_out, void* v_out,
+                              float* k_scales, float* v_scales);
 /* One decode step for M <= max_slots slots at once: slot slots_dev[m] takes
  * token tokens_dev[m] at position pos_dev[m] (all device int32 arrays of M;
  * slots distinct within a step; positions < max_seq), writes K/V at that

@@ -214,10 +214,20 @@ class Reference:
                 ("qref_model_hidden_size", C.c_uint32, [vp]),
                 ("qref_transformer_open", vp, [cp]), ("qref_transformer_close", None, [vp]),
                 ("qref_transformer_reset", None, [vp]),
-                ("qref_transformer_forward", C.c_int, [vp, C.c_uint32, C.c_int, _f32p, C.c_uint32])):
+                ("qref_transformer_forward", C.c_int, [vp, C.c_uint32, C.c_int, _f32p, C.c_uint32]),
+                ("qref_kvq_store", None, [_f32p, _f32p, C.c_int, C.c_int, vp, vp, _f32p, _f32p])):
             fn = getattr(lib, name)
             fn.restype, fn.argtypes = res, args
         self.lib = lib
+
+    def kv_quantize(self, k: np.ndarray, v: np.ndarray, kv_heads: int, head_dim: int):
+        """QuantizedKVCache::store of one K/V row: (k codes, v codes, k scales, v scales)."""
+        n = kv_heads * head_dim
+        kq, vq = np.empty(n, np.int8), np.empty(n, np.int8)
+        ks, vs = np.empty(kv_heads, np.float32), np.empty(kv_heads, np.float32)
+        self.lib.qref_kvq_store(np.ascontiguousarray(k, np.float32), np.ascontiguousarray(v, np.float32), kv_heads,
+                                head_dim, kq.ctypes.data, vq.ctypes.data, ks, vs)
+        return kq, vq, ks, vs
 
     def fill_normal(self, seed: int, mean: float, std: float, n: int) -> np.ndarray:
         out = np.empty(n, dtype=np.float32)

@@ -11,6 +11,7 @@
 #include "nn/attention.h"
 #include "nn/backend.h"
 #include "nn/ops.h"
+#include "nn/kv_cache_quant.h"
 #include "nn/transformer.h"
 #include "qraf/format.h"
 #include "qraf/loader.h"
@@ -215,6 +216,20 @@ int qref_transformer_forward(void* h, uint32_t token, int pos, float* logits, ui
     if (t.numel() != vocab) return 1;
     std::memcpy(logits, t.data_f32(), vocab * sizeof(float));
     return 0;
+}
+
+// The reference's int8 KV cache (include/nn/kv_cache_quant.h): one row of K and V
+// (kv_heads * head_dim floats each) stored at position 0 of a one-layer cache and
+// read back as codes and per-head scales; dot_with_key for a query against it.
+void qref_kvq_store(const float* k, const float* v, int kv_heads, int head_dim, int8_t* kq, int8_t* vq, float* ks,
+                    float* vs) {
+    QuantizedKVCache c;
+    c.init(1, kv_heads, head_dim, 1);
+    c.store(0, 0, k, v);
+    std::memcpy(kq, c.keys_q[0].data(), static_cast<size_t>(kv_heads) * head_dim);
+    std::memcpy(vq, c.values_q[0].data(), static_cast<size_t>(kv_heads) * head_dim);
+    std::memcpy(ks, c.key_scales[0].data(), kv_heads * sizeof(float));
+    std::memcpy(vs, c.value_scales[0].data(), kv_heads * sizeof(float));
 }
 
 // Seeded synthetic data with the reference's idiom (std::mt19937 +

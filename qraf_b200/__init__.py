@@ -29,6 +29,7 @@ MODE_TC = 2
 MODE_AUTO = 3
 MODE_FLAG_OVERLAP = 0x100
 MODEL_F32 = 1               # qraf_cuda_model_open_ex: upload the F32 tensors too
+DECODER_KV_INT8 = 1         # qraf_cuda_decoder_open_ex: int8 KV cache (the reference's QuantizedKVCache)
 
 OK = 0
 ERR_INVALID = 1
@@ -108,6 +109,8 @@ def _load() -> C.CDLL:
         "qraf_cuda_decoder_info": (i32, [vp, C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), C.POINTER(u32),
                                          C.POINTER(u32)]),
         "qraf_cuda_decoder_close": (i32, [vp]),
+        "qraf_cuda_decoder_open_ex": (i32, [C.c_char_p, u32, u32, u32, C.POINTER(vp)]),
+        "qraf_cuda_decoder_kv_read": (i32, [vp, u32, u32, u32, vp, vp, f32p, f32p]),
         "qraf_cuda_model_open_ex": (i32, [C.c_char_p, u32, C.POINTER(vp)]),
         "qraf_cuda_model_tensor_f32": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(u64)]),
         "qraf_fill_normal": (None, [u32, C.c_float, C.c_float, f32p, u64]),
@@ -305,9 +308,11 @@ class Decoder:
     """A Llama / Qwen2 decode engine over a .qraf file (qraf_cuda_decoder_*):
     step() runs one decode step for M slots at once, each with its own KV cache."""
 
-    def __init__(self, path: str, max_slots: int = 1, max_seq: int = 2048):
+    def __init__(self, path: str, max_slots: int = 1, max_seq: int = 2048, kv_int8: bool = False):
         h = C.c_void_p()
-        check(_get_lib().qraf_cuda_decoder_open(os.fsencode(path), max_slots, max_seq, C.byref(h)))
+        check(_get_lib().qraf_cuda_decoder_open_ex(os.fsencode(path), max_slots, max_seq,
+                                                   DECODER_KV_INT8 if kv_int8 else 0, C.byref(h)))
+        self.kv_int8 = kv_int8
         self._h = h
         v, hd, l, ms, mq = (C.c_uint32() for _ in range(5))
         check(_get_lib().qraf_cuda_decoder_info(h, C.byref(v), C.byref(hd), C.byref(l), C.byref(ms), C.byref(mq)))
@@ -327,6 +332,21 @@ class Decoder:
                                                 C.c_void_p(positions.data_ptr()), C.c_void_p(slots.data_ptr()),
                                                 C.c_void_p(logits.data_ptr()), mode, _stream(stream)))
         return logits
+
+    def kv_read(self, slot: int, layer: int, pos: int, kv_heads: int, head_dim: int):
+        """One cache row: (k, v) float32 [kv_heads * head_dim], or with the int8 cache
+        (k codes, v codes, k scales, v scales)."""
+        n = kv_heads * head_dim
+        if self.kv_int8:
+            k, v = np.empty(n, np.int8), np.empty(n, np.int8)
+            ks, vs = np.empty(kv_heads, np.float32), np.empty(kv_heads, np.float32)
+            check(_get_lib().qraf_cuda_decoder_kv_read(self._h, slot, layer, pos, k.ctypes.data, v.ctypes.data,
+                                                       ks.ctypes.data_as(C.POINTER(C.c_float)),
+                                                       vs.ctypes.data_as(C.POINTER(C.c_float))))
+            return k, v, ks, vs
+        k, v = np.empty(n, np.float32), np.empty(n, np.float32)
+        check(_get_lib().qraf_cuda_decoder_kv_read(self._h, slot, layer, pos, k.ctypes.data, v.ctypes.data, None, None))
+        return k, v
 
     def close(self) -> None:
         if self._h:

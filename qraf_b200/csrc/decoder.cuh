@@ -77,6 +77,10 @@ struct AttnParams {
     float* kc;                 // [max_slots][layers][max_seq][kv_dim]
     float* vc;
     float* out;                // [M][heads * hd]
+    int8_t* kq;                // int8 cache (QRAF_DECODER_KV_INT8): [max_slots][layers][max_seq][kv_dim]
+    int8_t* vq;
+    float* ksc;                // its scales: [max_slots][layers][max_seq][kv_heads]
+    float* vsc;
     float* part;               // [M][kv_heads][S][G][hd + 4]: unnormalised output, max, sum (16-byte records)
     uint32_t* counter;         // [M][kv_heads]: CTAs of the group finished (the last resets it)
     uint32_t heads, kv_heads, hd, G, layer, layers, max_seq, max_slots;
@@ -95,6 +99,34 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // two stages of K and V tiles [kAttnTile][hd + 4] each, probabilities [G][kAttnTile].
 __host__ __device__ constexpr size_t attn_smem_floats(uint32_t G, uint32_t hd) {
     return static_cast<size_t>(G) * hd + 2u * hd + 4u * kAttnTile * (hd + 4u) + static_cast<size_t>(G) * kAttnTile;
+}
+
+// The int8 cache's tiles: rows of hd codes at a stride of ld8 bytes (16-byte
+// aligned, an odd number of 16-byte chunks so a warp's 16-byte reads of 32 rows
+// meet no bank conflict), with the rows' scales.  Bytes of dynamic shared memory:
+// q rotated [G][hd] floats, the new k and v codes [hd] each, two stages of
+// {K codes [T][ld8], V codes [T][ld8], K scales [T], V scales [T]}, probabilities [G][T].
+__host__ __device__ constexpr uint32_t attn_ld8(uint32_t hd) { return ((hd / 16u) % 2u == 0u) ? hd + 16u : hd + 32u; }
+__host__ __device__ constexpr size_t attn_stage8_bytes(uint32_t hd) {
+    return 2u * kAttnTile * attn_ld8(hd) + 2u * kAttnTile * 4u;
+}
+__host__ __device__ constexpr size_t attn_smem_bytes8(uint32_t G, uint32_t hd) {
+    return 4u * static_cast<size_t>(G) * hd + 2u * hd + 2u * attn_stage8_bytes(hd) + 4u * static_cast<size_t>(G) * kAttnTile;
+}
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// QuantizedKVCache::store for one value (include/nn/kv_cache_quant.h:61-94):
+// clamp(round(x * inv), -127, 127), inv = 1 / (max |x| / 127) (0 when the max is 0).
+__device__ __forceinline__ int8_t kvq_code(float x, float inv) {
+    return static_cast<int8_t>(fmaxf(-127.0f, fminf(127.0f, roundf(__fmul_rn(x, inv)))));
+}
+__device__ __forceinline__ float4 i8x4_to_f4(uint32_t w) {
+    return make_float4(static_cast<float>(static_cast<int8_t>(w)), static_cast<float>(static_cast<int8_t>(w >> 8)),
+                       static_cast<float>(static_cast<int8_t>(w >> 16)), static_cast<float>(static_cast<int8_t>(w >> 24)));
 }
 
 // Attention of one step, fused with RoPE and the KV-cache store
@@ -118,12 +150,19 @@ __host__ __device__ constexpr size_t attn_smem_floats(uint32_t G, uint32_t hd) {
 // Slots of one step must be distinct.  Launched with programmatic dependent
 // launch: the positions, slots and the first K/V tile (earlier steps' rows) are
 // read before griddepcontrol.wait, this step's q, k and v after it.
-template <uint32_t QPT>   // output quads (four dimensions of one head) per thread: ceil(G hd / 4 / threads)
+// QPT: output quads (four dimensions of one head) per thread, ceil(G hd / 4 /
+// threads).  KV8: the cache holds int8 codes with a scale per (position, KV
+// head) (QRAF_DECODER_KV_INT8, the reference's QuantizedKVCache layout): scores
+// are fl(dot(q, codes) * scale) * 1 / sqrt(head_dim) (dot_with_key,
+// kv_cache_quant.h:113-123), and each value row's scale is folded into its
+// probability.
+template <uint32_t QPT, bool KV8>
 __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnParams a) {
     extern __shared__ __align__(16) float att_smem[];
     __shared__ float s_alpha[kAttnMaxGroup], s_sum[kAttnMaxGroup], s_pm[kAttnMaxSplits * kAttnMaxGroup],
         s_pl[kAttnMaxSplits * kAttnMaxGroup];
-    __shared__ uint32_t s_last;
+    __shared__ uint32_t s_last, s_kmax, s_vmax;
+    __shared__ float s_kscale, s_vscale;
     pdl_launch_dependents();
     const uint32_t s = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
@@ -144,19 +183,54 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
     float* vnew = knew + hd;                               // [hd]
     float* kv_st = vnew + hd;                              // stage b: K at kv_st + 2 b T ld, V after it
     float* pr = kv_st + 4u * kAttnTile * ld;               // [G][kAttnTile]
+    // the int8 layout (KV8): codes of the new row, then the two stages
+    const uint32_t ld8 = attn_ld8(hd);
+    int8_t* knew8 = reinterpret_cast<int8_t*>(qs + G * hd);
+    int8_t* vnew8 = knew8 + hd;
+    uint8_t* st8 = reinterpret_cast<uint8_t*>(vnew8 + hd);
+    if constexpr (KV8) pr = reinterpret_cast<float*>(st8 + 2u * attn_stage8_bytes(hd));
     const bool owner = (s == s_eff - 1u);
     const float2* cs = a.rope + static_cast<size_t>(p) * half;
     const size_t base =
         (static_cast<size_t>(sl) * a.layers + a.layer) * a.max_seq * kv_dim + static_cast<size_t>(kvh) * hd;
     const float* kbase = a.kc + base;
     const float* vbase = a.vc + base;
+    const size_t sbase = (static_cast<size_t>(sl) * a.layers + a.layer) * a.max_seq * a.kv_heads + kvh;   // scales
+    auto stage8 = [&](uint32_t b, int8_t*& kc8, int8_t*& vc8, float*& kscl, float*& vscl) {
+        uint8_t* st = st8 + b * attn_stage8_bytes(hd);
+        kc8 = reinterpret_cast<int8_t*>(st);
+        vc8 = kc8 + kAttnTile * ld8;
+        kscl = reinterpret_cast<float*>(vc8 + kAttnTile * ld8);
+        vscl = kscl + kAttnTile;
+    };
 
     // tile copies: rows [tt, tt + nt) of K and V into stage b, row pos excluded
     // (it is this step's, taken from knew / vnew).  Thread: 16-byte column c0 of
     // rows r0, r0 + rstep, ... (no division in the loop)
     const uint32_t rstep = kAttnThreads / q4, c0 = tid % q4, r0 = tid / q4;
+    const uint32_t q16 = hd / 16u, rstep8 = kAttnThreads / q16, c08 = tid % q16, r08 = tid / q16;
     auto issue = [&](uint32_t tt, uint32_t b) {
         const uint32_t nt = min(kAttnTile, t1 - tt);
+        if constexpr (KV8) {
+            int8_t *kc8, *vc8;
+            float *kscl, *vscl;
+            stage8(b, kc8, vc8, kscl, vscl);
+            if (r08 < rstep8) {
+                for (uint32_t r = r08; r < nt; r += rstep8) {
+                    const uint32_t t = tt + r;
+                    if (t == static_cast<uint32_t>(p)) continue;
+                    const size_t off = base + static_cast<size_t>(t) * kv_dim + 16u * c08;
+                    cp_async16(kc8 + r * ld8 + 16u * c08, a.kq + off);
+                    cp_async16(vc8 + r * ld8 + 16u * c08, a.vq + off);
+                }
+            }
+            if (tid < nt && tt + tid != static_cast<uint32_t>(p)) {
+                cp_async4(kscl + tid, a.ksc + sbase + static_cast<size_t>(tt + tid) * a.kv_heads);
+                cp_async4(vscl + tid, a.vsc + sbase + static_cast<size_t>(tt + tid) * a.kv_heads);
+            }
+            cp_async_commit();
+            return;
+        }
         float* ks = kv_st + 2u * b * kAttnTile * ld;
         float* vs = ks + kAttnTile * ld;
         if (r0 < rstep) {
@@ -183,7 +257,53 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         qs[g * hd + 2u * i] = r.x;
         qs[g * hd + 2u * i + 1u] = r.y;
     }
-    if (owner) {
+    if (owner && KV8) {
+        // the new row quantized as QuantizedKVCache::store does (kv_cache_quant.h:61-94):
+        // per head scale = max |x| / 127 (NaN never the max, as std::max skips it)
+        const float* km = a.k + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
+        const float* vm = a.v + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
+        if (tid == 0) {
+            s_kmax = 0u;
+            s_vmax = 0u;
+        }
+        __syncthreads();
+        float2 kr = make_float2(0.f, 0.f);
+        float vv = 0.0f;
+        if (tid < half) {
+            kr = rope_pair(km[2u * tid], km[2u * tid + 1u], cs[tid]);
+            if (!isnan(kr.x)) atomicMax(&s_kmax, __float_as_uint(fabsf(kr.x)));
+            if (!isnan(kr.y)) atomicMax(&s_kmax, __float_as_uint(fabsf(kr.y)));
+        }
+        if (tid < hd) {
+            vv = vm[tid];
+            if (!isnan(vv)) atomicMax(&s_vmax, __float_as_uint(fabsf(vv)));
+        }
+        __syncthreads();
+        const float kscale = __fdiv_rn(__uint_as_float(s_kmax), 127.0f);
+        const float vscale = __fdiv_rn(__uint_as_float(s_vmax), 127.0f);
+        const float kinv = kscale > 0.0f ? __fdiv_rn(1.0f, kscale) : 0.0f;
+        const float vinv = vscale > 0.0f ? __fdiv_rn(1.0f, vscale) : 0.0f;
+        const size_t row = base + static_cast<size_t>(p) * kv_dim;
+        if (tid < half) {
+            const int8_t c0 = kvq_code(kr.x, kinv), c1 = kvq_code(kr.y, kinv);
+            knew8[2u * tid] = c0;
+            knew8[2u * tid + 1u] = c1;
+            a.kq[row + 2u * tid] = c0;
+            a.kq[row + 2u * tid + 1u] = c1;
+        }
+        if (tid < hd) {
+            const int8_t c = kvq_code(vv, vinv);
+            vnew8[tid] = c;
+            a.vq[row + tid] = c;
+        }
+        if (tid == 0) {
+            s_kscale = kscale;
+            s_vscale = vscale;
+            a.ksc[sbase + static_cast<size_t>(p) * a.kv_heads] = kscale;
+            a.vsc[sbase + static_cast<size_t>(p) * a.kv_heads] = vscale;
+        }
+    }
+    if (owner && !KV8) {
         const float* km = a.k + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
         const float* vm = a.v + static_cast<size_t>(m) * kv_dim + static_cast<size_t>(kvh) * hd;
         float* kdst = a.kc + base + static_cast<size_t>(p) * kv_dim;
@@ -228,11 +348,23 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
         }
         float* ks = kv_st + 2u * b * kAttnTile * ld;
         float* vs = ks + kAttnTile * ld;
+        int8_t *kc8 = nullptr, *vc8 = nullptr;
+        float *kscl = nullptr, *vscl = nullptr;
+        if constexpr (KV8) stage8(b, kc8, vc8, kscl, vscl);
         if (static_cast<uint32_t>(p) >= tt && static_cast<uint32_t>(p) < tt + nt) {
             const uint32_t r = static_cast<uint32_t>(p) - tt;
             for (uint32_t j = tid; j < hd; j += kAttnThreads) {
-                ks[r * ld + j] = knew[j];
-                vs[r * ld + j] = vnew[j];
+                if constexpr (KV8) {
+                    kc8[r * ld8 + j] = knew8[j];
+                    vc8[r * ld8 + j] = vnew8[j];
+                } else {
+                    ks[r * ld + j] = knew[j];
+                    vs[r * ld + j] = vnew[j];
+                }
+            }
+            if (KV8 && tid == 0) {
+                kscl[r] = s_kscale;
+                vscl[r] = s_vscale;
             }
         }
         __syncthreads();
@@ -243,25 +375,43 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
             if (g < G) {
                 float sc = -INFINITY;
                 if (lane < nt) {
-                    const float4* kr = reinterpret_cast<const float4*>(ks + lane * ld);
                     const float4* qr = reinterpret_cast<const float4*>(qs + g * hd);
                     float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;   // four chains
+                    if constexpr (KV8) {
+                        const uint4* kr8 = reinterpret_cast<const uint4*>(kc8 + lane * ld8);
+                        for (uint32_t c = 0; c < q16; ++c) {
+                            const uint4 raw = kr8[c];
+                            const uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                            for (uint32_t j = 0; j < 4u; ++j) {
+                                const float4 kk = i8x4_to_f4(wd[j]), qq = qr[4u * c + j];
+                                d0 = fmaf(qq.x, kk.x, d0);
+                                d1 = fmaf(qq.y, kk.y, d1);
+                                d2 = fmaf(qq.z, kk.z, d2);
+                                d3 = fmaf(qq.w, kk.w, d3);
+                            }
+                        }
+                        sc = __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)), kscl[lane]), a.scale);
+                    } else {
+                        const float4* kr = reinterpret_cast<const float4*>(ks + lane * ld);
 #pragma unroll 4
-                    for (uint32_t c = 0; c < q4; ++c) {
-                        const float4 kk = kr[c], qq = qr[c];
-                        d0 = fmaf(qq.x, kk.x, d0);
-                        d1 = fmaf(qq.y, kk.y, d1);
-                        d2 = fmaf(qq.z, kk.z, d2);
-                        d3 = fmaf(qq.w, kk.w, d3);
+                        for (uint32_t c = 0; c < q4; ++c) {
+                            const float4 kk = kr[c], qq = qr[c];
+                            d0 = fmaf(qq.x, kk.x, d0);
+                            d1 = fmaf(qq.y, kk.y, d1);
+                            d2 = fmaf(qq.z, kk.z, d2);
+                            d3 = fmaf(qq.w, kk.w, d3);
+                        }
+                        sc = __fmul_rn(__fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)), a.scale);
                     }
-                    sc = __fmul_rn(__fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)), a.scale);
                 }
                 float mt = sc;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
                 const float mnew = fmaxf(run_max[i], mt);
                 const float e = (lane < nt) ? expf(__fsub_rn(sc, mnew)) : 0.0f;
-                pr[g * kAttnTile + lane] = e;
+                if constexpr (KV8) pr[g * kAttnTile + lane] = (lane < nt) ? __fmul_rn(e, vscl[lane]) : 0.0f;
+                else pr[g * kAttnTile + lane] = e;
                 const float alpha = expf(__fsub_rn(run_max[i], mnew));   // 0 on the first tile
                 run_sum[i] = __fadd_rn(__fmul_rn(run_sum[i], alpha), warp_sum(e));
                 run_max[i] = mnew;
@@ -286,7 +436,8 @@ __global__ void __launch_bounds__(kAttnThreads) dec_attention_kernel(const AttnP
 #pragma unroll
                     for (uint32_t k = 0; k < 4u; ++k) {
                         if (t + k < nt) {
-                            const float4 v = *reinterpret_cast<const float4*>(vcol + (t + k) * ld);
+                            const float4 v = KV8 ? i8x4_to_f4(*reinterpret_cast<const uint32_t*>(vc8 + (t + k) * ld8 + c4))
+                                                 : *reinterpret_cast<const float4*>(vcol + (t + k) * ld);
                             o.x = fmaf(e[k], v.x, o.x);
                             o.y = fmaf(e[k], v.y, o.y);
                             o.z = fmaf(e[k], v.z, o.z);
@@ -436,8 +587,13 @@ struct qraf_decoder {
     bool tied = false;
     qraf_weight_t lm_head{};
     std::vector<DecLayer> L;
+    bool kv8 = false;             // QRAF_DECODER_KV_INT8: the int8 cache below instead of kc / vc
     float* kc = nullptr;          // [max_slots][layers][max_seq][kv_dim]
     float* vc = nullptr;
+    int8_t* kq = nullptr;         // [max_slots][layers][max_seq][kv_dim]
+    int8_t* vq = nullptr;
+    float* ksc = nullptr;         // [max_slots][layers][max_seq][kv_heads]
+    float* vsc = nullptr;
     float2* rope = nullptr;       // [max_seq][hd / 2]
     float* part = nullptr;        // attention partials, sized for the largest step
     uint32_t* counter = nullptr;  // [max_slots][kv_heads]
@@ -470,6 +626,9 @@ int qraf_cuda_decoder_close(qraf_decoder_t d) {
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(d->device);
+    for (void* p : {static_cast<void*>(d->kq), static_cast<void*>(d->vq), static_cast<void*>(d->ksc),
+                    static_cast<void*>(d->vsc)})
+        if (p) cudaFree(p);
     for (void* p : {static_cast<void*>(d->kc), static_cast<void*>(d->vc), static_cast<void*>(d->rope),
                     static_cast<void*>(d->part), static_cast<void*>(d->counter), static_cast<void*>(d->work)})
         if (p) cudaFree(p);
@@ -480,8 +639,14 @@ int qraf_cuda_decoder_close(qraf_decoder_t d) {
 }
 
 int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_seq, qraf_decoder_t* out) {
+    return qraf_cuda_decoder_open_ex(path, max_slots, max_seq, 0u, out);
+}
+
+int qraf_cuda_decoder_open_ex(const char* path, uint32_t max_slots, uint32_t max_seq, uint32_t flags,
+                              qraf_decoder_t* out) {
     if (!out) return fail(QRAF_ERR_INVALID, "out is NULL");
     *out = nullptr;
+    if (flags & ~static_cast<uint32_t>(QRAF_DECODER_KV_INT8)) return fail(QRAF_ERR_INVALID, "unknown flags 0x%x", flags);
     if (max_slots == 0 || max_seq == 0) return fail(QRAF_ERR_INVALID, "max_slots and max_seq must be positive");
     if (max_slots > 65535u || max_seq > (1u << 24))
         return fail(QRAF_ERR_UNSUPPORTED, "max_slots above 65535 or max_seq above 2^24");
@@ -605,7 +770,9 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
         const uint32_t S = attn_splits(d.get(), M, dev->sm_count);
         part_floats = std::max<uint64_t>(part_floats, static_cast<uint64_t>(M) * d->heads * S * (d->hd + 4u));
     }
-    const size_t smem_max = attn_smem_floats(d->G, d->hd) * sizeof(float);
+    d->kv8 = (flags & QRAF_DECODER_KV_INT8) != 0;
+    if (d->kv8 && d->hd % 16u) return fail_close(QRAF_ERR_UNSUPPORTED, "the int8 KV cache needs head_dim % 16 == 0");
+    const size_t smem_max = d->kv8 ? attn_smem_bytes8(d->G, d->hd) : attn_smem_floats(d->G, d->hd) * sizeof(float);
     if (smem_max + kSmemReserve > static_cast<size_t>(dev->smem_optin)) {
         cudaSetDevice(cur);
         return fail_close(QRAF_ERR_UNSUPPORTED, "head_dim " + std::to_string(d->hd) + " with " + std::to_string(d->G) +
@@ -615,22 +782,37 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
     const uint64_t cache = static_cast<uint64_t>(max_slots) * d->layers * max_seq * kv_dim;
     const size_t ws = static_cast<size_t>(max_slots) * (2u * d->hidden + 2u * q_dim + 2u * kv_dim + 2u * d->inter);
     const size_t rope_n = static_cast<size_t>(max_seq) * (d->hd / 2u);
-    bool alloc_ok = cudaMalloc(&d->kc, cache * sizeof(float)) == cudaSuccess &&
-                    cudaMalloc(&d->vc, cache * sizeof(float)) == cudaSuccess &&
-                    cudaMalloc(&d->rope, rope_n * sizeof(float2)) == cudaSuccess &&
+    const uint64_t scales = static_cast<uint64_t>(max_slots) * d->layers * max_seq * d->kv_heads;
+    bool alloc_ok = d->kv8 ? (cudaMalloc(&d->kq, cache) == cudaSuccess && cudaMalloc(&d->vq, cache) == cudaSuccess &&
+                              cudaMalloc(&d->ksc, scales * sizeof(float)) == cudaSuccess &&
+                              cudaMalloc(&d->vsc, scales * sizeof(float)) == cudaSuccess)
+                           : (cudaMalloc(&d->kc, cache * sizeof(float)) == cudaSuccess &&
+                              cudaMalloc(&d->vc, cache * sizeof(float)) == cudaSuccess);
+    alloc_ok = alloc_ok && cudaMalloc(&d->rope, rope_n * sizeof(float2)) == cudaSuccess &&
                     cudaMalloc(&d->part, std::max<uint64_t>(part_floats, 1) * sizeof(float)) == cudaSuccess &&
                     cudaMalloc(&d->counter, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t)) ==
                         cudaSuccess &&
                     cudaMalloc(&d->work, ws * sizeof(float)) == cudaSuccess;
     cudaError_t e = cudaSuccess;
     if (alloc_ok) {
-        e = cudaMemset(d->kc, 0, cache * sizeof(float));
-        if (e == cudaSuccess) e = cudaMemset(d->vc, 0, cache * sizeof(float));
+        if (d->kv8) {   // QuantizedKVCache::init zero-fills codes and scales (kv_cache_quant.h:31-50)
+            e = cudaMemset(d->kq, 0, cache);
+            if (e == cudaSuccess) e = cudaMemset(d->vq, 0, cache);
+            if (e == cudaSuccess) e = cudaMemset(d->ksc, 0, scales * sizeof(float));
+            if (e == cudaSuccess) e = cudaMemset(d->vsc, 0, scales * sizeof(float));
+        } else {
+            e = cudaMemset(d->kc, 0, cache * sizeof(float));
+            if (e == cudaSuccess) e = cudaMemset(d->vc, 0, cache * sizeof(float));
+        }
         if (e == cudaSuccess)
             e = cudaMemset(d->counter, 0, static_cast<size_t>(max_slots) * d->kv_heads * sizeof(uint32_t));
         const uint32_t per = (d->G * (d->hd / 4u) + kAttnThreads - 1u) / kAttnThreads;   // quads per thread
-        d->attn_kernel = per <= 1u ? dec_attention_kernel<1> : per <= 2u ? dec_attention_kernel<2>
-                                                                         : dec_attention_kernel<4>;
+        if (d->kv8)
+            d->attn_kernel = per <= 1u ? dec_attention_kernel<1, true> : per <= 2u ? dec_attention_kernel<2, true>
+                                                                                   : dec_attention_kernel<4, true>;
+        else
+            d->attn_kernel = per <= 1u ? dec_attention_kernel<1, false> : per <= 2u ? dec_attention_kernel<2, false>
+                                                                                    : dec_attention_kernel<4, false>;
         if (e == cudaSuccess) e = cudaFuncSetAttribute(d->attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        static_cast<int>(smem_max));
         if (e == cudaSuccess) {
@@ -644,7 +826,8 @@ int qraf_cuda_decoder_open(const char* path, uint32_t max_slots, uint32_t max_se
     if (!alloc_ok) {
         cudaGetLastError();
         return fail_close(QRAF_ERR_NOMEM, "the KV caches and work buffers (" +
-                                              std::to_string(2 * cache * 4 + ws * 4 + part_floats * 4) +
+                                              std::to_string((d->kv8 ? 2 * cache + 8 * scales : 8 * cache) + ws * 4 +
+                                                             part_floats * 4) +
                                               " bytes) could not be allocated");
     }
     if (e != cudaSuccess) return fail_close(QRAF_ERR_CUDA, std::string("decoder set-up: ") + cudaGetErrorString(e));
@@ -765,6 +948,34 @@ int tc_step(qraf_decoder* d, uint32_t M, const DeviceInfo* dev, AttnParams ap, c
 
 extern "C" {
 
+int qraf_cuda_decoder_kv_read(qraf_decoder_t d, uint32_t slot, uint32_t layer, uint32_t pos, void* k_out, void* v_out,
+                              float* k_scales, float* v_scales) {
+    if (!d) return fail(QRAF_ERR_INVALID, "decoder is NULL");
+    if (slot >= d->max_slots || layer >= d->layers || pos >= d->max_seq)
+        return fail(QRAF_ERR_INVALID, "slot %u, layer %u or position %u out of range", slot, layer, pos);
+    if (!k_out || !v_out || (d->kv8 && (!k_scales || !v_scales)))
+        return fail(QRAF_ERR_INVALID, "an output pointer is NULL");
+    const uint32_t kv_dim = d->kv_heads * d->hd;
+    const size_t row = ((static_cast<size_t>(slot) * d->layers + layer) * d->max_seq + pos) * kv_dim;
+    const size_t srow = ((static_cast<size_t>(slot) * d->layers + layer) * d->max_seq + pos) * d->kv_heads;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    cudaError_t e;
+    if (d->kv8) {
+        e = cudaMemcpy(k_out, d->kq + row, kv_dim, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(v_out, d->vq + row, kv_dim, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(k_scales, d->ksc + srow, d->kv_heads * sizeof(float), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(v_scales, d->vsc + srow, d->kv_heads * sizeof(float), cudaMemcpyDeviceToHost);
+    } else {
+        e = cudaMemcpy(k_out, d->kc + row, kv_dim * sizeof(float), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(v_out, d->vc + row, kv_dim * sizeof(float), cudaMemcpyDeviceToHost);
+    }
+    cudaSetDevice(cur);
+    if (e != cudaSuccess) return fail(QRAF_ERR_CUDA, "reading the KV cache: %s", cudaGetErrorString(e));
+    return QRAF_OK;
+}
+
 int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_dev, const int32_t* pos_dev,
                            const int32_t* slots_dev, float* logits_dev, int mode, void* stream) {
     if (!d) return fail(QRAF_ERR_INVALID, "decoder is NULL");
@@ -793,6 +1004,10 @@ int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_d
     ap.slots = slots_dev;
     ap.kc = d->kc;
     ap.vc = d->vc;
+    ap.kq = d->kq;
+    ap.vq = d->vq;
+    ap.ksc = d->ksc;
+    ap.vsc = d->vsc;
     ap.out = d->att;
     ap.part = d->part;
     ap.counter = d->counter;
@@ -807,7 +1022,7 @@ int qraf_cuda_decoder_step(qraf_decoder_t d, uint32_t M, const int32_t* tokens_d
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, d->kv_heads, M);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_floats(d->G, d->hd) * sizeof(float);
+    cfg.dynamicSmemBytes = d->kv8 ? attn_smem_bytes8(d->G, d->hd) : attn_smem_floats(d->G, d->hd) * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

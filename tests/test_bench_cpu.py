@@ -72,8 +72,12 @@ def test_reference_arm_prints_the_contract_line():
 
 
 def test_decode_workload_names_and_bytes():
-    assert bench.parse_decode_workload("qwen3b_decode") == ("qwen3b", 1, 512)
-    assert bench.parse_decode_workload("qwen3b_decode_m8_c1024") == ("qwen3b", 8, 1024)
+    assert bench.parse_decode_workload("qwen3b_decode") == ("qwen3b", 1, 512, False)
+    assert bench.parse_decode_workload("qwen3b_decode_m8_c1024") == ("qwen3b", 8, 1024, False)
+    assert bench.parse_decode_workload("qwen3b_decode_c4096_kv8") == ("qwen3b", 1, 4096, True)
+    total8, _ = bench.decode_bytes_per_step("qwen3b", 1, 512, kv8=True)
+    # 513 positions read + 1 written per layer: 2 x 4 x 256 bytes each in f32, 2 x (256 + 2 x 4) in int8
+    assert total8 == bench.decode_bytes_per_step("qwen3b", 1, 512)[0] - 514 * 36 * (2 * 4 * 256 - 2 * (256 + 2 * 4))
     assert bench.parse_decode_workload("qwen3b_token") is None
     total, weights = bench.decode_bytes_per_step("qwen3b", 1, 512)
     # 36 layers of Q8_0 projections (q, k, v, o, gate, up, down) + the 151936 x 2048 head

@@ -210,3 +210,53 @@ def test_tensor_core_route(tmp_path, cuda, oracle_lib, arch, dt, tied):
     dec.close()
     assert per_layer == 9
     assert qb.device_status() == qb.OK
+
+
+def test_int8_cache_holds_the_reference_quantizer_bytes(tmp_path, cuda, oracle_lib):
+    """QRAF_DECODER_KV_INT8: the codes and scales the step stores are the reference's
+    QuantizedKVCache::store of the row the f32 cache holds (layer 0, where both
+    decoders see the same inputs), at every position."""
+    path, vocab = _model(tmp_path, oracle_lib, "qwen2", qb.Q8_0, max_seq=64)
+    spec = dict(qraf_spec.tiny_decoder("qwen2", qb.Q8_0)["config"])
+    kvh, hd = spec["num_kv_heads"], spec["hidden_size"] // spec["num_heads"]
+    ref = oracle.Reference()
+    f32 = qb.Decoder(path, max_slots=1, max_seq=64)
+    i8 = qb.Decoder(path, max_slots=1, max_seq=64, kv_int8=True)
+    for p, t in enumerate([3, 9, 27, 81, 243, 217, 139, 1]):
+        for dec in (f32, i8):
+            dec.step(_i32([t], cuda), _i32([p], cuda), _i32([0], cuda), mode=qb.MODE_FAST)
+        k, v = f32.kv_read(0, 0, p, kvh, hd)
+        got = i8.kv_read(0, 0, p, kvh, hd)
+        want = ref.kv_quantize(k, v, kvh, hd)
+        for g, w, name in zip(got, want, ("k codes", "v codes", "k scales", "v scales")):
+            assert g.tobytes() == w.tobytes(), f"position {p}: {name} differ"
+    f32.close()
+    i8.close()
+    assert qb.device_status() == qb.OK
+
+
+@pytest.mark.parametrize("route", ["one slot", "tensor cores"])
+def test_int8_cache_decodes_close_to_the_reference(tmp_path, cuda, oracle_lib, route):
+    """With the int8 cache the logits stay close to the reference's f32-cache
+    forward (the codes carry 1/254 of each row's range): every position's logits
+    within 2e-2 of the largest and a cosine above 0.9999 (measured on B200: 6.8e-3, 0.99998); one slot over 150
+    positions (split attention), and three slots on the tensor-core route."""
+    path, vocab = _model(tmp_path, oracle_lib, "qwen2", qb.Q8_0, heads=8, kv_heads=2, max_seq=160)
+    rng = np.random.default_rng(31)
+    n_seq, n = (1, 150) if route == "one slot" else (3, 40)
+    seqs = [[int(t) for t in rng.integers(0, vocab, n)] for _ in range(n_seq)]
+    want = _reference_runs(path, vocab, seqs)
+    dec = qb.Decoder(path, max_slots=n_seq, max_seq=160, kv_int8=True)
+    worst, low_cos = 0.0, 1.0
+    for p in range(n):
+        got = dec.step(_i32([s[p] for s in seqs], cuda), _i32([p] * n_seq, cuda), _i32(list(range(n_seq)), cuda),
+                       mode=qb.MODE_AUTO).cpu().numpy()
+        for i in range(n_seq):
+            w = np.asarray(want[i][p], np.float64)
+            g = got[i].astype(np.float64)
+            worst = max(worst, float(np.abs(g - w).max() / np.abs(w).max()))
+            low_cos = min(low_cos, float(g @ w / np.linalg.norm(g) / np.linalg.norm(w)))
+    dec.close()
+    print(f"int8 cache ({route}): worst |d| / max |logit| {worst:.2e}, lowest cosine {low_cos:.6f}")
+    assert worst < 2e-2 and low_cos > 0.9999
+    assert qb.device_status() == qb.OK

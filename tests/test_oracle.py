@@ -166,3 +166,41 @@ def test_rms_norm_matches_the_reference(oracle_lib):
         x = (rng.normal(size=size) * scale).astype(np.float32)
         w = rng.normal(1.0, 0.1, size=size).astype(np.float32)
         assert oracle_lib.rms_norm(x, w, eps).tobytes() == ref.rms_norm(x, w, eps).tobytes(), (size, eps)
+
+
+def test_kv_int8_quantizer_is_the_reference():
+    """The reference's QuantizedKVCache::store (include/nn/kv_cache_quant.h:61-94),
+    restated: per head scale = max |x| / 127 (a NaN is never the max), codes
+    clamp(round-half-away(x * (1 / scale)), -127, 127), 0 for an all-zero head."""
+    import oracle
+
+    if not oracle.reference_available():
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.default_rng(21)
+    kv_heads, hd = 4, 32
+    k = rng.normal(0, 2, kv_heads * hd).astype(np.float32)
+    v = rng.normal(0, 0.5, kv_heads * hd).astype(np.float32)
+    k[hd:2 * hd] = 0.0                    # an all-zero head
+    v[5] = np.nan                         # NaN is skipped by the max and clamps to 127
+    k[3 * hd] = np.float32(0.5) * np.float32(np.abs(k[3 * hd + 1:4 * hd]).max())   # ordinary value
+    kq, vq, ks, vs = oracle.Reference().kv_quantize(k, v, kv_heads, hd)
+
+    def restate(x):
+        codes, scales = np.empty(x.size, np.int8), np.empty(kv_heads, np.float32)
+        for h in range(kv_heads):
+            seg = x[h * hd:(h + 1) * hd]
+            finite = seg[~np.isnan(seg)]
+            mx = np.float32(np.abs(finite).max()) if finite.size else np.float32(0)
+            sc = np.float32(mx / np.float32(127.0))
+            inv = np.float32(np.float32(1.0) / sc) if sc > 0 else np.float32(0)
+            prod = (seg * inv).astype(np.float32)
+            r = np.where(np.isnan(prod), 127.0, np.sign(prod) * np.floor(np.abs(prod).astype(np.float64) + 0.5))
+            codes[h * hd:(h + 1) * hd] = np.clip(r, -127, 127).astype(np.int8)
+            scales[h] = sc
+        return codes, scales
+
+    want_kq, want_ks = restate(k)
+    want_vq, want_vs = restate(v)
+    assert np.array_equal(kq, want_kq) and np.array_equal(ks, want_ks)
+    assert np.array_equal(vq, want_vq) and np.array_equal(vs, want_vs)
+    assert (kq[hd:2 * hd] == 0).all() and ks[1] == 0 and vq[5] == 127
