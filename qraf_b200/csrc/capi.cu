@@ -75,9 +75,15 @@ inline cudaError_t counted(cudaError_t e) {
 
 constexpr int kSmemReserve = 1024;
 
+// Let `kernel` take up to `bytes` of shared memory per CTA, static included
+// (the dynamic limit is what the static arrays leave).
 template <typename K>
 cudaError_t allow_smem(K kernel, int bytes) {
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaFuncAttributes a;
+    const cudaError_t e = cudaFuncGetAttributes(&a, kernel);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                bytes - static_cast<int>(a.sharedSizeBytes));
 }
 
 int ensure_device(int* dev_out, DeviceInfo** info_out) {
