@@ -571,9 +571,7 @@ def run_shard(args, dt, n, k, m):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     qb.init(local)
-    if args.mode not in ("fast", "exact"):
-        raise SystemExit("sharded projections run FAST or EXACT")
-    mode = qb.MODE_EXACT if args.mode == "exact" else qb.MODE_FAST
+    mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
     fused = world > 1 and args.allgather == "fused"
     r0, r1 = n * rank // world, n * (rank + 1) // world
     rows = r1 - r0
@@ -819,8 +817,6 @@ def run_token(args, model, m):
     qb.init(local)
     mode = {"exact": qb.MODE_EXACT, "fast": qb.MODE_FAST, "tc": qb.MODE_TC, "auto": qb.MODE_AUTO}[args.mode]
     fused = world > 1 and args.allgather == "fused"
-    if fused and mode in (qb.MODE_TC, qb.MODE_AUTO):
-        raise SystemExit("the fused row-sharded path runs EXACT or FAST; use --allgather nccl for the tensor cores")
 
     # Seeded weights with the reference's idiom: for every projection shape one
     # std::mt19937(42) draw of N(0, 0.02) over the whole [N][K] tensor (the same

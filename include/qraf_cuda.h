@@ -262,10 +262,15 @@ int qraf_cuda_comm_destroy(qraf_comm_t comm);
  * peer's receive array over NVLink; before it ends it copies the other ranks'
  * rows into this rank's buffer, so Y[m][n] for all n is in *y_out (this rank's
  * buffer for this call, valid for the next QRAF_COMM_BUFFERS - 1 calls) when
- * the launch completes.  Same arguments as qraf_cuda_matvec_q, modes EXACT
- * and FAST (AUTO runs FAST); needs block size 32, K a multiple of 32 and
- * 16-byte-aligned rows and pointers.  Any M: the vectors go in groups of one
- * launch each (FAST: two), every launch one numbered call of the protocol.
+ * the launch completes.  Same arguments as qraf_cuda_matvec_q, modes EXACT,
+ * FAST and TC; AUTO runs TC from three vectors (where the tensor-core path
+ * applies) and FAST below.  EXACT and FAST need block size 32, K a multiple of
+ * 32 and 16-byte-aligned rows and pointers; TC what qraf_cuda_matvec_q's TC mode
+ * needs.  Any M: the vectors go in groups of one launch each (FAST: two; TC: up
+ * to 64, the tile storing into the peers from its epilogue), every launch one
+ * numbered call of the protocol.  EXACT and FAST give exactly the unsharded
+ * result's bits; TC gives on each rank the bits of its shard's own TC call
+ * (the tile's split of K among CTAs depends on the shard's row count).
  * The calls of one comm go to one stream, in the same order on every rank.  Calls are numbered on the device, so a sequence of
  * calls may be captured in a CUDA graph and replayed; capture a multiple of
  * QRAF_COMM_BUFFERS calls per comm so that replays keep the buffer rotation

@@ -644,8 +644,22 @@ struct TcFusion {
 
 // Y = W X on the tensor cores, in groups of up to 64 vectors, with scratch at
 // `scratch` (pl.bytes for the largest group; nullptr: the stream's own area).
+// A row-sharded tensor-core call: this rank's rows [row_off, row_off + rows) of a
+// y with y_ld rows, gathered through the comm's receive arrays (TcParams).  Every
+// group of up to kTcMaxVectors vectors is one numbered call of the comm.
+struct TcShard {
+    uint32_t world = 0, rank = 0, y_ld = 0, row_off = 0, v_off = 0;
+    float* y_full = nullptr;
+    unsigned long long* local_ll = nullptr;
+    unsigned long long* peer_ll[kMaxWorld] = {};
+    uint64_t ll_cap = 0;
+    uint32_t* cta_counter = nullptr;
+    uint32_t* seq = nullptr;
+};
+
 int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool overlap, cudaStream_t st,
-              const DeviceInfo& dev, uint8_t* scratch, size_t scratch_cap, const TcFusion* fz = nullptr) {
+              const DeviceInfo& dev, uint8_t* scratch, size_t scratch_cap, const TcFusion* fz = nullptr,
+              const TcShard* sh = nullptr) {
     TcPlan pl;
     const uint32_t first = std::min(M, kTcMaxVectors);
     if (!plan_tc(w, first, dev, &pl)) return fail(QRAF_ERR_UNSUPPORTED, "no tensor-core plan for this weight");
@@ -682,6 +696,20 @@ int matmul_tc(const qraf_weight_t& w, const float* x, float* y, uint32_t M, bool
             for (int i = 0; i <= kMaxSeg; ++i) p.seg_row0[i] = fz->seg_row0[i];
             in = fz->in;
             if (in.up) in.up += static_cast<size_t>(m0) * w.cols;
+        }
+        if (sh) {
+            TcParams& p = one.p;
+            p.world = sh->world;
+            p.rank = sh->rank;
+            p.y_ld = sh->y_ld;
+            p.row_off = sh->row_off;
+            p.v_off = sh->v_off + m0;
+            p.y_full = sh->y_full;
+            p.local_ll = sh->local_ll;
+            p.ll_cap = sh->ll_cap;
+            for (int r = 0; r < kMaxWorld; ++r) p.peer_ll[r] = sh->peer_ll[r];
+            p.cta_counter = sh->cta_counter;
+            p.seq = sh->seq;
         }
         const bool pdl_prep = overlap || m0 > 0;
         const cudaError_t e = w.dtype == QRAF_DTYPE_Q8_0
@@ -1681,9 +1709,38 @@ int qraf_cuda_matvec_q_sharded(qraf_comm_t c, const qraf_weight_t* shard, uint32
                     static_cast<unsigned long long>(M) * total_rows, static_cast<unsigned long long>(c->cap));
     const bool overlap = (mode_in & QRAF_MODE_FLAG_OVERLAP) != 0;
     int mode = mode_in & 0xFF;
-    if (mode == QRAF_MODE_AUTO) mode = QRAF_MODE_FAST;
-    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST) return fail(QRAF_ERR_UNSUPPORTED, "mode %d", mode_in);
+    // AUTO as for an unsharded call: the tensor-core tile from three vectors
+    if (mode == QRAF_MODE_AUTO) mode = (M >= kAutoTcMinVectors && tc_eligible(*shard)) ? QRAF_MODE_TC : QRAF_MODE_FAST;
+    if (mode != QRAF_MODE_EXACT && mode != QRAF_MODE_FAST && mode != QRAF_MODE_TC)
+        return fail(QRAF_ERR_UNSUPPORTED, "mode %d", mode_in);
     const bool exact = mode == QRAF_MODE_EXACT;
+    if (mode == QRAF_MODE_TC) {
+        // the tile with the all-gather in its store: one launch pair (one numbered call)
+        // per group of up to kTcMaxVectors vectors, each group at its vector offset
+        if (!tc_eligible(*shard))
+            return fail(QRAF_ERR_UNSUPPORTED, "the tensor-core path needs block size 32, K a multiple of %u and "
+                                              "16-byte-aligned weights", shard->dtype == QRAF_DTYPE_Q4_0 ? 256 : 128);
+        DeviceInfo* dev = nullptr;
+        rc = ensure_device(nullptr, &dev);
+        if (rc) return rc;
+        const int buf = static_cast<int>(++c->calls % QRAF_COMM_BUFFERS);
+        TcShard sh;
+        sh.world = static_cast<uint32_t>(c->world);
+        sh.rank = static_cast<uint32_t>(c->rank);
+        sh.y_ld = total_rows;
+        sh.row_off = row_offset;
+        sh.y_full = c->y[buf];
+        sh.local_ll = c->ll;
+        sh.ll_cap = c->cap;
+        for (int r = 0; r < c->world; ++r) sh.peer_ll[r] = c->peer_ll[r];
+        sh.cta_counter = c->counter;
+        sh.seq = c->counter + 32;
+        rc = matmul_tc(*shard, x_dev, nullptr, M, overlap, static_cast<cudaStream_t>(stream), *dev, nullptr, 0, nullptr,
+                       &sh);
+        if (rc) return rc;
+        *y_out = c->y[buf];
+        return QRAF_OK;
+    }
     if (!rows_eligible(*shard, x_dev))
         return fail(QRAF_ERR_UNSUPPORTED, "the sharded path needs block size 32, K a multiple of 32, and 16-byte-aligned "
                                           "rows and pointers");

@@ -81,10 +81,27 @@ struct TcParams {
     float* seg_y[kMaxSeg];
     const float* seg_b[kMaxSeg];
     uint32_t seg_row0[kMaxSeg + 1];
+    // Row-sharded launch (world > 0, no output fusions): as the row kernel's
+    // (RowParams), rows [row_off, row_off + N) of a y with y_ld rows; every element
+    // goes to this rank's y_full and, as a (call, value) word, to every peer's
+    // receive array, and the CTAs then copy the other ranks' rows in
+    // (sharded_gather).  call = *seq + 1, read after the dependency wait.
+    float* y_full;
+    uint32_t v_off;
+    unsigned long long* peer_ll[kMaxWorld];
+    unsigned long long* local_ll;
+    uint64_t ll_cap;
+    uint32_t* cta_counter;
+    uint32_t* seq;
+    uint32_t world, rank, y_ld, row_off;
 };
 
 // One output element of row r (of the virtual weight) and vector m of this launch.
-__device__ __forceinline__ void tc_store(const TcParams& p, uint32_t r, uint32_t m, float v) {
+__device__ __forceinline__ void tc_store(const TcParams& p, uint32_t r, uint32_t m, float v, uint32_t call) {
+    if (p.world) {
+        sharded_store(p, call, m, r, v);
+        return;
+    }
     float* dst;
     const float* b;
     if (p.nseg <= 1) {
@@ -617,6 +634,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
 #pragma unroll
         for (uint32_t m = 0; m < HV; ++m) acc[m] = 0.0f;
         bool waited = false, ok = true;
+        uint32_t call = 0;   // the sharded call number (world > 0), read after the dependency wait
         uint32_t ncomb = 0;
         Ring rd(p.nd), rs(p.ns), rf(p.nf), rm(R);
         uint32_t k = k0, tile = tile0;
@@ -742,8 +760,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             }
             if (!seg_last) continue;
             // ── the segment of tile t_now ends here: write it, or hand it to the combiner
-            if (p.pdl && !waited) {
-                pdl_wait();
+            if (!waited) {
+                if (p.pdl) pdl_wait();
+                if (p.world) call = *reinterpret_cast<volatile const uint32_t*>(p.seq) + 1u;
                 waited = true;
             }
             const uint32_t t0u = t_now * p.upt, t1u = t0u + p.upt;
@@ -753,7 +772,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
                 if (row < rows) {
 #pragma unroll
                     for (uint32_t v = 0; v < HV; ++v)
-                        if (m0 + v < p.M) tc_store(p, grow, m0 + v, acc[v]);
+                        if (m0 + v < p.M) tc_store(p, grow, m0 + v, acc[v], call);
                 }
                 continue;
             }
@@ -794,7 +813,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
             if (row < rows) {
 #pragma unroll
                 for (uint32_t v = 0; v < HV; ++v)
-                    if (m0 + v < p.M) tc_store(p, grow, m0 + v, sum[v]);
+                    if (m0 + v < p.M) tc_store(p, grow, m0 + v, sum[v], call);
             }
         }
         tc_fence_before();
@@ -803,6 +822,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     if (warp == kTcWarpMma) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+    }
+    if (p.world) {   // every role is done: the other ranks' rows of this call, by all threads
+        uint32_t* s_call = bcast + 1;
+        if (threadIdx.x == 0) {
+            if (p.pdl) pdl_wait();   // returns at once where the epilogue waited already
+            *s_call = *reinterpret_cast<volatile const uint32_t*>(p.seq) + 1u;
+        }
+        __syncthreads();
+        sharded_gather(p, *s_call);
     }
 }
 

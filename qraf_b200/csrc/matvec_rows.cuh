@@ -149,6 +149,21 @@ __device__ __forceinline__ const uint8_t* row_src(const RowParams& p, uint32_t r
     return p.seg_w[i] + static_cast<size_t>(row - p.seg_row0[i]) * p.row_bytes;
 }
 
+// Row-sharded store of output element (vector v of the launch, local row `row`)
+// into this rank's y and, as a (call, value) word, every peer's receive array.
+// P: the launch's parameters (RowParams or the tensor-core tile's TcParams, which
+// carry the same sharding fields).
+template <class P>
+__device__ __forceinline__ void sharded_store(const P& p, uint32_t call, uint32_t v, uint32_t row, float t) {
+    const size_t idx = static_cast<size_t>(v + p.v_off) * p.y_ld + p.row_off + row;
+    p.y_full[idx] = t;
+    const unsigned long long word = (static_cast<unsigned long long>(call) << 32) | __float_as_uint(t);
+    const size_t off = static_cast<size_t>(call & 1u) * p.ll_cap + idx;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+        if (r < static_cast<int>(p.world) && r != static_cast<int>(p.rank)) st_relaxed_sys_u64(p.peer_ll[r] + off, word);
+}
+
 // One output element: into y (or its weight's y), or (row-sharded) into this
 // rank's y and every peer's receive array.
 __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uint32_t v, uint32_t row, float t) {
@@ -166,13 +181,7 @@ __device__ __forceinline__ void store_out(const RowParams& p, uint32_t call, uin
         }
         return;
     }
-    const size_t idx = static_cast<size_t>(v + p.v_off) * p.y_ld + p.row_off + row;
-    p.y_full[idx] = t;
-    const unsigned long long word = (static_cast<unsigned long long>(call) << 32) | __float_as_uint(t);
-    const size_t off = static_cast<size_t>(call & 1u) * p.ll_cap + idx;
-#pragma unroll
-    for (int r = 0; r < kMaxWorld; ++r)
-        if (r < static_cast<int>(p.world) && r != static_cast<int>(p.rank)) st_relaxed_sys_u64(p.peer_ll[r] + off, word);
+    sharded_store(p, call, v, row, t);
 }
 
 // SwiGLU output of the pair (gate, up) = virtual rows (2i, 2i + 1).
@@ -199,8 +208,9 @@ __global__ void __launch_bounds__(256) swiglu_apply_kernel(float* __restrict__ h
 // half of the receive array before this rank has finished reading it: it
 // writes call c + 2 only after finishing call c + 1, which needs this rank's
 // rows of c + 1, which this rank computes only after this launch (call c)
-// has completed.
-__device__ __forceinline__ void sharded_gather(const RowParams& p, uint32_t call) {
+// has completed.  P as for sharded_store; p.M vectors, p.N local rows.
+template <class P>
+__device__ __forceinline__ void sharded_gather(const P& p, uint32_t call) {
     // this launch's vectors [v_off, v_off + M) of the host call
     const size_t base = static_cast<size_t>(p.v_off) * p.y_ld;
     const size_t total = static_cast<size_t>(p.M) * p.y_ld;

@@ -1,6 +1,8 @@
 """Row-sharded matvec with the all-gather fused into the kernel (peer stores over
-NVLink + bounded flag waits).  Sharding never changes a row's arithmetic, so the
-gathered y must be bit-identical to the unsharded one, in both modes."""
+NVLink + bounded flag waits).  In EXACT and FAST sharding never changes a row's
+arithmetic, so the gathered y must be bit-identical to the unsharded one; in TC
+each rank's rows are its shard's own TC bits (the tile splits K among CTAs by the
+shard's size), gathered unchanged."""
 from __future__ import annotations
 
 import os
@@ -39,6 +41,28 @@ def test_single_rank_group_equals_plain_matvec(cuda, dt, mode):
         for _ in range(3):   # the output buffer alternates call by call
             got = comm.matvec_q(w, n, 0, x, mode=mode).cpu().numpy()
             assert got.tobytes() == want.tobytes(), f"M={m}"
+    assert qb.device_status() == qb.OK
+    comm.destroy()
+
+
+@pytest.mark.parametrize("dt,n,k", [(qb.Q8_0, 1024, 2048), (qb.Q4_0, 2304, 4096)])
+def test_single_rank_group_on_the_tensor_cores(cuda, dt, n, k):
+    """TC (and AUTO from three vectors) through a one-rank group: the tile's
+    sharded store, call numbering and gather give the plain TC call's bits, for one
+    group of vectors and for several (70 vectors: groups of 64 and 6, two numbered
+    calls), call after call."""
+    import torch
+
+    q = _weight(torch, cuda, dt, n, k)
+    w = qb.Weight.from_device(q, dt, n, k)
+    comm = qb.Comm(1, 0, 70 * n)
+    qb.Comm.open_local([comm])
+    for m in (3, 16, 70):
+        x = torch.from_numpy(qb.fill_normal(50 + m, 0.0, 1.0, m * k)).to(cuda).reshape(m, k)
+        want = qb.matvec_q(w, x, mode=qb.MODE_TC).cpu().numpy()
+        for md in (qb.MODE_TC, qb.MODE_AUTO, qb.MODE_TC):
+            got = comm.matvec_q(w, n, 0, x, mode=md).cpu().numpy()
+            assert got.tobytes() == want.tobytes(), f"M={m} mode {md}"
     assert qb.device_status() == qb.OK
     comm.destroy()
 
@@ -88,6 +112,31 @@ def test_missing_peer_times_out_and_is_reported(cuda):
     c1.destroy()
 
 
+def test_missing_peer_times_out_on_the_tensor_cores(cuda):
+    """The tile's gather, as the row kernel's: rank 0 of a 2-rank group runs alone,
+    its wait for rank 1's rows ends after the time limit with QRAF_ERR_TIMEOUT, its
+    own rows are in y and the GPU stays usable.  One launch pair; nothing else
+    waits on it."""
+    import torch
+
+    n, k, m = 512, 2048, 16
+    q = _weight(torch, cuda, qb.Q8_0, n, k)
+    full = qb.Weight.from_device(q, qb.Q8_0, n, k)
+    c0, c1 = qb.Comm(2, 0, m * n), qb.Comm(2, 1, m * n)
+    qb.Comm.open_local([c0, c1])
+    x = torch.from_numpy(qb.fill_normal(6, 0.0, 1.0, m * k)).to(cuda).reshape(m, k)
+    shard0 = full.shard(2, 0)
+    y0 = c0.matvec_q(shard0, n, 0, x, mode=qb.MODE_TC)
+    assert qb.device_status(clear=True) == qb.ERR_TIMEOUT
+    want = qb.matvec_q(shard0, x, mode=qb.MODE_TC).cpu().numpy()
+    assert y0.cpu().numpy()[:, :n // 2].tobytes() == want.tobytes()   # its own rows arrived anyway
+    again = qb.matvec_q(shard0, x, mode=qb.MODE_TC).cpu().numpy()     # the context is still usable
+    assert again.tobytes() == want.tobytes()
+    assert qb.device_status() == qb.OK
+    c0.destroy()
+    c1.destroy()
+
+
 @pytest.mark.parametrize("dt,n,k", [(qb.Q4_0, 8192, 4096), (qb.Q8_0, 2048, 11008)])
 def test_single_process_multi_gpu_group(cuda, dt, n, k):
     import torch
@@ -125,9 +174,33 @@ def test_single_process_multi_gpu_group(cuda, dt, n, k):
             torch.cuda.set_device(r)
             assert outs[r].cpu().numpy().tobytes() == want[md].tobytes(), f"rank {r} mode {md}"
             assert qb.device_status() == qb.OK
+    # TC: every rank's y holds each shard's own TC bits (16 vectors, one group)
+    mt = 16
+    xt0 = torch.from_numpy(qb.fill_normal(47, 0.0, 1.0, mt * k)).reshape(mt, k)
+    want_tc, xts = [], []
+    for r in range(world):
+        torch.cuda.set_device(r)
+        xts.append(xt0.to(torch.device("cuda", r)))
+        want_tc.append(qb.matvec_q(shards[r], xts[r], mode=qb.MODE_TC).cpu().numpy())
+    want_tc = np.concatenate(want_tc, axis=1)
+    tcomms = []
+    for r in range(world):
+        torch.cuda.set_device(r)
+        tcomms.append(qb.Comm(world, r, mt * n))
+    qb.Comm.open_local(tcomms)
+    for md in (qb.MODE_TC, qb.MODE_AUTO):
+        outs = []
+        for r in range(world):
+            torch.cuda.set_device(r)
+            outs.append(tcomms[r].matvec_q(shards[r], n, offs[r], xts[r], mode=md))
+        for r in range(world):
+            torch.cuda.set_device(r)
+            assert outs[r].cpu().numpy().tobytes() == want_tc.tobytes(), f"rank {r} mode {md}"
+            assert qb.device_status() == qb.OK
     for r in range(world):
         torch.cuda.set_device(r)
         comms[r].destroy()
+        tcomms[r].destroy()
     torch.cuda.set_device(0)
 
 
