@@ -87,6 +87,18 @@ def launches_per_call(n_rows, k, sm_count):
     return 2 if k // 32 >= 256 and -(-n_rows // sm_count) <= 96 else 1
 
 
+def shard_call_kernels(mode, n_rows, k, m, sm_count):
+    """(kernel timed, kernels launched) for one call of a row-sharded or plain
+    projection of m vectors: the tensor-core tile in TC, and in AUTO from three
+    vectors (a prep and a tile launch per group of up to 64 vectors); else the row
+    kernel, FAST in launches of two vectors (each with its limb prep where
+    launches_per_call says so), EXACT in one launch."""
+    if mode == "tc" or (mode == "auto" and m >= 3):
+        return "qmm_tc_kernel", 2 * -(-m // 64)
+    groups = 1 if mode == "exact" else -(-m // 2)
+    return "qmv_rows_kernel", groups * launches_per_call(n_rows, k, sm_count)
+
+
 def alg_bytes(dt, n, k, m):
     return n * (k // 32) * BLOCK_BYTES[dt] + 4 * m * k + 4 * m * n
 
@@ -722,11 +734,11 @@ def run_shard(args, dt, n, k, m):
             "e2e": {"value": e2e_steps * R * full / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": m * k * 4,
                     "d2h_bytes_per_step": m * n * 4, "steps": e2e_steps,
                     "path": "H2D x from pinned memory, the step's graph, D2H of the last call's y, stream sync"},
-            "gpu_launches": calls * launches_per_call(rows, k, props.multi_processor_count),
+            "gpu_launches": calls * shard_call_kernels(args.mode, rows, k, m, props.multi_processor_count)[1],
             "roofline": {"bound": "hbm", "achieved": shard / (call_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": shard / (call_ms / 1e3) / 1e9 / peak, "traffic": None, "peak_source": peak_src,
                          "what": "per GPU: shard bytes of one call / the call's duration alone",
-                         "kernel": "qmv_rows_kernel"},
+                         "kernel": shard_call_kernels(args.mode, rows, k, m, props.multi_processor_count)[0]},
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "device_status": status,

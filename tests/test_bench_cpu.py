@@ -108,3 +108,18 @@ def test_decode_file_runs_in_the_reference_transformer(tmp_path, monkeypatch):
     assert n == os.path.getsize(path)
     cpu = bench.decode_cpu_baseline("tiny", 8, 0.05, path)
     assert cpu["kind"] == "reference" and cpu["value"] > 0
+
+
+def test_sharded_call_kernel_count():
+    """A sharded call's kernels: the tile pair per 64 vectors in TC (AUTO from three
+    vectors), the row kernel in pairs of vectors in FAST (with the limb prep for
+    long K and few rows per CTA), one launch in EXACT."""
+    import bench
+
+    assert bench.shard_call_kernels("auto", 14336, 8192, 16, 148) == ("qmm_tc_kernel", 2)
+    assert bench.shard_call_kernels("tc", 14336, 8192, 70, 148) == ("qmm_tc_kernel", 4)
+    assert bench.shard_call_kernels("auto", 14336, 8192, 2, 148) == ("qmv_rows_kernel", 1)   # 97 rows per CTA
+    assert bench.shard_call_kernels("fast", 14336, 8192, 5, 148) == ("qmv_rows_kernel", 3)
+    assert bench.shard_call_kernels("fast", 7168, 8192, 5, 148) == ("qmv_rows_kernel", 6)    # 49 rows: limb prep
+    assert bench.shard_call_kernels("fast", 3584, 28672, 1, 148) == ("qmv_rows_kernel", 2)
+    assert bench.shard_call_kernels("exact", 14336, 8192, 4, 148) == ("qmv_rows_kernel", 1)
