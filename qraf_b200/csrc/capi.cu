@@ -305,6 +305,15 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     for (int i = 0; i < kMaxSeg; ++i) p.seg_b[i] = nullptr;
     p.pdl = 0;
     p.xrec = nullptr;
+    // Ring stages issued before the dependency wait: a few, not the whole first lap.
+    // The activation loads and limb records that follow the wait are slowed by the
+    // copies in flight (the issuing lanes are held while theirs are served), so the
+    // rest of the lap goes out after the activations are staged.  Measured on B200
+    // (pipelined launches, against the whole lap early): Q4 4096 x 4096 5.89 -> 5.54
+    // us, Q8 4096 x 4096 6.65 -> 6.02, Q8 11008 x 2048 8.99 -> 7.53, Q8 2048 x 11008
+    // 11.43 -> 9.50, Q4 28672 x 8192 37.95 -> 35.53; 2, 8 and 12 stages did worse on
+    // most shapes, and stages above ~10 KB want 4.
+    p.early = std::min<uint32_t>(nst, slot_stride <= 10240u ? 6u : 4u);
     p.nseg = 0;
     for (int i = 0; i < kMaxSeg; ++i) {
         p.seg_w[i] = nullptr;

@@ -77,6 +77,8 @@ struct RowParams {
     uint32_t row_unit;       // 1, or 2 for paired (SwiGLU) rows
     uint32_t pdl;            // 1: programmatic dependent launch protocol
     const uint8_t* xrec;     // FAST: limb records built by limb_prep_kernel ([M][nblk] x kLimbRec), or null
+    uint32_t early;          // ring stages issued before the dependency wait; the rest of the first lap after
+                             // the activations are staged (their loads queue behind the SM's copies in flight)
     // Several weights of one input in one launch (nseg >= 2): virtual rows
     // [seg_row0[i], seg_row0[i+1]) are the rows of weight i (seg_w[i]), whose
     // outputs go to seg_y[i] ([M][rows of weight i]); same cols, dtype and
@@ -690,7 +692,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
         slot_stage[slot] = s;   // the slot's barrier is now in stage s's phase
     };
     if (lane == 0)
-        for (uint32_t s = warp; s < min(nst, nstages); s += kRowWarps) issue(s, s);
+        for (uint32_t s = warp; s < min(min(nst, nstages), p.early); s += kRowWarps) issue(s, s);
 
     // ── stage the activations (after the previous kernel finished) ──
     // L2-coherent loads (__ldcg): under programmatic dependent launch x may have
@@ -719,6 +721,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                                p.norm_eps, red);
     }
     __syncthreads();
+    if (lane == 0)   // the rest of the first lap (each warp issues its own stages before it waits on them)
+        for (uint32_t s = warp; s < min(nst, nstages); s += kRowWarps)
+            if (s >= p.early) issue(s, s);
 
     // this warp's stages s = warp, warp + 16, ...: ring slot s % nst and phase
     // parity (s / nst) & 1, advanced by subtraction (no division in the loop)

@@ -1,6 +1,8 @@
 """A CPU model of the batch-1 row kernel's slot ring (qraf_b200/csrc/matvec_rows.cuh,
 qmv_rows_kernel): stage s belongs to warp s % 16 and lives in slot s % nst; lane 0
-of each warp issues its first stages into their slots; a warp that finishes stage s
+of each warp issues its first stages into their slots (those below the launch's
+`early` count before the activations are staged, the rest after the CTA barrier that
+ends the staging); a warp that finishes stage s
 issues stage s + nst into the slot it just freed (bulk copies completing on the
 slot's mbarrier later, in any order), publishing the stage id in shared memory; a
 consumer waits for its own stage id, then for the slot's phase parity.
@@ -42,8 +44,12 @@ class Bar:
         return (self.completed & 1) != parity
 
 
-def run_model(nst, nstages, seed, stage_id_wait=True):
+def run_model(nst, nstages, seed, stage_id_wait=True, early=None):
+    """early: stages of the first lap issued before the CTA barrier that ends the
+    activation staging (the rest of the lap after it); None = the whole lap."""
     rng = random.Random(seed)
+    early = nst if early is None else early
+    arrived = [0]                   # warps at the staging barrier
     full = [Bar() for _ in range(nst)]
     slot_stage = [None] * nst
     content = [None] * nst          # the stage whose bytes the slot holds (set when the copy lands)
@@ -57,10 +63,18 @@ def run_model(nst, nstages, seed, stage_id_wait=True):
         slot_stage[slot] = s
 
     def warp_prog(w):
-        # lane 0 issues the warp's first stages (s < nst)
-        for s in range(w, min(nst, nstages), WARPS):
+        # lane 0 issues the warp's first stages below `early`, the CTA stages the
+        # activations (a barrier every warp reaches), then the rest of the lap
+        for s in range(w, min(nst, nstages, early), WARPS):
             issue(s, s)
             yield
+        arrived[0] += 1
+        while arrived[0] < WARPS:
+            yield
+        for s in range(w, min(nst, nstages), WARPS):
+            if s >= early:
+                issue(s, s)
+                yield
         slot, phase = w % nst, (w // nst) & 1
         for s in range(w, nstages, WARPS):
             if stage_id_wait:
@@ -102,9 +116,10 @@ def run_model(nst, nstages, seed, stage_id_wait=True):
 
 @pytest.mark.parametrize("nst", [1, 2, 3, 5, 8, 16, 17, 32])
 @pytest.mark.parametrize("nstages", [1, 7, 16, 40, 97])
-def test_slot_ring_is_safe_and_live(nst, nstages):
+@pytest.mark.parametrize("early", [0, 4, 6, None])
+def test_slot_ring_is_safe_and_live(nst, nstages, early):
     for seed in range(5):
-        run_model(nst, nstages, seed=seed * 31 + nst * 1000 + nstages)
+        run_model(nst, nstages, seed=seed * 31 + nst * 1000 + nstages, early=early)
 
 
 def test_model_catches_a_missing_stage_id_wait():
