@@ -73,12 +73,13 @@ def test_one_slot_matches_the_reference_forward(tmp_path, cuda, oracle_lib, arch
     assert qb.device_status() == qb.OK
 
 
-@pytest.mark.parametrize("max_seq,n", [(160, 150), (1024, 600)])
+@pytest.mark.parametrize("max_seq,n", [(160, 150), (1024, 600), (2200, 1100)])
 def test_long_sequence_splits_attention(tmp_path, cuda, oracle_lib, max_seq, n):
     """From position 32 on, a slot's attention runs over several chunks (one CTA
-    per 32 positions of max_seq, at most 16) whose partials the last CTA merges;
-    past 512 positions a chunk spans several 32-position tiles.  GQA with 4
-    query heads per KV head."""
+    per 32 positions of max_seq, at most 64) whose partials the last CTA merges;
+    with few CTAs per chunk count a chunk spans several 32-position tiles, and past
+    1024 positions more than 32 chunks meet in the merge (lanes take several
+    chunks each).  GQA with 4 query heads per KV head."""
     path, vocab = _model(tmp_path, oracle_lib, "qwen2", qb.Q8_0, heads=8, kv_heads=2, max_seq=max_seq)
     rng = np.random.default_rng(3)
     tokens = [int(t) for t in rng.integers(0, vocab, n)]
