@@ -83,8 +83,8 @@ def uses_tc1(mode_name, n, k, m, sm_count):
 
 def launches_per_call(n_rows, k, sm_count):
     """Kernels one FAST M <= 2 matvec launches: the activation-limb prep kernel runs
-    when a row has at least 256 blocks and a CTA gets at most 96 rows (capi.cu)."""
-    return 2 if k // 32 >= 256 and -(-n_rows // sm_count) <= 96 else 1
+    when a row has at least 320 blocks and a CTA gets at most 96 rows (capi.cu)."""
+    return 2 if k // 32 >= 320 and -(-n_rows // sm_count) <= 96 else 1
 
 
 def shard_call_kernels(mode, n_rows, k, m, sm_count):

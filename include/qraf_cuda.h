@@ -56,7 +56,7 @@ extern "C" {
                               batch-1 tensor-core kernel instead (int8 MMAs on the FAST
                               path's activation limbs). */
 /* Per-stream scratch.  QRAF_MODE_TC, and QRAF_MODE_FAST (also the sharded FAST
- * path) when a row has at least 256 blocks (K >= 8192) and a CTA gets at most 96
+ * path) when a row has at least 320 blocks (K >= 10240) and a CTA gets at most 96
  * rows (long-K projections, row shards), use scratch memory that the library
  * allocates per (device, stream) at the stream's first call that needs that much.
  * Make one call of each such shape on a stream before capturing the stream in a

@@ -377,14 +377,18 @@ int stream_scratch(cudaStream_t st, size_t bytes, uint8_t** out, const char* wha
 // time building them (long K, few rows per CTA: long-K projections, row shards on
 // many GPUs); the row kernel then copies the records and waits for the prep kernel
 // through programmatic dependent launch (its weight copies start meanwhile).
-constexpr uint32_t kPrepMinBlocks = 256;   // K >= 8192
+// Measured on B200 with the early-stage rule (pipelined launches, prep / no prep):
+// Q4 2048 x 28672 18.7 / 21.3 us, Q4 8192 x 28672 53.8 / 56.5, Q8 2048 x 11008
+// 9.60 / 9.57 alone but 1.80 / 1.87 ms per decode step (its down projection, where
+// the dependency wait is long), Q4 8192 x 8192 13.46 / 12.78.
+constexpr uint32_t kPrepMinBlocks = 320;   // K >= 10240
 constexpr uint32_t kPrepMaxRows = 96;      // rows per CTA
 
 int launch_rows_fast(uint32_t dtype, RowPlan& pl, int MT, bool overlap, cudaStream_t st) {
     if (pl.p.nblk >= kPrepMinBlocks && pl.p.rows_base + (pl.p.rows_extra ? 1u : 0u) <= kPrepMaxRows) {
         const size_t bytes = static_cast<size_t>(pl.p.M) * pl.p.nblk * kLimbRec;
         uint8_t* recs = nullptr;
-        const int rc = stream_scratch(st, bytes, &recs, "the FAST path's activation-limb prep (K >= 8192 with few rows per CTA)");
+        const int rc = stream_scratch(st, bytes, &recs, "the FAST path's activation-limb prep (K >= 10240 with few rows per CTA)");
         if (rc) return rc;
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];

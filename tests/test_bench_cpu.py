@@ -39,11 +39,12 @@ def test_algorithmic_bytes_match_the_measurement_plan():
 
 
 def test_launch_count_rule():
-    """The limb-prep kernel runs for rows of >= 256 blocks when a CTA gets <= 96 rows."""
+    """The limb-prep kernel runs for rows of >= 320 blocks when a CTA gets <= 96 rows."""
     assert bench.launches_per_call(4096, 4096, 148) == 1        # 128 blocks per row
-    assert bench.launches_per_call(10240, 8192, 148) == 2       # 70 rows per CTA
-    assert bench.launches_per_call(14336, 8192, 148) == 1       # 97 rows per CTA
-    assert bench.launches_per_call(8192, 28672, 148) == 2
+    assert bench.launches_per_call(10240, 8192, 148) == 1       # 256 blocks per row
+    assert bench.launches_per_call(2048, 11008, 148) == 2       # 344 blocks per row
+    assert bench.launches_per_call(8192, 28672, 148) == 2       # 896 blocks, 56 rows per CTA
+    assert bench.launches_per_call(28672, 28672, 148) == 1      # 194 rows per CTA
 
 
 def test_reference_arm_prints_the_contract_line():
@@ -120,6 +121,6 @@ def test_sharded_call_kernel_count():
     assert bench.shard_call_kernels("tc", 14336, 8192, 70, 148) == ("qmm_tc_kernel", 4)
     assert bench.shard_call_kernels("auto", 14336, 8192, 2, 148) == ("qmv_rows_kernel", 1)   # 97 rows per CTA
     assert bench.shard_call_kernels("fast", 14336, 8192, 5, 148) == ("qmv_rows_kernel", 3)
-    assert bench.shard_call_kernels("fast", 7168, 8192, 5, 148) == ("qmv_rows_kernel", 6)    # 49 rows: limb prep
+    assert bench.shard_call_kernels("fast", 7168, 28672, 5, 148) == ("qmv_rows_kernel", 6)   # 49 rows: limb prep
     assert bench.shard_call_kernels("fast", 3584, 28672, 1, 148) == ("qmv_rows_kernel", 2)
     assert bench.shard_call_kernels("exact", 14336, 8192, 4, 148) == ("qmv_rows_kernel", 1)
