@@ -241,7 +241,10 @@ bool plan_rows(const qraf_weight_t& w, const float* x, float* y, uint32_t mcount
     // fit ~18 KB (more rows share each staged activation block).  Whole rows.
     while (G < kRowGMax && (2 * G) * rb <= 18432 && 5 * ((max_rows + 2 * G - 1) / (2 * G)) >= 4 * kRowWarps) G *= 2;
     if (!exact && mcount == 2) G = 2;
-    if (pairs) G = 2;
+    // SwiGLU pairs: two pairs per stage where four rows fit the stage (one vector), so
+    // that each staged activation record serves four rows; a row's sum does not
+    // depend on the rows beside it
+    if (pairs) G = (mcount == 1 && 4 * rb <= 18432 && max_rows >= 8) ? 4u : 2u;
     const bool long_rows = 2 * rb > 18432;   // not even 2 whole rows per stage
     if (!exact && long_rows) {
         // FAST, long rows: stages of 4 rows (2 for two vectors) x one piece of K, so

@@ -799,7 +799,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) qmv_rows_kernel(const RowParam
                         if (p.npieces > 1)
                             part[(static_cast<size_t>(v) * p.part_rows + (row0 - r0 + g)) * p.npieces + pc] = tsum[g][v];
                         else if (p.swiglu)
-                            { if (GT == 2 && g == 1) store_swiglu(p, v, row0 >> 1, tsum[0][v], tsum[GT - 1][v]); }
+                            { if (g & 1) store_swiglu(p, v, (row0 + g) >> 1, tsum[g > 0 ? g - 1 : 0][v], tsum[g][v]); }
                         else
                             store_out(p, call, v, row0 + g, tsum[g][v]);
                     }
